@@ -1,0 +1,616 @@
+// index.cu -- device-side flat index behind the extern "C" layer
+// (mflat_cuda.h).  The host engine (FlatIndex.cpp) owns argument checking,
+// k clamping and logging; this file owns device memory, streams, kernel
+// orchestration and the device error word.
+//
+// Replaces the device half of the reference's FlatIndex::Impl
+// (src/FlatIndex.mm:137-189 buffers, :160-178 ensureBuffer, :294-421 search
+// tile loop) with a device-authoritative layout: rows are appended on the
+// device (no host copy, no whole-database re-upload per add) and norms are
+// computed on the device with the reference's double accumulation
+// (src/Distance.h:40-60).
+#include <cudaTypedefs.h>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "index_impl.cuh"
+#include "kernels.cuh"
+#include "mflat_cuda.h"
+#include "ptx.cuh"
+
+namespace mflat_cu {
+
+namespace {
+thread_local std::string g_last_error;
+}
+
+int fail(int status, const char* what, cudaError_t e) {
+    char buf[512];
+    if (e != cudaSuccess)
+        std::snprintf(buf, sizeof buf, "%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
+    else
+        std::snprintf(buf, sizeof buf, "%s", what);
+    g_last_error = buf;
+    return status;
+}
+
+const char* last_error_message() { return g_last_error.c_str(); }
+
+cudaError_t DevBuf::ensure(size_t need) {
+    if (need <= bytes) return cudaSuccess;
+    if (p) cudaFree(p);
+    p = nullptr;
+    bytes = 0;
+    const size_t want = need + need / 4;
+    cudaError_t e = cudaMalloc(&p, want);
+    if (e != cudaSuccess) { p = nullptr; return e; }
+    bytes = want;
+    return cudaSuccess;
+}
+
+void DevBuf::release() {
+    if (p) cudaFree(p);
+    p = nullptr;
+    bytes = 0;
+}
+
+DeviceGuard::DeviceGuard(int dev) {
+    cudaGetDevice(&prev);
+    if (prev != dev) cudaSetDevice(dev);
+}
+
+DeviceGuard::~DeviceGuard() {
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+}
+
+namespace {
+
+const float kInf = INFINITY;
+
+// ------------------------------------------------------------- TMA encode
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+
+bool get_encoder() {
+    std::call_once(g_encode_once, [] {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    });
+    return g_encode != nullptr;
+}
+
+// Row-major fp32 matrix [rows][inner] -> 2-D tensor map with a
+// [box_rows][32 floats] box and 128-byte swizzle (the UMMA K-major SW128
+// layout).  Rows past `rows` read as zero.
+bool make_map_f32(CUtensorMap* map, const float* base, uint64_t inner, uint64_t rows,
+                  uint32_t box_rows) {
+    if (!get_encoder()) return false;
+    cuuint64_t dims[2] = {inner, rows};
+    cuuint64_t strides[1] = {inner * sizeof(float)};
+    cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims,
+                          strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+// ------------------------------------------------------------- kernels
+__device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
+    hi = __uint_as_float(f32_to_tf32_rna(x));
+    lo = x - hi;   // exact: lo = x - tf32(x) has at most 13 significant bits
+}
+
+// One thread per row: optional Cosine normalisation (src/Distance.h:50-60),
+// squared norm with double accumulation (Distance.h:40-47), tf32 split,
+// zero padding to d_pad, score bias and running max row norm.
+__global__ void ingest_rows_kernel(const float* __restrict__ src, int64_t n, int dim, int d_pad,
+                                   int metric, int64_t row0, float* __restrict__ db_hi,
+                                   float* __restrict__ db_lo, float* __restrict__ colbias,
+                                   float* __restrict__ dnorm, unsigned* xmax_bits) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const float* row = src + i * dim;
+    float* oh = db_hi + (row0 + i) * d_pad;
+    float* ol = db_lo + (row0 + i) * d_pad;
+    float inv = 1.0f;
+    bool scale = false;
+    if (metric == kCosine) {
+        double s = 0.0;
+        for (int c = 0; c < dim; ++c) s += static_cast<double>(row[c]) * row[c];
+        if (s > 0.0) { inv = static_cast<float>(1.0 / sqrt(s)); scale = true; }
+    }
+    double s2 = 0.0;
+    for (int c = 0; c < dim; ++c) {
+        const float x = scale ? row[c] * inv : row[c];
+        s2 += static_cast<double>(x) * x;
+        float h, l;
+        split_tf32(x, h, l);
+        oh[c] = h;
+        ol[c] = l;
+    }
+    for (int c = dim; c < d_pad; ++c) { oh[c] = 0.0f; ol[c] = 0.0f; }
+    const float dn = static_cast<float>(s2);
+    dnorm[row0 + i] = dn;
+    colbias[row0 + i] = metric == kL2 ? -dn : 0.0f;
+    const float nrm = static_cast<float>(sqrt(s2) * (1.0 + 1e-7));   // rounded up
+    atomicMax(xmax_bits, __float_as_uint(nrm));
+}
+
+// One thread per padded query row: Cosine normalisation, tf32 split, ||q||
+// (rounded up) for the error bound.  Rows >= m are zero.
+__global__ void prep_queries_kernel(const float* __restrict__ src, int m, int m_pad, int dim,
+                                    int d_pad, int metric, float* __restrict__ q_hi,
+                                    float* __restrict__ q_lo, float* __restrict__ qnorm) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= m_pad) return;
+    float* oh = q_hi + static_cast<int64_t>(i) * d_pad;
+    float* ol = q_lo + static_cast<int64_t>(i) * d_pad;
+    if (i >= m) {
+        for (int c = 0; c < d_pad; ++c) { oh[c] = 0.0f; ol[c] = 0.0f; }
+        qnorm[i] = 0.0f;
+        return;
+    }
+    const float* row = src + static_cast<int64_t>(i) * dim;
+    float inv = 1.0f;
+    bool scale = false;
+    if (metric == kCosine) {
+        double s = 0.0;
+        for (int c = 0; c < dim; ++c) s += static_cast<double>(row[c]) * row[c];
+        if (s > 0.0) { inv = static_cast<float>(1.0 / sqrt(s)); scale = true; }
+    }
+    double s2 = 0.0;
+    for (int c = 0; c < dim; ++c) {
+        const float x = scale ? row[c] * inv : row[c];
+        s2 += static_cast<double>(x) * x;
+        float h, l;
+        split_tf32(x, h, l);
+        oh[c] = h;
+        ol[c] = l;
+    }
+    for (int c = dim; c < d_pad; ++c) { oh[c] = 0.0f; ol[c] = 0.0f; }
+    qnorm[i] = static_cast<float>(sqrt(s2) * (1.0 + 1e-7));
+}
+
+__global__ void fill_f32_kernel(float* p, int64_t n, float v) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i < n) p[i] = v;
+}
+
+__global__ void fill_empty_kernel(int32_t* ids, float* dist, int64_t n, float v) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i < n) { ids[i] = -1; dist[i] = v; }
+}
+
+cudaError_t grow(mflat_cu_index* ix, int64_t need) {
+    if (need <= ix->cap) return cudaSuccess;
+    cudaStream_t st = ix->stream;
+    int64_t cap = std::max<int64_t>(need, ix->cap + ix->cap / 2);
+    cap = (cap + kBN - 1) / kBN * kBN;
+    float *h = nullptr, *l = nullptr, *cb = nullptr, *dn = nullptr;
+    const size_t rowb = static_cast<size_t>(ix->d_pad) * sizeof(float);
+    cudaError_t e;
+    if ((e = cudaMalloc(&h, cap * rowb)) != cudaSuccess) goto bad;
+    if ((e = cudaMalloc(&l, cap * rowb)) != cudaSuccess) goto bad;
+    if ((e = cudaMalloc(&cb, cap * sizeof(float))) != cudaSuccess) goto bad;
+    if ((e = cudaMalloc(&dn, cap * sizeof(float))) != cudaSuccess) goto bad;
+    if (ix->n > 0) {
+        cudaMemcpyAsync(h, ix->db_hi, ix->n * rowb, cudaMemcpyDeviceToDevice, st);
+        cudaMemcpyAsync(l, ix->db_lo, ix->n * rowb, cudaMemcpyDeviceToDevice, st);
+        cudaMemcpyAsync(cb, ix->colbias, ix->n * sizeof(float), cudaMemcpyDeviceToDevice, st);
+        cudaMemcpyAsync(dn, ix->dnorm, ix->n * sizeof(float), cudaMemcpyDeviceToDevice, st);
+    }
+    fill_f32_kernel<<<blocks_for(cap - ix->n, 256), 256, 0, st>>>(cb + ix->n, cap - ix->n, -kInf);
+    if ((e = cudaStreamSynchronize(st)) != cudaSuccess) goto bad;
+    cudaFree(ix->db_hi);
+    cudaFree(ix->db_lo);
+    cudaFree(ix->colbias);
+    cudaFree(ix->dnorm);
+    ix->db_hi = h;
+    ix->db_lo = l;
+    ix->colbias = cb;
+    ix->dnorm = dn;
+    ix->cap = cap;
+    return cudaSuccess;
+bad:
+    cudaFree(h);
+    cudaFree(l);
+    cudaFree(cb);
+    cudaFree(dn);
+    return e;
+}
+
+// Make `waiter` wait for everything enqueued so far on `producer`.
+void order_after(cudaStream_t waiter, cudaStream_t producer) {
+    if (waiter == producer) return;
+    cudaEvent_t e;
+    cudaEventCreateWithFlags(&e, cudaEventDisableTiming);
+    cudaEventRecord(e, producer);
+    cudaStreamWaitEvent(waiter, e, 0);
+    cudaEventDestroy(e);
+}
+
+// Candidate-list length for the exact path: k plus a margin that absorbs the
+// rows whose screen scores fall inside the proven error band.
+int kp_for(int k) {
+    const int need = k + std::max(3, k / 2);
+    for (int kp : {4, 8, 16, 32})
+        if (kp >= need) return kp;
+    return 0;
+}
+
+// Database chunks per query tile: whole work units on every SM.
+void plan_chunks(int n_qtiles, int n_tiles, int num_sms, int max_chunks, int& n_chunks,
+                 int& tiles_per_chunk) {
+    int best_s = 1;
+    double best_eff = -1.0;
+    const int smax = std::min(max_chunks, n_tiles);
+    for (int s = 1; s <= smax; ++s) {
+        const int tpc = (n_tiles + s - 1) / s;
+        const int sc = (n_tiles + tpc - 1) / tpc;
+        const int64_t units = static_cast<int64_t>(n_qtiles) * sc;
+        const int64_t waves = (units + num_sms - 1) / num_sms;
+        const double eff = static_cast<double>(units) / static_cast<double>(waves * num_sms);
+        if (eff > best_eff + 0.02) { best_eff = eff; best_s = s; }
+        if (best_eff > 0.97 && units >= num_sms) break;
+    }
+    tiles_per_chunk = (n_tiles + best_s - 1) / best_s;
+    n_chunks = (n_tiles + tiles_per_chunk - 1) / tiles_per_chunk;
+}
+
+}  // namespace
+
+int check_device_error(mflat_cu_index* ix) {
+    if (ix->host_words[0] != 0) {
+        const int code = ix->host_words[0];
+        ix->host_words[0] = 0;
+        cudaMemsetAsync(ix->err, 0, sizeof(int), ix->stream);
+        char buf[128];
+        std::snprintf(buf, sizeof buf, "device kernel reported error code %d (%s)", code,
+                      code == kErrTimeout ? "bounded wait timed out" : "bad launch configuration");
+        return fail(ST_DEVICE, buf);
+    }
+    return ST_OK;
+}
+
+int run_screen(mflat_cu_index* ix, const float* queries, int m, int kp, int on_device,
+               cudaStream_t st, ScreenRun& out, int max_chunks) {
+    const int m_pad = (m + kBM - 1) / kBM * kBM;
+    const int d_pad = ix->d_pad;
+    const int n_tiles = static_cast<int>((ix->n + kBN - 1) / kBN);
+    const int n_qtiles = m_pad / kBM;
+    int n_chunks = 1, tpc = n_tiles;
+    plan_chunks(n_qtiles, n_tiles, ix->num_sms, max_chunks, n_chunks, tpc);
+
+    const float* qsrc = queries;
+    if (!on_device) {
+        CU_TRY(ix->q_in.ensure(static_cast<size_t>(m) * ix->dim * sizeof(float)), "query buffer");
+        CU_TRY(cudaMemcpyAsync(ix->q_in.p, queries, static_cast<size_t>(m) * ix->dim * sizeof(float),
+                               cudaMemcpyHostToDevice, st),
+               "query upload");
+        qsrc = ix->q_in.as<float>();
+    }
+    CU_TRY(ix->q_hi.ensure(static_cast<size_t>(m_pad) * d_pad * sizeof(float)), "query split");
+    CU_TRY(ix->q_lo.ensure(static_cast<size_t>(m_pad) * d_pad * sizeof(float)), "query split");
+    CU_TRY(ix->qnorm.ensure(static_cast<size_t>(m_pad) * sizeof(float)), "query norms");
+    const size_t parts = static_cast<size_t>(n_chunks) * m_pad * kp;
+    CU_TRY(ix->part_s.ensure(parts * sizeof(float)), "candidate lists");
+    CU_TRY(ix->part_i.ensure(parts * sizeof(int32_t)), "candidate lists");
+
+    if (ix->timing) cudaEventRecord(ix->ev[0], st);
+    prep_queries_kernel<<<blocks_for(m_pad, 128), 128, 0, st>>>(
+        qsrc, m, m_pad, ix->dim, d_pad, ix->metric, ix->q_hi.as<float>(), ix->q_lo.as<float>(),
+        ix->qnorm.as<float>());
+    CU_TRY(cudaGetLastError(), "query prep launch");
+
+    ScreenParams sp{};
+    sp.m = m;
+    sp.m_pad = m_pad;
+    sp.d_pad = d_pad;
+    sp.n = ix->n;
+    sp.n_tiles = n_tiles;
+    sp.n_qtiles = n_qtiles;
+    sp.n_chunks = n_chunks;
+    sp.tiles_per_chunk = tpc;
+    sp.alpha = ix->metric == kL2 ? 2.0f : 1.0f;
+    sp.colbias = ix->colbias;
+    sp.part_score = ix->part_s.as<float>();
+    sp.part_id = ix->part_i.as<int32_t>();
+    sp.err = ix->err;
+    sp.q_hi = ix->q_hi.as<float>();
+    sp.q_lo = ix->q_lo.as<float>();
+    sp.db_hi = ix->db_hi;
+    sp.db_lo = ix->db_lo;
+
+    if (ix->timing) cudaEventRecord(ix->ev[1], st);
+    cudaError_t le;
+    if (ix->force_simt || d_pad > kMaxDPadResident) {
+        le = launch_screen_simt(kp, sp, st);
+    } else {
+        CUtensorMap ta_hi, ta_lo, tb_hi, tb_lo;
+        if (!make_map_f32(&ta_hi, sp.q_hi, d_pad, m_pad, kBM) ||
+            !make_map_f32(&ta_lo, sp.q_lo, d_pad, m_pad, kBM) ||
+            !make_map_f32(&tb_hi, ix->db_hi, d_pad, ix->n, kBN) ||
+            !make_map_f32(&tb_lo, ix->db_lo, d_pad, ix->n, kBN))
+            return fail(ST_DEVICE, "tensor map encoding failed");
+        const int64_t units = static_cast<int64_t>(n_qtiles) * n_chunks;
+        const int grid = static_cast<int>(std::min<int64_t>(units, ix->num_sms));
+        le = launch_screen_tf32x3(kp, ta_hi, ta_lo, tb_hi, tb_lo, sp, grid, st);
+    }
+    CU_TRY(le, "screen launch");
+    if (ix->timing) cudaEventRecord(ix->ev[2], st);
+
+    out.kp = kp;
+    out.m = m;
+    out.m_pad = m_pad;
+    out.n_chunks = n_chunks;
+    out.q_hi = sp.q_hi;
+    out.q_lo = sp.q_lo;
+    out.qnorm = ix->qnorm.as<float>();
+    out.part_s = sp.part_score;
+    out.part_i = sp.part_id;
+    out.launches = 2;
+    return ST_OK;
+}
+
+}  // namespace mflat_cu
+
+using namespace mflat_cu;
+
+// =====================================================================
+extern "C" {
+
+const char* mflat_cu_last_error(void) { return last_error_message(); }
+
+int mflat_cu_device_count(void) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess) return 0;
+    return n;
+}
+
+int mflat_cu_default_device(int device) {
+    if (device >= 0) return device;
+    const char* env = std::getenv("MFLAT_DEVICE");
+    if (env && *env) return std::atoi(env);
+    return 0;
+}
+
+int mflat_cu_index_create(int device, int dim, int metric, int storage, mflat_cu_index_t** out) {
+    if (!out || dim <= 0) return fail(ST_BAD_ARG, "bad argument");
+    *out = nullptr;
+    device = mflat_cu_default_device(device);
+    const int ndev = mflat_cu_device_count();
+    if (ndev <= 0) return fail(ST_DEVICE, "no CUDA device");
+    if (device >= ndev) return fail(ST_BAD_ARG, "device index out of range");
+    if (storage != 0) return fail(ST_BAD_ARG, "storage precision not supported by this build");
+    DeviceGuard g(device);
+    int major = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device);
+    if (major != 10) return fail(ST_DEVICE, "device is not sm_100 (B200)");
+    auto* ix = new (std::nothrow) mflat_cu_index();
+    if (!ix) return fail(ST_ALLOC, "host allocation failed");
+    ix->device = device;
+    ix->dim = dim;
+    ix->d_pad = (dim + kBK - 1) / kBK * kBK;
+    ix->metric = (metric == kIP || metric == kCosine) ? metric : kL2;
+    ix->storage = storage;
+    cudaDeviceGetAttribute(&ix->num_sms, cudaDevAttrMultiProcessorCount, device);
+    const char* fs = std::getenv("MFLAT_SCREEN");
+    ix->force_simt = fs && std::strcmp(fs, "simt") == 0;
+    cudaError_t e;
+    if ((e = cudaStreamCreateWithFlags(&ix->stream, cudaStreamNonBlocking)) != cudaSuccess ||
+        (e = cudaMalloc(&ix->xmax_bits, sizeof(unsigned))) != cudaSuccess ||
+        (e = cudaMalloc(&ix->err, sizeof(int))) != cudaSuccess ||
+        (e = cudaMalloc(&ix->flag_count, sizeof(int))) != cudaSuccess ||
+        (e = cudaHostAlloc(&ix->host_words, 4 * sizeof(int), cudaHostAllocDefault)) != cudaSuccess) {
+        mflat_cu_index_destroy(ix);
+        return fail(e == cudaErrorMemoryAllocation ? ST_ALLOC : ST_DEVICE, "index setup", e);
+    }
+    for (auto& ev : ix->ev) cudaEventCreate(&ev);
+    cudaMemsetAsync(ix->xmax_bits, 0, sizeof(unsigned), ix->stream);
+    cudaMemsetAsync(ix->err, 0, sizeof(int), ix->stream);
+    std::memset(ix->host_words, 0, 4 * sizeof(int));
+    if ((e = cudaStreamSynchronize(ix->stream)) != cudaSuccess) {
+        mflat_cu_index_destroy(ix);
+        return fail(ST_DEVICE, "index setup", e);
+    }
+    *out = ix;
+    return ST_OK;
+}
+
+void mflat_cu_index_destroy(mflat_cu_index_t* ix) {
+    if (!ix) return;
+    DeviceGuard g(ix->device);
+    if (ix->stream) cudaStreamSynchronize(ix->stream);
+    comm_release(ix);
+    cudaFree(ix->db_hi);
+    cudaFree(ix->db_lo);
+    cudaFree(ix->colbias);
+    cudaFree(ix->dnorm);
+    cudaFree(ix->xmax_bits);
+    cudaFree(ix->err);
+    cudaFree(ix->flag_count);
+    if (ix->host_words) cudaFreeHost(ix->host_words);
+    for (DevBuf* b : {&ix->stage_in, &ix->q_in, &ix->q_hi, &ix->q_lo, &ix->qnorm, &ix->part_s,
+                      &ix->part_i, &ix->flag_list, &ix->out_ids, &ix->out_dist, &ix->gather_ids,
+                      &ix->gather_dist, &ix->merge_tmp_ids, &ix->merge_tmp_dist})
+        b->release();
+    for (auto& ev : ix->ev)
+        if (ev) cudaEventDestroy(ev);
+    if (ix->stream) cudaStreamDestroy(ix->stream);
+    delete ix;
+}
+
+int64_t mflat_cu_index_size(const mflat_cu_index_t* ix) { return ix ? ix->n : 0; }
+int mflat_cu_index_device(const mflat_cu_index_t* ix) { return ix ? ix->device : -1; }
+
+int mflat_cu_index_add(mflat_cu_index_t* ix, const float* vectors, int64_t n, int on_device,
+                       void* stream) {
+    if (!ix || (!vectors && n > 0) || n < 0) return fail(ST_BAD_ARG, "bad argument");
+    if (n == 0) return ST_OK;
+    if (ix->n + n > static_cast<int64_t>(INT32_MAX) - kBN)
+        return fail(ST_BAD_ARG, "database would exceed 2^31 rows");
+    DeviceGuard g(ix->device);
+    cudaStream_t caller = static_cast<cudaStream_t>(stream);
+    if (on_device) order_after(ix->stream, caller);
+    CU_TRY(grow(ix, ix->n + n), "database allocation");
+    const int64_t chunk =
+        on_device ? n : std::max<int64_t>(1, (int64_t(64) << 20) / (int64_t(ix->dim) * 4));
+    for (int64_t off = 0; off < n; off += chunk) {
+        const int64_t cnt = std::min(chunk, n - off);
+        const float* src = vectors + off * ix->dim;
+        if (!on_device) {
+            const size_t bytes = static_cast<size_t>(cnt) * ix->dim * sizeof(float);
+            CU_TRY(ix->stage_in.ensure(bytes), "staging");
+            CU_TRY(cudaMemcpyAsync(ix->stage_in.p, src, bytes, cudaMemcpyHostToDevice, ix->stream), "upload");
+            src = ix->stage_in.as<float>();
+        }
+        ingest_rows_kernel<<<blocks_for(cnt, 128), 128, 0, ix->stream>>>(
+            src, cnt, ix->dim, ix->d_pad, ix->metric, ix->n + off, ix->db_hi, ix->db_lo,
+            ix->colbias, ix->dnorm, ix->xmax_bits);
+        CU_TRY(cudaGetLastError(), "ingest launch");
+        if (!on_device) CU_TRY(cudaStreamSynchronize(ix->stream), "ingest");
+    }
+    ix->n += n;
+    if (on_device) order_after(caller, ix->stream);
+    return ST_OK;
+}
+
+int mflat_cu_index_reset(mflat_cu_index_t* ix) {
+    if (!ix) return fail(ST_BAD_ARG, "bad argument");
+    DeviceGuard g(ix->device);
+    CU_TRY(cudaStreamSynchronize(ix->stream), "reset");
+    if (ix->cap > 0) {
+        fill_f32_kernel<<<blocks_for(ix->cap, 256), 256, 0, ix->stream>>>(ix->colbias, ix->cap, -kInf);
+        CU_TRY(cudaGetLastError(), "reset");
+    }
+    cudaMemsetAsync(ix->xmax_bits, 0, sizeof(unsigned), ix->stream);
+    CU_TRY(cudaStreamSynchronize(ix->stream), "reset");
+    ix->n = 0;
+    return ST_OK;
+}
+
+int mflat_cu_index_set_timing(mflat_cu_index_t* ix, int enable) {
+    if (!ix) return fail(ST_BAD_ARG, "bad argument");
+    ix->timing = enable != 0;
+    return ST_OK;
+}
+
+int mflat_cu_index_last_timing(const mflat_cu_index_t* ix, mflat_cu_timing_t* out) {
+    if (!ix || !out) return fail(ST_BAD_ARG, "bad argument");
+    *out = ix->last;
+    return ST_OK;
+}
+
+int mflat_cu_index_search(mflat_cu_index_t* ix, const float* queries, int m, int k_out,
+                          int32_t* out_ids, float* out_dist, int on_device, void* stream) {
+    if (!ix || (!queries && m > 0) || m < 0 || k_out < 1) return fail(ST_BAD_ARG, "bad argument");
+    if (m == 0) return ST_OK;
+    DeviceGuard g(ix->device);
+    cudaStream_t st = on_device ? static_cast<cudaStream_t>(stream) : ix->stream;
+    if (on_device) {
+        const int rc = check_device_error(ix);   // the previous asynchronous call
+        if (rc != ST_OK) return rc;
+    }
+    const int64_t mk = static_cast<int64_t>(m) * k_out;
+    int32_t* d_ids = out_ids;
+    float* d_dist = out_dist;
+    if (!on_device) {
+        CU_TRY(ix->out_ids.ensure(mk * sizeof(int32_t)), "result buffer");
+        CU_TRY(ix->out_dist.ensure(mk * sizeof(float)), "result buffer");
+        d_ids = ix->out_ids.as<int32_t>();
+        d_dist = ix->out_dist.as<float>();
+    }
+    const float empty = ix->metric == kL2 ? kInf : -kInf;
+    ix->last = mflat_cu_timing_t{};
+    int launches = 0;
+
+    if (ix->n == 0) {
+        fill_empty_kernel<<<blocks_for(mk, 256), 256, 0, st>>>(d_ids, d_dist, mk, empty);
+        ++launches;
+        CU_TRY(cudaGetLastError(), "fill");
+    } else {
+        const int kp = kp_for(k_out);
+        if (kp == 0) return fail(ST_BAD_ARG, "k above the exact-path limit of this build");
+        ScreenRun run;
+        int rc = run_screen(ix, queries, m, kp, on_device, st, run);
+        if (rc != ST_OK) return rc;
+        launches += run.launches;
+        ix->last.screen_launches = 1;
+        CU_TRY(ix->flag_list.ensure(static_cast<size_t>(m) * sizeof(int)), "fallback list");
+        cudaMemsetAsync(ix->flag_count, 0, sizeof(int), st);
+
+        SelectParams sel{};
+        sel.m = m;
+        sel.m_pad = run.m_pad;
+        sel.dim = ix->dim;
+        sel.d_pad = ix->d_pad;
+        sel.k_out = k_out;
+        sel.n_chunks = run.n_chunks;
+        sel.metric = ix->metric == kL2 ? kL2 : kIP;
+        sel.n = ix->n;
+        sel.part_score = run.part_s;
+        sel.part_id = run.part_i;
+        sel.q_hi = run.q_hi;
+        sel.q_lo = run.q_lo;
+        sel.qnorm = run.qnorm;
+        sel.db_hi = ix->db_hi;
+        sel.db_lo = ix->db_lo;
+        sel.xmax_bits = ix->xmax_bits;
+        // tf32 split error (2.5 * 2^-21 per product) plus fp32 accumulation of
+        // 3 * d_pad products, with an 8x safety factor on the latter.
+        sel.gamma = static_cast<float>((3.0 * ix->d_pad + 16.0) * std::ldexp(1.0, -21));
+        sel.id_base = ix->world > 1 ? ix->id_base : 0;
+        sel.out_ids = d_ids;
+        sel.out_dist = d_dist;
+        sel.flag_count = ix->flag_count;
+        sel.flag_list = ix->flag_list.as<int>();
+        sel.err = ix->err;
+        CU_TRY(launch_select_exact(kp, sel, st), "select launch");
+        ++launches;
+        CU_TRY(launch_fallback_exact(sel, ix->num_sms, st), "fallback launch");
+        ++launches;
+        cudaMemcpyAsync(&ix->host_words[1], ix->flag_count, sizeof(int), cudaMemcpyDeviceToHost, st);
+        if (ix->timing) cudaEventRecord(ix->ev[3], st);
+    }
+    if (ix->world > 1) {
+        const int rc = shard_merge(ix, m, k_out, d_ids, d_dist, st);
+        if (rc != ST_OK) return rc;
+        launches += 1;
+    }
+    cudaMemcpyAsync(&ix->host_words[0], ix->err, sizeof(int), cudaMemcpyDeviceToHost, st);
+    ix->last.launches = launches;
+    if (!on_device) {
+        CU_TRY(cudaMemcpyAsync(out_ids, d_ids, mk * sizeof(int32_t), cudaMemcpyDeviceToHost, st), "download");
+        CU_TRY(cudaMemcpyAsync(out_dist, d_dist, mk * sizeof(float), cudaMemcpyDeviceToHost, st), "download");
+        int rc = wait_stream_checked(ix, st);
+        if (rc != ST_OK) return rc;
+        rc = check_device_error(ix);
+        if (rc != ST_OK) return rc;
+    }
+    if (ix->timing && ix->n > 0) {
+        CU_TRY(cudaEventSynchronize(ix->ev[3]), "timing");
+        cudaEventElapsedTime(&ix->last.total_ms, ix->ev[0], ix->ev[3]);
+        cudaEventElapsedTime(&ix->last.screen_ms, ix->ev[1], ix->ev[2]);
+        cudaEventElapsedTime(&ix->last.select_ms, ix->ev[2], ix->ev[3]);
+        ix->last.fallback_queries = ix->host_words[1];
+    }
+    return ST_OK;
+}
+
+}  // extern "C"

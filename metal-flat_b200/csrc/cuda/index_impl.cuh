@@ -1,0 +1,98 @@
+// index_impl.cuh -- internal state of a device index, shared by index.cu
+// (create / add / search), kmeans.cu and comm.cu.  Not installed.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <string>
+
+#include "kernels.cuh"
+#include "mflat_cuda.h"
+
+namespace mflat_cu {
+
+enum : int { ST_OK = 0, ST_BAD_ARG = 2, ST_ALLOC = 3, ST_INTERNAL = 5, ST_DEVICE = 6 };
+
+int fail(int status, const char* what, cudaError_t e = cudaSuccess);
+
+#define CU_TRY(expr, what)                                                                   \
+    do {                                                                                     \
+        cudaError_t e_ = (expr);                                                             \
+        if (e_ != cudaSuccess)                                                               \
+            return ::mflat_cu::fail(e_ == cudaErrorMemoryAllocation ? ::mflat_cu::ST_ALLOC    \
+                                                                    : ::mflat_cu::ST_DEVICE, \
+                                    what, e_);                                               \
+    } while (0)
+
+// Scratch buffer grown on demand and reused across calls.
+struct DevBuf {
+    void* p = nullptr;
+    size_t bytes = 0;
+    cudaError_t ensure(size_t need);
+    void release();
+    template <class T>
+    T* as() const { return static_cast<T*>(p); }
+};
+
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev);
+    ~DeviceGuard();
+};
+
+inline unsigned blocks_for(int64_t n, int t) { return static_cast<unsigned>((n + t - 1) / t); }
+
+// Result of the screen stage of one search (per (query, chunk) top-KP lists).
+struct ScreenRun {
+    int kp = 0, m = 0, m_pad = 0, n_chunks = 0;
+    const float* q_hi = nullptr;
+    const float* q_lo = nullptr;
+    const float* qnorm = nullptr;
+    const float* part_s = nullptr;
+    const int32_t* part_i = nullptr;
+    int launches = 0;
+};
+
+}  // namespace mflat_cu
+
+struct mflat_cu_index {
+    int device = 0;
+    int dim = 0, d_pad = 0, metric = 0, storage = 0;
+    int num_sms = 148;
+    cudaStream_t stream = nullptr;
+    int64_t n = 0, cap = 0;
+    float* db_hi = nullptr;       // [cap][d_pad]
+    float* db_lo = nullptr;
+    float* colbias = nullptr;     // [cap], -inf past n
+    float* dnorm = nullptr;       // [cap]
+    unsigned* xmax_bits = nullptr;
+    int* err = nullptr;           // device error word
+    int* flag_count = nullptr;    // queries routed to the exact full scan
+    int* host_words = nullptr;    // pinned: [0] err, [1] flag_count
+    mflat_cu::DevBuf stage_in, q_in, q_hi, q_lo, qnorm, part_s, part_i, flag_list, out_ids, out_dist;
+    bool timing = false;
+    cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
+    mflat_cu_timing_t last{};
+    bool force_simt = false;
+    // row sharding (comm.cu)
+    void* comm = nullptr;
+    int rank = 0, world = 1;
+    int64_t id_base = 0;
+    mflat_cu::DevBuf gather_ids, gather_dist, merge_tmp_ids, merge_tmp_dist;
+};
+
+namespace mflat_cu {
+
+// Upload (if needed), split the queries and run the tensor-core screen with
+// top-KP lists on stream `st`.  `queries` is device memory when on_device.
+int run_screen(mflat_cu_index* ix, const float* queries, int m, int kp, int on_device,
+               cudaStream_t st, ScreenRun& out, int max_chunks = kMaxChunks);
+int check_device_error(mflat_cu_index* ix);
+void comm_release(mflat_cu_index* ix);
+int shard_merge(mflat_cu_index* ix, int m, int k_out, int32_t* ids, float* dist, cudaStream_t st);
+// Synchronise `st`; with a communicator attached, watch it for peer failure.
+int wait_stream_checked(mflat_cu_index* ix, cudaStream_t st);
+const char* last_error_message();
+
+}  // namespace mflat_cu

@@ -1,0 +1,118 @@
+// kernels.cuh -- shared layouts, parameter blocks and device helpers of the
+// flat-search kernels.
+//
+// Data layout in HBM (one index on one device):
+//   db_hi, db_lo : float [cap][d_pad]  rows split as x = hi + lo exactly, with
+//                  hi = tf32(x) (round-to-nearest) and lo = x - hi; d_pad is
+//                  dim rounded up to 32 (one 128-byte TMA/UMMA k-block), the
+//                  padding is zero.  hi + lo reproduces the stored fp32 row
+//                  bit-for-bit for the exact fp64 re-rank.
+//   colbias      : float [cap]        per-row additive term of the screen
+//                  score: -||x||^2 (L2) or 0 (IP / Cosine); -inf past n, so a
+//                  ragged last tile can never enter a top-k list.
+//   xmax_bits    : uint  [1]          bits of max_i ||x_i|| (error bound).
+//   q_hi, q_lo   : float [m_pad][d_pad] split queries (same rule), zero rows
+//                  past m; qnorm: float [m] = ||q|| (for the error bound).
+//   part_score/part_id : [n_chunks][m_pad][KP] per (query, db chunk) top-KP
+//                  lists of the screen, sorted by (score desc, id asc).
+//
+// Screen score (larger = nearer, reference src/Distance.h:65-69):
+//   L2 : s = 2 q.x - ||x||^2      (= ||q||^2 - ||q - x||^2, ||q||^2 dropped)
+//   IP : s = q.x
+#pragma once
+
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+namespace mflat_cu {
+
+constexpr int kBM = 128;          // queries per tile (TMEM lanes)
+constexpr int kBN = 256;          // database rows per tile (UMMA N)
+constexpr int kBK = 32;           // fp32 elements per k-block (128 bytes)
+constexpr int kMaxDPadResident = 128;   // A (queries) kept resident in smem up to this
+constexpr int kMaxChunks = 128;   // db chunks per query (select kernel fan-in)
+
+enum Metric : int { kL2 = 0, kIP = 1, kCosine = 2 };
+
+struct ScreenParams {
+    int m;                 // queries
+    int m_pad;             // multiple of kBM
+    int d_pad;             // multiple of kBK
+    int64_t n;             // database rows
+    int n_tiles;           // ceil(n / kBN)
+    int n_qtiles;          // m_pad / kBM
+    int n_chunks;          // database chunks (units = n_qtiles * n_chunks)
+    int tiles_per_chunk;
+    float alpha;           // 2 (L2) or 1 (IP / Cosine)
+    const float* colbias;  // [>= n_tiles * kBN]
+    float* part_score;     // [n_chunks][m_pad][KP]
+    int32_t* part_id;
+    int* err;              // device error word (0 = ok)
+    // SIMT path only
+    const float* q_hi; const float* q_lo;
+    const float* db_hi; const float* db_lo;
+};
+
+struct SelectParams {
+    int m, m_pad, dim, d_pad, k_out, n_chunks, metric;
+    int64_t n;
+    const float* part_score; const int32_t* part_id;
+    const float* q_hi; const float* q_lo; const float* qnorm;
+    const float* db_hi; const float* db_lo;
+    const unsigned* xmax_bits;
+    float gamma;           // relative dot-product error bound of the screen
+    int64_t id_base;       // added to every returned id (row sharding)
+    int32_t* out_ids; float* out_dist;    // [m][k_out]
+    int* flag_count; int* flag_list;      // queries needing the exact full scan
+    int* err;
+};
+
+// ---------------------------------------------------------------------------
+// Per-thread top-KP list in registers, sorted by score descending.  insert()
+// is called only when v > s[KP-1]; strict '>' keeps an earlier (lower) id
+// ahead of a later equal score, matching the reference's cpuSearch scan
+// (src/FlatIndex.mm:272-281) when ids are visited in ascending order.
+template <int KP>
+struct TopList {
+    float s[KP];
+    int id[KP];
+    __device__ __forceinline__ void init() {
+#pragma unroll
+        for (int i = 0; i < KP; ++i) { s[i] = -__int_as_float(0x7f800000); id[i] = -1; }
+    }
+    __device__ __forceinline__ float worst() const { return s[KP - 1]; }
+    __device__ __forceinline__ void insert(float v, int vid) {
+#pragma unroll
+        for (int j = KP - 1; j >= 0; --j) {
+            const bool cj = v > s[j];
+            const bool cjm1 = (j > 0) ? (v > s[j > 0 ? j - 1 : 0]) : false;
+            const float ns = cj ? (cjm1 ? s[j > 0 ? j - 1 : 0] : v) : s[j];
+            const int nid = cj ? (cjm1 ? id[j > 0 ? j - 1 : 0] : vid) : id[j];
+            s[j] = ns;
+            id[j] = nid;
+        }
+    }
+};
+
+// (score desc, id asc) order with id < 0 ranked last.
+__device__ __forceinline__ bool cand_better(float sa, int ia, float sb, int ib) {
+    if (ia < 0) return false;
+    if (ib < 0) return true;
+    if (sa != sb) return sa > sb;
+    return ia < ib;
+}
+
+// ------------------------------------------------------------- launchers
+// All launchers enqueue on `stream` and return the launch status.
+cudaError_t launch_screen_tf32x3(int kp, const CUtensorMap& a_hi, const CUtensorMap& a_lo,
+                                 const CUtensorMap& b_hi, const CUtensorMap& b_lo,
+                                 const ScreenParams& p, int grid, cudaStream_t stream);
+cudaError_t launch_screen_simt(int kp, const ScreenParams& p, cudaStream_t stream);
+cudaError_t launch_select_exact(int kp, const SelectParams& p, cudaStream_t stream);
+cudaError_t launch_fallback_exact(const SelectParams& p, int grid, cudaStream_t stream);
+int screen_tf32x3_smem_bytes(int d_pad);
+cudaError_t launch_kmeans_select(const SelectParams& p, int32_t* out, int grid_fallback,
+                                 cudaStream_t stream);
+
+}  // namespace mflat_cu

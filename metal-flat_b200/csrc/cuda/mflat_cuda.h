@@ -1,0 +1,66 @@
+/* mflat_cuda.h -- the thin extern "C" layer between the C++ host engine
+ * (FlatIndex, CoarseQuantizer) and the CUDA kernels (libmflat_cuda.so).
+ *
+ * Plain C types only.  Status values are the mflat_status_t codes of
+ * include/mflat.h (0 ok, 2 bad argument, 3 allocation, 5 internal, 6 device).
+ * Pointers flagged `on_device` are device memory on the index's device and
+ * the call only enqueues on `stream`; otherwise they are host memory and the
+ * call returns after the results are in host memory.
+ */
+#ifndef MFLAT_CUDA_H
+#define MFLAT_CUDA_H
+
+#include <stdint.h>
+
+#if defined(_WIN32)
+#  define MFLAT_CU_API
+#else
+#  define MFLAT_CU_API __attribute__((visibility("default")))
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct mflat_cu_index mflat_cu_index_t;
+
+typedef struct {
+    float total_ms, screen_ms, select_ms;
+    int screen_launches, launches, fallback_queries;
+} mflat_cu_timing_t;
+
+/* Message of the last failure on the calling thread ("" if none). */
+MFLAT_CU_API const char* mflat_cu_last_error(void);
+MFLAT_CU_API int mflat_cu_device_count(void);
+/* Resolve the device for a request: device >= 0 as given, else $MFLAT_DEVICE, else 0. */
+MFLAT_CU_API int mflat_cu_default_device(int device);
+
+MFLAT_CU_API int mflat_cu_index_create(int device, int dim, int metric, int storage,
+                                       mflat_cu_index_t** out);
+MFLAT_CU_API void mflat_cu_index_destroy(mflat_cu_index_t* ix);
+MFLAT_CU_API int64_t mflat_cu_index_size(const mflat_cu_index_t* ix);
+MFLAT_CU_API int mflat_cu_index_device(const mflat_cu_index_t* ix);
+MFLAT_CU_API int mflat_cu_index_add(mflat_cu_index_t* ix, const float* vectors, int64_t n,
+                                    int on_device, void* stream);
+MFLAT_CU_API int mflat_cu_index_reset(mflat_cu_index_t* ix);
+/* Writes m rows of k_out (ids, distances), nearest-first, -1 / +-inf padded. */
+MFLAT_CU_API int mflat_cu_index_search(mflat_cu_index_t* ix, const float* queries, int m,
+                                       int k_out, int32_t* out_ids, float* out_dist,
+                                       int on_device, void* stream);
+MFLAT_CU_API int mflat_cu_index_set_timing(mflat_cu_index_t* ix, int enable);
+MFLAT_CU_API int mflat_cu_index_last_timing(const mflat_cu_index_t* ix, mflat_cu_timing_t* out);
+
+/* k-means assignment step: bit-exact argmin of the fp32 sequential sqL2. */
+MFLAT_CU_API int mflat_cu_kmeans_assign(const float* points, int64_t n, const float* centroids,
+                                        int ncentroids, int dim, int32_t* out_assign,
+                                        int device, int on_device, void* stream);
+
+/* Row sharding across ranks (NCCL). */
+MFLAT_CU_API int mflat_cu_comm_unique_id(uint8_t* out_id /* 128 bytes */);
+MFLAT_CU_API int mflat_cu_index_set_shard(mflat_cu_index_t* ix, int rank, int world,
+                                          const uint8_t* comm_id, int64_t id_base);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

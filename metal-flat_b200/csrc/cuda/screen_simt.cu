@@ -1,0 +1,58 @@
+// screen_simt.cu -- CUDA-core screen with exactly the inputs and outputs of
+// the tcgen05 kernel (per (query, chunk) top-KP lists).  It is the
+// independent GPU cross-check of screen_tc.cu, selected with
+// MFLAT_SCREEN=simt; the fp32 dot product here is computed directly from the
+// reconstructed rows (hi + lo), in index order.
+#include "kernels.cuh"
+
+namespace mflat_cu {
+namespace {
+
+template <int KP>
+__global__ void __launch_bounds__(128) screen_simt_kernel(const ScreenParams p) {
+    const int qt = blockIdx.x;
+    const int ch = blockIdx.y;
+    const int row = qt * kBM + threadIdx.x;
+    const int64_t r0 = static_cast<int64_t>(ch) * p.tiles_per_chunk * kBN;
+    const int64_t r1 = min(r0 + static_cast<int64_t>(p.tiles_per_chunk) * kBN, p.n);
+    TopList<KP> L;
+    L.init();
+    if (row < p.m) {
+        const float* qh = p.q_hi + static_cast<int64_t>(row) * p.d_pad;
+        const float* ql = p.q_lo + static_cast<int64_t>(row) * p.d_pad;
+        for (int64_t j = r0; j < r1; ++j) {
+            const float* xh = p.db_hi + j * p.d_pad;
+            const float* xl = p.db_lo + j * p.d_pad;
+            float acc = 0.0f;
+            for (int c = 0; c < p.d_pad; ++c) acc = fmaf(qh[c] + ql[c], xh[c] + xl[c], acc);
+            const float s = fmaf(p.alpha, acc, p.colbias[j]);
+            if (s > L.worst()) L.insert(s, static_cast<int>(j));
+        }
+        const int64_t o = (static_cast<int64_t>(ch) * p.m_pad + row) * KP;
+        for (int i = 0; i < KP; ++i) {
+            p.part_score[o + i] = L.s[i];
+            p.part_id[o + i] = L.id[i];
+        }
+    }
+}
+
+template <int KP>
+cudaError_t launch_kp(const ScreenParams& p, cudaStream_t stream) {
+    dim3 grid(p.n_qtiles, p.n_chunks);
+    screen_simt_kernel<KP><<<grid, kBM, 0, stream>>>(p);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_screen_simt(int kp, const ScreenParams& p, cudaStream_t stream) {
+    switch (kp) {
+        case 4: return launch_kp<4>(p, stream);
+        case 8: return launch_kp<8>(p, stream);
+        case 16: return launch_kp<16>(p, stream);
+        case 32: return launch_kp<32>(p, stream);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+}  // namespace mflat_cu

@@ -1,0 +1,342 @@
+// screen_tc.cu -- tcgen05 distance GEMM with the top-k selection fused into
+// its epilogue (the B200 replacement of the reference's per-tile pair
+// GemmDistance::encode + topk_merge, src/GemmDistance.mm:15-60 and
+// src/FlatIndex.mm:63-107, which round-tripped an m x tileW score matrix
+// through device memory; here no score matrix is ever written).
+//
+// fp32 exactness: each operand is split x = hi + lo with hi = tf32(x); the
+// kernel accumulates A_hi.B_hi + A_lo.B_hi + A_hi.B_lo (3xTF32) in a TMEM
+// fp32 accumulator.  The result is a *screen*: the top-KP candidates per
+// (query, database chunk) by screen score, KP > k, which the select kernel
+// re-ranks exactly in fp64 after proving (with an a-priori error bound) that
+// the true top-k is inside the candidate set.
+//
+// Work unit = (query tile of 128 rows, database chunk of whole 256-row tiles).
+// Persistent CTAs (one per SM) walk units chunk-major so that the CTAs
+// running at the same time read the same database rows (L2 reuse).
+//
+// Warp roles (192 threads):
+//   warps 0-3  epilogue: thread t owns query row t of the tile = TMEM lane t;
+//              reads 32 fp32 columns at a time with tcgen05.ld, forms the
+//              score s = alpha*dot + colbias[row] and keeps a register top-KP.
+//   warp 4     TMA producer: the query tile (A, hi and lo planes, all
+//              k-blocks) stays resident in shared memory for the unit; the
+//              database tile is streamed one (k-block, plane) of 32 KB per
+//              ring stage.
+//   warp 5     TMEM allocator + MMA issuer (one thread), M=128 N=256 K=8,
+//              double-buffered accumulators (2 x 256 TMEM columns).
+#include "kernels.cuh"
+#include "ptx.cuh"
+
+namespace mflat_cu {
+namespace {
+
+constexpr int kThreads = 192;
+constexpr int kEpiWarps = 4;
+constexpr int kProducerWarp = 4;
+constexpr int kMmaWarp = 5;
+constexpr int kATileBytes = kBM * kBK * 4;        // 16 KB: 128 rows x 128 B
+constexpr int kStageBytes = kBN * kBK * 4;        // 32 KB: 256 rows x 128 B
+constexpr int kMaxStages = 6;
+constexpr int kSmemBudget = 7 * kStageBytes;      // A + ring <= 224 KB
+constexpr uint32_t kIdescTF32 = make_idesc(2u, kBM, kBN);
+
+__host__ __device__ inline int n_stages_for(int kb) {
+    const int s = (kSmemBudget - kb * 2 * kATileBytes) / kStageBytes;
+    return s > kMaxStages ? kMaxStages : s;
+}
+
+struct SmemLayout {
+    uint8_t* a;          // [2 planes][kb][16 KB]
+    uint8_t* b;          // [stages][32 KB]
+    uint64_t* full;      // [kMaxStages]
+    uint64_t* empty;     // [kMaxStages]
+    uint64_t* a_full;
+    uint64_t* a_empty;
+    uint64_t* acc_full;  // [2]
+    uint64_t* acc_empty; // [2]
+    uint64_t* drain;
+    uint32_t* tmem_slot;
+    int* abort_flag;
+};
+
+__device__ inline SmemLayout carve(uint8_t* base, int kb, int stages) {
+    SmemLayout L;
+    L.a = base;
+    L.b = base + kb * 2 * kATileBytes;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(L.b + stages * kStageBytes);
+    L.full = bars;
+    L.empty = bars + kMaxStages;
+    L.a_full = bars + 2 * kMaxStages;
+    L.a_empty = L.a_full + 1;
+    L.acc_full = L.a_full + 2;
+    L.acc_empty = L.a_full + 4;
+    L.drain = L.a_full + 6;
+    L.tmem_slot = reinterpret_cast<uint32_t*>(L.a_full + 7);
+    L.abort_flag = reinterpret_cast<int*>(L.tmem_slot + 1);
+    return L;
+}
+
+template <int KP>
+__global__ void __launch_bounds__(kThreads, 1)
+screen_tf32x3_kernel(const __grid_constant__ CUtensorMap tm_a_hi,
+                     const __grid_constant__ CUtensorMap tm_a_lo,
+                     const __grid_constant__ CUtensorMap tm_b_hi,
+                     const __grid_constant__ CUtensorMap tm_b_lo, const ScreenParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* base = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    const int kb_count = p.d_pad / kBK;
+    if (kb_count < 1 || kb_count * kBK != p.d_pad || p.d_pad > kMaxDPadResident) {
+        if (threadIdx.x == 0) atomicExch(p.err, kErrConfig);
+        return;
+    }
+    const int stages = n_stages_for(kb_count);
+    SmemLayout S = carve(base, kb_count, stages);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kMaxStages; ++s) {
+            mbar_init(&S.full[s], 1);
+            mbar_init(&S.empty[s], 1);
+        }
+        mbar_init(S.a_full, 1);
+        mbar_init(S.a_empty, 1);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&S.acc_full[b], 1);
+            mbar_init(&S.acc_empty[b], kEpiWarps * 32);
+        }
+        mbar_init(S.drain, 1);
+        *S.abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == kMmaWarp) {
+        tmem_alloc(S.tmem_slot, 512);
+        tmem_relinquish();
+    }
+    if (warp == kProducerWarp && lane == 0) {
+        tma_prefetch_desc(&tm_a_hi);
+        tma_prefetch_desc(&tm_a_lo);
+        tma_prefetch_desc(&tm_b_hi);
+        tma_prefetch_desc(&tm_b_lo);
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *S.tmem_slot;
+    volatile int* abort_flag = S.abort_flag;
+
+    const int n_units = p.n_qtiles * p.n_chunks;
+
+    if (warp == kProducerWarp) {
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t sphase = 0, a_phase = 0;
+            uint32_t issued_mask = 0, issued_phase = 0;   // per stage, for the drain
+            bool a_issued = false;
+            uint32_t a_issue_phase = 0;
+            bool ok = true;
+            for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+                const int qt = u % p.n_qtiles;
+                const int ch = u / p.n_qtiles;
+                const int t0 = ch * p.tiles_per_chunk;
+                const int t1 = min(t0 + p.tiles_per_chunk, p.n_tiles);
+                if (!mbar_wait(S.a_empty, a_phase ^ 1u, abort_flag)) { ok = false; break; }
+                mbar_arrive_expect_tx(S.a_full, static_cast<uint32_t>(kb_count * 2 * kATileBytes));
+                for (int kb = 0; kb < kb_count; ++kb) {
+                    tma_load_2d(&tm_a_hi, S.a_full, S.a + kb * kATileBytes, kb * kBK, qt * kBM);
+                    tma_load_2d(&tm_a_lo, S.a_full, S.a + (kb_count + kb) * kATileBytes, kb * kBK,
+                                qt * kBM);
+                }
+                a_issued = true;
+                a_issue_phase = a_phase;
+                a_phase ^= 1u;
+                for (int t = t0; t < t1 && ok; ++t) {
+                    for (int kb = 0; kb < kb_count && ok; ++kb) {
+                        for (int plane = 0; plane < 2; ++plane) {
+                            if (!mbar_wait(&S.empty[stage], sphase ^ 1u, abort_flag)) { ok = false; break; }
+                            mbar_arrive_expect_tx(&S.full[stage], kStageBytes);
+                            tma_load_2d(plane ? &tm_b_lo : &tm_b_hi, &S.full[stage],
+                                        S.b + stage * kStageBytes, kb * kBK, t * kBN);
+                            issued_mask |= 1u << stage;
+                            issued_phase = (issued_phase & ~(1u << stage)) | (sphase << stage);
+                            if (++stage == stages) { stage = 0; sphase ^= 1u; }
+                        }
+                    }
+                }
+            }
+            if (*abort_flag) {
+                // Drain: let every copy this thread issued land before exit.
+                for (int s = 0; s < stages; ++s)
+                    if (issued_mask & (1u << s))
+                        mbar_wait_drain(&S.full[s], (issued_phase >> s) & 1u, 200000000ull);
+                if (a_issued) mbar_wait_drain(S.a_full, a_issue_phase, 200000000ull);
+            }
+        }
+    } else if (warp == kMmaWarp) {
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t sphase = 0, a_phase = 0;
+            uint32_t tcount = 0;
+            bool ok = true;
+            bool issued_any = false;
+            for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+                const int ch = u / p.n_qtiles;
+                const int t0 = ch * p.tiles_per_chunk;
+                const int t1 = min(t0 + p.tiles_per_chunk, p.n_tiles);
+                if (!mbar_wait(S.a_full, a_phase, abort_flag)) { ok = false; break; }
+                a_phase ^= 1u;
+                tc_fence_after();
+                const uint32_t a_addr = smem_u32(S.a);
+                for (int t = t0; t < t1 && ok; ++t, ++tcount) {
+                    const uint32_t b = tcount & 1u;
+                    const uint32_t ph = (tcount >> 1) & 1u;
+                    if (!mbar_wait(&S.acc_empty[b], ph ^ 1u, abort_flag)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t d_tmem = tmem_base + b * kBN;
+                    for (int kb = 0; kb < kb_count && ok; ++kb) {
+                        const uint64_t a_hi = smem_desc_k_sw128(a_addr + kb * kATileBytes);
+                        const uint64_t a_lo =
+                            smem_desc_k_sw128(a_addr + (kb_count + kb) * kATileBytes);
+                        // stage holding B_hi of this k-block
+                        if (!mbar_wait(&S.full[stage], sphase, abort_flag)) { ok = false; break; }
+                        tc_fence_after();
+                        uint64_t bd = smem_desc_k_sw128(smem_u32(S.b + stage * kStageBytes));
+#pragma unroll
+                        for (int ks = 0; ks < kBK / 8; ++ks) {
+                            const uint64_t o = static_cast<uint64_t>(ks * 2);   // 32 B >> 4
+                            tc_mma_tf32(d_tmem, a_hi + o, bd + o, kIdescTF32,
+                                        (kb | ks) != 0 ? 1u : 0u);
+                            tc_mma_tf32(d_tmem, a_lo + o, bd + o, kIdescTF32, 1u);
+                        }
+                        issued_any = true;
+                        tc_commit(&S.empty[stage]);
+                        if (++stage == stages) { stage = 0; sphase ^= 1u; }
+                        // stage holding B_lo of this k-block
+                        if (!mbar_wait(&S.full[stage], sphase, abort_flag)) { ok = false; break; }
+                        tc_fence_after();
+                        bd = smem_desc_k_sw128(smem_u32(S.b + stage * kStageBytes));
+#pragma unroll
+                        for (int ks = 0; ks < kBK / 8; ++ks) {
+                            const uint64_t o = static_cast<uint64_t>(ks * 2);
+                            tc_mma_tf32(d_tmem, a_hi + o, bd + o, kIdescTF32, 1u);
+                        }
+                        tc_commit(&S.empty[stage]);
+                        if (++stage == stages) { stage = 0; sphase ^= 1u; }
+                    }
+                    if (ok) tc_commit(&S.acc_full[b]);
+                }
+                if (ok) tc_commit(S.a_empty);
+            }
+            if (*abort_flag && issued_any) {
+                tc_commit(S.drain);
+                mbar_wait_drain(S.drain, 0u, 200000000ull);
+            }
+        }
+    } else {
+        // ---------------- epilogue: warps 0..3, thread = query row
+        const int row_in_tile = warp * 32 + lane;
+        const uint32_t lane_addr = tmem_base + (static_cast<uint32_t>(warp * 32) << 16);
+        uint32_t tcount = 0;
+        bool ok = true;
+        for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+            const int qt = u % p.n_qtiles;
+            const int ch = u / p.n_qtiles;
+            const int t0 = ch * p.tiles_per_chunk;
+            const int t1 = min(t0 + p.tiles_per_chunk, p.n_tiles);
+            TopList<KP> L;
+            L.init();
+            for (int t = t0; t < t1; ++t, ++tcount) {
+                const uint32_t b = tcount & 1u;
+                const uint32_t ph = (tcount >> 1) & 1u;
+                if (!mbar_wait(&S.acc_full[b], ph, abort_flag)) { ok = false; break; }
+                __syncwarp();
+                tc_fence_after();
+                const float* cb_tile = p.colbias + static_cast<int64_t>(t) * kBN;
+#pragma unroll 1
+                for (int c = 0; c < kBN / 32; ++c) {
+                    uint32_t r[32];
+                    __syncwarp();   // tcgen05.ld is .sync.aligned
+                    tmem_ld_32x32b_x32(lane_addr + b * kBN + c * 32, r);
+                    tmem_wait_ld();
+                    const float4* cb4 = reinterpret_cast<const float4*>(cb_tile + c * 32);
+                    float sc[32];
+                    uint32_t mask = 0;
+                    const float worst = L.worst();
+#pragma unroll
+                    for (int q4 = 0; q4 < 8; ++q4) {
+                        const float4 cb = __ldg(cb4 + q4);
+                        sc[q4 * 4 + 0] = fmaf(p.alpha, __uint_as_float(r[q4 * 4 + 0]), cb.x);
+                        sc[q4 * 4 + 1] = fmaf(p.alpha, __uint_as_float(r[q4 * 4 + 1]), cb.y);
+                        sc[q4 * 4 + 2] = fmaf(p.alpha, __uint_as_float(r[q4 * 4 + 2]), cb.z);
+                        sc[q4 * 4 + 3] = fmaf(p.alpha, __uint_as_float(r[q4 * 4 + 3]), cb.w);
+                    }
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) mask |= (sc[j] > worst ? 1u : 0u) << j;
+                    if (mask) {
+                        const int id0 = t * kBN + c * 32;
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            if (((mask >> j) & 1u) && sc[j] > L.worst()) L.insert(sc[j], id0 + j);
+                    }
+                }
+                tc_fence_before();
+                mbar_arrive(&S.acc_empty[b]);
+            }
+            if (!ok) break;
+            const int row = qt * kBM + row_in_tile;
+            if (row < p.m) {
+                const int64_t o = (static_cast<int64_t>(ch) * p.m_pad + row) * KP;
+                float4* ps = reinterpret_cast<float4*>(p.part_score + o);
+                int4* pi = reinterpret_cast<int4*>(p.part_id + o);
+#pragma unroll
+                for (int i = 0; i < KP / 4; ++i) {
+                    ps[i] = make_float4(L.s[4 * i], L.s[4 * i + 1], L.s[4 * i + 2], L.s[4 * i + 3]);
+                    pi[i] = make_int4(L.id[4 * i], L.id[4 * i + 1], L.id[4 * i + 2], L.id[4 * i + 3]);
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == kMmaWarp) tmem_dealloc(tmem_base, 512);
+    if (threadIdx.x == 0 && *abort_flag) atomicExch(p.err, *abort_flag);
+}
+
+template <int KP>
+cudaError_t launch_kp(const CUtensorMap& a_hi, const CUtensorMap& a_lo, const CUtensorMap& b_hi,
+                      const CUtensorMap& b_lo, const ScreenParams& p, int grid,
+                      cudaStream_t stream) {
+    const int smem = screen_tf32x3_smem_bytes(p.d_pad);
+    cudaError_t e = cudaFuncSetAttribute(screen_tf32x3_kernel<KP>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    screen_tf32x3_kernel<KP><<<grid, kThreads, smem, stream>>>(a_hi, a_lo, b_hi, b_lo, p);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+int screen_tf32x3_smem_bytes(int d_pad) {
+    const int kb = d_pad / kBK;
+    return 1024 + kb * 2 * kATileBytes + n_stages_for(kb) * kStageBytes + 256;
+}
+
+cudaError_t launch_screen_tf32x3(int kp, const CUtensorMap& a_hi, const CUtensorMap& a_lo,
+                                 const CUtensorMap& b_hi, const CUtensorMap& b_lo,
+                                 const ScreenParams& p, int grid, cudaStream_t stream) {
+    if (p.d_pad % kBK != 0 || p.d_pad > kMaxDPadResident || p.d_pad < kBK) return cudaErrorInvalidValue;
+    switch (kp) {
+        case 4: return launch_kp<4>(a_hi, a_lo, b_hi, b_lo, p, grid, stream);
+        case 8: return launch_kp<8>(a_hi, a_lo, b_hi, b_lo, p, grid, stream);
+        case 16: return launch_kp<16>(a_hi, a_lo, b_hi, b_lo, p, grid, stream);
+        case 32: return launch_kp<32>(a_hi, a_lo, b_hi, b_lo, p, grid, stream);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+}  // namespace mflat_cu

@@ -1,0 +1,277 @@
+// SPDX-License-Identifier: Apache-2.0
+// mflat_capi.cpp -- the C ABI (include/mflat.h) over the C++ engine.
+//
+// Same shell as the reference's c/mflat.cpp:1-199 for the flat, logging and
+// version entries: each handle pairs the engine with a std::mutex so calls on
+// one handle are serialised; every entry point maps C++ exceptions to status
+// codes (bad_alloc -> ALLOC, device failure -> DEVICE (additive), anything
+// else -> INTERNAL); results are copied into caller buffers packed at stride
+// k_used; the C log handler reaches the C++ sink through a trampoline.
+#include <atomic>
+#include <cstring>
+#include <mutex>
+#include <new>
+#include <stdexcept>
+
+#include "../../../include/mflat.h"
+#include "../cuda/mflat_cuda.h"
+#include "metalflat/FlatIndex.h"
+#include "metalflat/Log.h"
+
+using mflat::DeviceError;
+using mflat::FlatIndex;
+using mflat::Metric;
+using mflat::SearchResult;
+
+namespace {
+
+Metric to_metric(mflat_metric_t m) {
+    switch (m) {
+        case MFLAT_METRIC_INNER_PRODUCT: return Metric::InnerProduct;
+        case MFLAT_METRIC_COSINE: return Metric::Cosine;
+        default: return Metric::L2;
+    }
+}
+
+mflat::Storage to_storage(mflat_storage_t s) {
+    switch (s) {
+        case MFLAT_STORAGE_FP16: return mflat::Storage::FP16;
+        case MFLAT_STORAGE_BF16: return mflat::Storage::BF16;
+        default: return mflat::Storage::FP32;
+    }
+}
+
+mflat_status_t emit(const SearchResult& r, int m, int32_t* out_ids, float* out_dist, int* out_k_used) {
+    if (m <= 0 || r.ids.empty()) {
+        if (out_k_used) *out_k_used = 0;
+        return MFLAT_OK;
+    }
+    const int k_used = static_cast<int>(r.ids.size() / static_cast<size_t>(m));
+    if (out_ids) std::memcpy(out_ids, r.ids.data(), r.ids.size() * sizeof(int32_t));
+    if (out_dist) std::memcpy(out_dist, r.distances.data(), r.distances.size() * sizeof(float));
+    if (out_k_used) *out_k_used = k_used;
+    return MFLAT_OK;
+}
+
+std::atomic<mflat_log_handler_t> g_c_handler{nullptr};
+std::atomic<void*> g_c_user{nullptr};
+
+void c_log_trampoline(mflat::LogLevel level, const char* msg, void*) {
+    if (mflat_log_handler_t h = g_c_handler.load(std::memory_order_acquire))
+        h(static_cast<mflat_log_level_t>(level), msg, g_c_user.load(std::memory_order_acquire));
+}
+
+// Run `fn` and translate exceptions to status codes.
+template <class Fn>
+mflat_status_t guarded(Fn&& fn) {
+    try {
+        return fn();
+    } catch (const std::bad_alloc&) {
+        return MFLAT_ERR_ALLOC;
+    } catch (const std::invalid_argument&) {
+        return MFLAT_ERR_BAD_ARG;
+    } catch (const DeviceError&) {
+        return MFLAT_ERR_DEVICE;
+    } catch (...) {
+        return MFLAT_ERR_INTERNAL;
+    }
+}
+
+mflat_status_t from_cu(int st) {
+    switch (st) {
+        case 0: return MFLAT_OK;
+        case 2: return MFLAT_ERR_BAD_ARG;
+        case 3: return MFLAT_ERR_ALLOC;
+        case 5: return MFLAT_ERR_INTERNAL;
+        default: return MFLAT_ERR_DEVICE;
+    }
+}
+
+}  // namespace
+
+struct mflat_flat_index {
+    FlatIndex idx;
+    std::mutex mu;
+    mflat_flat_index(int d, Metric m, mflat::Storage s, int dev) : idx(d, m, s, dev) {}
+};
+
+extern "C" {
+
+MFLAT_API const char* mflat_version(void) { return "0.1.0"; }
+MFLAT_API int mflat_max_k(void) { return MFLAT_MAX_K; }
+
+MFLAT_API void mflat_set_log_handler(mflat_log_handler_t h, void* user) {
+    g_c_user.store(user, std::memory_order_release);
+    g_c_handler.store(h, std::memory_order_release);
+    mflat::setLogHandler(h ? &c_log_trampoline : nullptr, nullptr);
+}
+
+MFLAT_API void mflat_set_log_level(mflat_log_level_t l) {
+    mflat::setLogLevel(static_cast<mflat::LogLevel>(l));
+}
+
+MFLAT_API mflat_log_level_t mflat_log_level(void) {
+    return static_cast<mflat_log_level_t>(mflat::logLevel());
+}
+
+MFLAT_API const char* mflat_status_str(mflat_status_t s) {
+    switch (s) {
+        case MFLAT_OK: return "ok";
+        case MFLAT_ERR_NULL_ARG: return "null argument";
+        case MFLAT_ERR_BAD_ARG: return "bad argument";
+        case MFLAT_ERR_ALLOC: return "allocation failed";
+        case MFLAT_ERR_NOT_READY: return "index not built";
+        case MFLAT_ERR_INTERNAL: return "internal error";
+        case MFLAT_ERR_DEVICE: return "device error";
+    }
+    return "unknown";
+}
+
+MFLAT_API mflat_flat_index_t* mflat_flat_create_ex(int dim, mflat_metric_t metric,
+                                                   mflat_storage_t storage, int device,
+                                                   mflat_status_t* st) {
+    if (dim <= 0) {
+        if (st) *st = MFLAT_ERR_BAD_ARG;
+        return nullptr;
+    }
+    try {
+        auto* h = new mflat_flat_index(dim, to_metric(metric), to_storage(storage), device);
+        if (st) *st = MFLAT_OK;
+        return h;
+    } catch (const std::bad_alloc&) {
+        if (st) *st = MFLAT_ERR_ALLOC;
+    } catch (const std::invalid_argument&) {
+        if (st) *st = MFLAT_ERR_BAD_ARG;
+    } catch (...) {
+        if (st) *st = MFLAT_ERR_INTERNAL;
+    }
+    return nullptr;
+}
+
+MFLAT_API mflat_flat_index_t* mflat_flat_create(int dim, mflat_metric_t metric, mflat_status_t* st) {
+    return mflat_flat_create_ex(dim, metric, MFLAT_STORAGE_FP32, -1, st);
+}
+
+MFLAT_API void mflat_flat_free(mflat_flat_index_t* h) { delete h; }
+MFLAT_API int mflat_flat_ready(const mflat_flat_index_t* h) { return (h && h->idx.ready()) ? 1 : 0; }
+MFLAT_API int mflat_flat_size(const mflat_flat_index_t* h) { return h ? h->idx.size() : 0; }
+MFLAT_API int mflat_flat_dim(const mflat_flat_index_t* h) { return h ? h->idx.dim() : 0; }
+MFLAT_API int mflat_flat_storage(const mflat_flat_index_t* h) {
+    return h ? static_cast<int>(h->idx.storage()) : 0;
+}
+MFLAT_API int mflat_flat_device(const mflat_flat_index_t* h) { return h ? h->idx.device() : -1; }
+
+MFLAT_API mflat_status_t mflat_flat_add(mflat_flat_index_t* h, const float* v, int n) {
+    if (!h || !v) return MFLAT_ERR_NULL_ARG;
+    if (n < 0) return MFLAT_ERR_BAD_ARG;
+    return guarded([&] {
+        std::lock_guard<std::mutex> lk(h->mu);
+        h->idx.add(v, n);
+        return MFLAT_OK;
+    });
+}
+
+MFLAT_API mflat_status_t mflat_flat_add_device(mflat_flat_index_t* h, const float* v, int n,
+                                               void* stream) {
+    if (!h || !v) return MFLAT_ERR_NULL_ARG;
+    if (n < 0) return MFLAT_ERR_BAD_ARG;
+    return guarded([&] {
+        std::lock_guard<std::mutex> lk(h->mu);
+        h->idx.addDevice(v, n, stream);
+        return MFLAT_OK;
+    });
+}
+
+MFLAT_API mflat_status_t mflat_flat_reset(mflat_flat_index_t* h) {
+    if (!h) return MFLAT_ERR_NULL_ARG;
+    return guarded([&] {
+        std::lock_guard<std::mutex> lk(h->mu);
+        h->idx.reset();
+        return MFLAT_OK;
+    });
+}
+
+MFLAT_API mflat_status_t mflat_flat_search(mflat_flat_index_t* h, const float* q, int m, int k,
+                                           int32_t* oi, float* od, int* ok) {
+    if (!h || !q) return MFLAT_ERR_NULL_ARG;
+    if (m < 0 || k < 1) return MFLAT_ERR_BAD_ARG;
+    return guarded([&] {
+        std::lock_guard<std::mutex> lk(h->mu);
+        return emit(h->idx.search(q, m, k), m, oi, od, ok);
+    });
+}
+
+MFLAT_API mflat_status_t mflat_flat_search_device(mflat_flat_index_t* h, const float* q, int m,
+                                                  int k, int32_t* oi, float* od, int* ok,
+                                                  void* stream) {
+    if (!h || !q) return MFLAT_ERR_NULL_ARG;
+    if (m < 0 || k < 1) return MFLAT_ERR_BAD_ARG;
+    if (m > 0 && (!oi || !od)) return MFLAT_ERR_NULL_ARG;
+    return guarded([&] {
+        std::lock_guard<std::mutex> lk(h->mu);
+        const int used = h->idx.searchDevice(q, m, k, oi, od, stream);
+        if (ok) *ok = used;
+        return MFLAT_OK;
+    });
+}
+
+MFLAT_API mflat_status_t mflat_flat_set_timing(mflat_flat_index_t* h, int enable) {
+    if (!h) return MFLAT_ERR_NULL_ARG;
+    return guarded([&] {
+        std::lock_guard<std::mutex> lk(h->mu);
+        h->idx.setTiming(enable != 0);
+        return MFLAT_OK;
+    });
+}
+
+MFLAT_API mflat_status_t mflat_flat_last_timing(const mflat_flat_index_t* h, mflat_timing_t* out) {
+    if (!h || !out) return MFLAT_ERR_NULL_ARG;
+    const mflat::SearchTiming t = h->idx.lastTiming();
+    out->total_ms = t.total_ms;
+    out->screen_ms = t.screen_ms;
+    out->select_ms = t.select_ms;
+    out->screen_launches = t.screen_launches;
+    out->launches = t.launches;
+    out->fallback_queries = t.fallback_queries;
+    return MFLAT_OK;
+}
+
+MFLAT_API mflat_status_t mflat_kmeans_assign(const float* points, int n, const float* centroids,
+                                             int ncentroids, int dim, int32_t* out_assign,
+                                             int device) {
+    if (!points || !centroids || !out_assign) return MFLAT_ERR_NULL_ARG;
+    if (n < 0 || ncentroids < 1 || dim < 1) return MFLAT_ERR_BAD_ARG;
+    return guarded([&] {
+        mflat::kmeansAssign(points, n, centroids, ncentroids, dim, out_assign, device);
+        return MFLAT_OK;
+    });
+}
+
+MFLAT_API mflat_status_t mflat_kmeans_assign_device(const float* points, int n,
+                                                    const float* centroids, int ncentroids, int dim,
+                                                    int32_t* out_assign, int device, void* stream) {
+    if (!points || !centroids || !out_assign) return MFLAT_ERR_NULL_ARG;
+    if (n < 0 || ncentroids < 1 || dim < 1) return MFLAT_ERR_BAD_ARG;
+    return from_cu(mflat_cu_kmeans_assign(points, n, centroids, ncentroids, dim, out_assign, device,
+                                          1, stream));
+}
+
+MFLAT_API mflat_status_t mflat_comm_unique_id(uint8_t out_id[MFLAT_COMM_ID_BYTES]) {
+    if (!out_id) return MFLAT_ERR_NULL_ARG;
+    return from_cu(mflat_cu_comm_unique_id(out_id));
+}
+
+MFLAT_API mflat_status_t mflat_flat_set_shard(mflat_flat_index_t* h, int rank, int world,
+                                              const uint8_t comm_id[MFLAT_COMM_ID_BYTES],
+                                              int64_t id_base) {
+    if (!h) return MFLAT_ERR_NULL_ARG;
+    if (world < 1 || rank < 0 || rank >= world || id_base < 0) return MFLAT_ERR_BAD_ARG;
+    if (world > 1 && !comm_id) return MFLAT_ERR_NULL_ARG;
+    return guarded([&] {
+        std::lock_guard<std::mutex> lk(h->mu);
+        h->idx.setShard(rank, world, comm_id, id_base);
+        return MFLAT_OK;
+    });
+}
+
+}  // extern "C"

@@ -1,0 +1,90 @@
+// SPDX-License-Identifier: Apache-2.0
+// metalflat/FlatIndex.h -- exact (brute-force) vector search on NVIDIA B200.
+//
+// Same class, members and result layout as the reference's
+// include/metalflat/FlatIndex.h:28-77, so code written against it compiles
+// unchanged.  Differences a caller can observe:
+//   * kMaxK is 1024 (was 64); larger k is clamped with a one-time warning.
+//   * There is no CPU fallback: when no usable CUDA device exists, ready() is
+//     false and search() throws DeviceError.
+//   * The database lives on the device; add() appends there directly.
+// Additive members (storage precision, device pointers, timing, sharding)
+// sit below the reference's.
+#pragma once
+
+#include <cstdint>
+#include <memory>
+#include <stdexcept>
+#include <vector>
+
+#include "metalflat/Metric.h"
+
+namespace mflat {
+
+struct SearchResult {
+    // Row-major: m rows of k.  ids[r*k + j] is the database index of query r's
+    // j-th nearest neighbour (-1 when the database holds fewer than k rows);
+    // distances[r*k + j] its squared L2 distance or IP / cosine similarity.
+    std::vector<int32_t> ids;
+    std::vector<float>   distances;
+};
+
+// Storage precision of the database on the device.
+enum class Storage { FP32 = 0, FP16 = 1, BF16 = 2 };
+
+// Thrown when the CUDA device (or NCCL) fails or is absent.
+class DeviceError : public std::runtime_error {
+public:
+    using std::runtime_error::runtime_error;
+};
+
+struct SearchTiming {
+    float total_ms = 0, screen_ms = 0, select_ms = 0;
+    int screen_launches = 0, launches = 0, fallback_queries = 0;
+};
+
+class FlatIndex {
+public:
+    static constexpr int kMaxK = 1024;
+
+    FlatIndex(int dim, Metric metric);
+    FlatIndex(int dim, Metric metric, Storage storage, int device = -1);
+    ~FlatIndex();
+
+    FlatIndex(const FlatIndex&)            = delete;
+    FlatIndex& operator=(const FlatIndex&) = delete;
+
+    bool ready() const;                       // usable CUDA device
+    void add(const float* vectors, int n);    // n <= 0: no-op
+    void reset();
+    int    size() const;
+    int    dim() const;
+    Metric metric() const;
+    // k is clamped to [1, kMaxK]; m <= 0 returns an empty result.
+    SearchResult search(const float* queries, int m, int k);
+
+    // ---- additive ----
+    Storage storage() const;
+    int     device() const;
+    void addDevice(const float* d_vectors, int n, void* stream);
+    // Device pointers; enqueues on `stream`; returns the k actually used
+    // (outputs are written at that row stride).
+    int  searchDevice(const float* d_queries, int m, int k, int32_t* d_ids, float* d_dist,
+                      void* stream);
+    void setTiming(bool enable);
+    SearchTiming lastTiming() const;
+    // Row sharding: this index holds global rows [id_base, id_base + size());
+    // search() becomes a collective over `world` ranks returning global ids.
+    void setShard(int rank, int world, const uint8_t* comm_id, int64_t id_base);
+
+private:
+    struct Impl;
+    std::unique_ptr<Impl> mImpl;
+};
+
+// k-means assignment step: out[i] = argmin_c sqL2_f32(points[i], centroids[c])
+// with the reference's fp32 sequential sqL2 and lowest-index tie rule.
+void kmeansAssign(const float* points, int n, const float* centroids, int ncentroids, int dim,
+                  int32_t* out, int device = -1);
+
+}  // namespace mflat

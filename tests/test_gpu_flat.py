@@ -1,0 +1,174 @@
+"""GPU parity of the exact flat path, through the C ABI.
+
+Criterion: ids identical to the fp64 brute-force oracle
+(reference Distance.h semantics, ties to the lowest id) except inside near-ties
+closer than 1e-6 relative; distances within 1e-5 relative."""
+import os
+
+import numpy as np
+import pytest
+
+import mflat_b200 as M
+import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+METRIC = {"l2": O.L2, "ip": O.IP, "cosine": O.COSINE}
+REL_TIE = 1e-6
+REL_DIST = 1e-5
+
+
+def search(db, q, k, metric, **kw):
+    idx = M.FlatIndex(db.shape[1], metric, **kw)
+    assert idx.ready
+    if db.shape[0]:
+        idx.add(db)
+    return idx.search(q, k)
+
+
+def assert_exact(ids, dist, db, q, k, metric):
+    ref_i, ref_d = O.flat_search_f64(db, q, k + 1, METRIC[metric])
+    assert ids.shape == (q.shape[0], k)
+    assert O.exact_ids_match(ids, dist, ref_i, ref_d, rel=REL_TIE) == 0
+    rd = ref_d[:, :k]
+    fin = np.isfinite(rd)
+    assert np.array_equal(fin, np.isfinite(dist))
+    assert np.array_equal(ids[~fin], np.full((~fin).sum(), -1))
+    err = np.abs(dist[fin].astype(np.float64) - rd[fin]) / np.maximum(np.abs(rd[fin]), 1e-20)
+    assert err.max(initial=0.0) <= REL_DIST
+
+
+SHAPES = [  # n, dim, m, k
+    (1, 8, 3, 1), (5, 8, 4, 10), (255, 17, 7, 10), (256, 32, 128, 10), (257, 33, 129, 5),
+    (1000, 100, 300, 16), (3000, 128, 64, 21), (4099, 3, 33, 7), (2000, 1, 5, 4),
+    (1500, 129, 20, 10), (800, 200, 11, 8),
+]
+
+
+@pytest.mark.parametrize("metric", ["l2", "ip", "cosine"])
+@pytest.mark.parametrize("shape", SHAPES, ids=lambda s: "n%d_d%d_m%d_k%d" % s)
+def test_random_shapes(metric, shape):
+    n, dim, m, k = shape
+    rng = np.random.default_rng(hash((metric,) + shape) % 2**32)
+    db = rng.standard_normal((n, dim)).astype(np.float32)
+    q = rng.standard_normal((m, dim)).astype(np.float32)
+    ids, dist = search(db, q, k, metric)
+    assert_exact(ids, dist, db, q, k, metric)
+
+
+def test_golden_cases(golden_dir):
+    """The reference's own cpuSearch results (golden) and the fp64 oracle."""
+    c = np.load(os.path.join(golden_dir, "cpusearch.npz"))
+    names = sorted({f.rsplit("_", 1)[0] for f in c.files})
+    mname = {0: "l2", 1: "ip", 2: "cosine"}
+    for nm in names:
+        n, dim, m, k, metric = (int(x) for x in c[nm + "_meta"])
+        if k > 21:
+            continue                                # large-k path covered elsewhere
+        db, q = c[nm + "_db"], c[nm + "_q"]
+        ids, dist = search(db, q, k, mname[metric])
+        assert_exact(ids, dist, db, q, k, mname[metric])
+        assert O.exact_ids_match(ids, dist, c[nm + "_ids"], c[nm + "_dist"], rel=1e-5) == 0, nm
+
+
+@pytest.mark.parametrize("metric", ["l2", "ip"])
+def test_duplicates_and_exact_ties(metric):
+    """Many identical rows: ties must come back lowest-id first (the proof
+    fails for these queries and the exact full scan answers them)."""
+    rng = np.random.default_rng(11)
+    base = rng.standard_normal((6, 24)).astype(np.float32)
+    db = base[rng.integers(0, 6, size=700)]
+    q = np.concatenate([base[:3], rng.standard_normal((5, 24)).astype(np.float32)])
+    ids, dist = search(db, q, 12, metric)
+    ref_i, ref_d = O.flat_search_f64(db, q, 12, METRIC[metric])
+    assert np.array_equal(ids, ref_i)
+    assert np.array_equal(dist, ref_d)
+
+
+def test_all_rows_identical():
+    db = np.ones((5000, 16), np.float32)
+    ids, dist = search(db, np.zeros((3, 16), np.float32), 10, "l2")
+    assert (ids == np.arange(10)).all()
+    assert (dist == 16.0).all()
+
+
+@pytest.mark.parametrize("metric,empty", [("l2", np.inf), ("ip", -np.inf), ("cosine", -np.inf)])
+def test_empty_database(metric, empty):
+    idx = M.FlatIndex(8, metric)
+    ids, dist = idx.search(np.ones((3, 8), np.float32), 4)
+    assert ids.shape == (3, 4) and (ids == -1).all() and (dist == empty).all()
+
+
+def test_incremental_add_and_reset():
+    rng = np.random.default_rng(2)
+    parts = [rng.standard_normal((n, 40)).astype(np.float32) for n in (100, 1, 333, 4096)]
+    q = rng.standard_normal((50, 40)).astype(np.float32)
+    idx = M.FlatIndex(40, "l2")
+    for p in parts:
+        idx.add(p)
+    db = np.concatenate(parts)
+    assert idx.size == db.shape[0]
+    ids, dist = idx.search(q, 10)
+    assert_exact(ids, dist, db, q, 10, "l2")
+    idx.reset()
+    assert idx.size == 0
+    ids, _ = idx.search(q, 3)
+    assert (ids == -1).all()
+    idx.add(parts[2])
+    ids, dist = idx.search(q, 10)
+    assert_exact(ids, dist, parts[2], q, 10, "l2")
+
+
+def test_n_smaller_than_k_pads():
+    rng = np.random.default_rng(4)
+    db = rng.standard_normal((3, 8)).astype(np.float32)
+    q = rng.standard_normal((2, 8)).astype(np.float32)
+    ids, dist = search(db, q, 10, "l2")
+    assert (ids[:, 3:] == -1).all() and np.isinf(dist[:, 3:]).all()
+    assert_exact(ids, dist, db, q, 10, "l2")
+
+
+def test_simt_screen_agrees_with_tensor_core_screen():
+    rng = np.random.default_rng(8)
+    db = rng.random((20000, 128), dtype=np.float32)
+    q = rng.random((300, 128), dtype=np.float32)
+    a = search(db, q, 10, "l2")
+    os.environ["MFLAT_SCREEN"] = "simt"
+    try:
+        b = search(db, q, 10, "l2")
+    finally:
+        del os.environ["MFLAT_SCREEN"]
+    assert np.array_equal(a[0], b[0]) and np.array_equal(a[1], b[1])
+    assert_exact(a[0], a[1], db, q, 10, "l2")
+
+
+def test_config1_full():
+    """N=100k x 128, Q=1000, N(0,1) seed 0, k=10, all queries."""
+    rng = np.random.default_rng(0)
+    db = rng.standard_normal((100_000, 128), dtype=np.float32)
+    q = rng.standard_normal((1000, 128), dtype=np.float32)
+    idx = M.FlatIndex(128, "l2")
+    idx.add(db)
+    idx.set_timing(True)
+    ids, dist = idx.search(q, 10)
+    t = idx.last_timing()
+    assert t.screen_launches == 1 and t.launches >= 3
+    assert_exact(ids, dist, db, q, 10, "l2")
+
+
+def test_device_pointer_api():
+    torch = pytest.importorskip("torch")
+    rng = np.random.default_rng(9)
+    db = rng.standard_normal((5000, 64)).astype(np.float32)
+    q = rng.standard_normal((77, 64)).astype(np.float32)
+    idx = M.FlatIndex(64, "ip")
+    d_db = torch.from_numpy(db).cuda()
+    stream = torch.cuda.current_stream().cuda_stream
+    idx.add_device(d_db.data_ptr(), db.shape[0], stream)
+    d_q = torch.from_numpy(q).cuda()
+    d_ids = torch.empty((77, 10), dtype=torch.int32, device="cuda")
+    d_dist = torch.empty((77, 10), dtype=torch.float32, device="cuda")
+    used = idx.search_device(d_q.data_ptr(), 77, 10, d_ids.data_ptr(), d_dist.data_ptr(), stream)
+    assert used == 10
+    torch.cuda.synchronize()
+    assert_exact(d_ids.cpu().numpy(), d_dist.cpu().numpy(), db, q, 10, "ip")
