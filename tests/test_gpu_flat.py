@@ -18,12 +18,16 @@ REL_TIE = 1e-6
 REL_DIST = 1e-5
 
 
-def search(db, q, k, metric, **kw):
+def search(db, q, k, metric, timing=None, **kw):
     idx = M.FlatIndex(db.shape[1], metric, **kw)
     assert idx.ready
     if db.shape[0]:
         idx.add(db)
-    return idx.search(q, k)
+    idx.set_timing(True)
+    out = idx.search(q, k)
+    if timing is not None:
+        timing.append(idx.last_timing())
+    return out
 
 
 def assert_exact(ids, dist, db, q, k, metric):
@@ -52,8 +56,13 @@ def test_random_shapes(metric, shape):
     rng = np.random.default_rng(hash((metric,) + shape) % 2**32)
     db = rng.standard_normal((n, dim)).astype(np.float32)
     q = rng.standard_normal((m, dim)).astype(np.float32)
-    ids, dist = search(db, q, k, metric)
+    tm = []
+    ids, dist = search(db, q, k, metric, timing=tm)
     assert_exact(ids, dist, db, q, k, metric)
+    if dim >= 32 and n >= 256:
+        # well-separated data: the error-bound proof holds for every query,
+        # so the tensor-core screen alone produced the candidates
+        assert tm[0].fallback_queries == 0
 
 
 def test_golden_cases(golden_dir):
@@ -79,7 +88,9 @@ def test_duplicates_and_exact_ties(metric):
     base = rng.standard_normal((6, 24)).astype(np.float32)
     db = base[rng.integers(0, 6, size=700)]
     q = np.concatenate([base[:3], rng.standard_normal((5, 24)).astype(np.float32)])
-    ids, dist = search(db, q, 12, metric)
+    tm = []
+    ids, dist = search(db, q, 12, metric, timing=tm)
+    assert tm[0].fallback_queries > 0            # the exact full scan was exercised
     ref_i, ref_d = O.flat_search_f64(db, q, 12, METRIC[metric])
     assert np.array_equal(ids, ref_i)
     assert np.array_equal(dist, ref_d)
@@ -132,13 +143,15 @@ def test_simt_screen_agrees_with_tensor_core_screen():
     rng = np.random.default_rng(8)
     db = rng.random((20000, 128), dtype=np.float32)
     q = rng.random((300, 128), dtype=np.float32)
-    a = search(db, q, 10, "l2")
+    ta, tb = [], []
+    a = search(db, q, 10, "l2", timing=ta)
     os.environ["MFLAT_SCREEN"] = "simt"
     try:
-        b = search(db, q, 10, "l2")
+        b = search(db, q, 10, "l2", timing=tb)
     finally:
         del os.environ["MFLAT_SCREEN"]
     assert np.array_equal(a[0], b[0]) and np.array_equal(a[1], b[1])
+    assert ta[0].fallback_queries == 0 and tb[0].fallback_queries == 0
     assert_exact(a[0], a[1], db, q, 10, "l2")
 
 
@@ -153,6 +166,7 @@ def test_config1_full():
     ids, dist = idx.search(q, 10)
     t = idx.last_timing()
     assert t.screen_launches == 1 and t.launches >= 3
+    assert t.fallback_queries == 0 and t.screen_ms > 0
     assert_exact(ids, dist, db, q, 10, "l2")
 
 
