@@ -245,14 +245,10 @@ void order_after(cudaStream_t waiter, cudaStream_t producer) {
     cudaEventDestroy(e);
 }
 
-// Candidate-list length for the exact path: k plus a margin that absorbs the
-// rows whose screen scores fall inside the proven error band.
-int kp_for(int k) {
-    const int need = k + std::max(3, k / 2);
-    for (int kp : {4, 8, 16, 32})
-        if (kp >= need) return kp;
-    return 0;
-}
+// Candidate-list length for the exact path: k plus a margin (>= 11 rows)
+// that absorbs the rows whose screen scores fall inside the proven error
+// band, so that the exact fallback stays rare.
+int kp_for(int k) { return k <= 21 ? 32 : 0; }
 
 // Database chunks per query tile: whole work units on every SM.
 void plan_chunks(int n_qtiles, int n_tiles, int num_sms, int max_chunks, int& n_chunks,
@@ -311,6 +307,8 @@ int run_screen(mflat_cu_index* ix, const float* queries, int m, int kp, int on_d
     const size_t parts = static_cast<size_t>(n_chunks) * m_pad * kp;
     CU_TRY(ix->part_s.ensure(parts * sizeof(float)), "candidate lists");
     CU_TRY(ix->part_i.ensure(parts * sizeof(int32_t)), "candidate lists");
+    CU_TRY(ix->thr.ensure(static_cast<size_t>(m_pad) * sizeof(uint32_t)), "score floors");
+    CU_TRY(cudaMemsetAsync(ix->thr.p, 0, static_cast<size_t>(m_pad) * sizeof(uint32_t), st), "floors");
 
     if (ix->timing) cudaEventRecord(ix->ev[0], st);
     prep_queries_kernel<<<blocks_for(m_pad, 128), 128, 0, st>>>(
@@ -332,6 +330,7 @@ int run_screen(mflat_cu_index* ix, const float* queries, int m, int kp, int on_d
     sp.part_score = ix->part_s.as<float>();
     sp.part_id = ix->part_i.as<int32_t>();
     sp.err = ix->err;
+    sp.thr = ix->thr.as<uint32_t>();
     sp.q_hi = ix->q_hi.as<float>();
     sp.q_lo = ix->q_lo.as<float>();
     sp.db_hi = ix->db_hi;
@@ -448,7 +447,8 @@ void mflat_cu_index_destroy(mflat_cu_index_t* ix) {
     if (ix->host_words) cudaFreeHost(ix->host_words);
     for (DevBuf* b : {&ix->stage_in, &ix->q_in, &ix->q_hi, &ix->q_lo, &ix->qnorm, &ix->part_s,
                       &ix->part_i, &ix->flag_list, &ix->out_ids, &ix->out_dist, &ix->gather_ids,
-                      &ix->gather_dist, &ix->merge_tmp_ids, &ix->merge_tmp_dist})
+                      &ix->gather_dist, &ix->merge_tmp_ids, &ix->merge_tmp_dist, &ix->thr, &ix->fb_s,
+                      &ix->fb_i})
         b->release();
     for (auto& ev : ix->ev)
         if (ev) cudaEventDestroy(ev);
@@ -581,10 +581,15 @@ int mflat_cu_index_search(mflat_cu_index_t* ix, const float* queries, int m, int
         sel.flag_count = ix->flag_count;
         sel.flag_list = ix->flag_list.as<int>();
         sel.err = ix->err;
+        const size_t fb = static_cast<size_t>(m) * kFbChunks * k_out;
+        CU_TRY(ix->fb_s.ensure(fb * sizeof(double)), "fallback scratch");
+        CU_TRY(ix->fb_i.ensure(fb * sizeof(int32_t)), "fallback scratch");
+        sel.fb_s = ix->fb_s.as<double>();
+        sel.fb_i = ix->fb_i.as<int32_t>();
         CU_TRY(launch_select_exact(kp, sel, st), "select launch");
         ++launches;
         CU_TRY(launch_fallback_exact(sel, ix->num_sms, st), "fallback launch");
-        ++launches;
+        launches += 2;
         cudaMemcpyAsync(&ix->host_words[1], ix->flag_count, sizeof(int), cudaMemcpyDeviceToHost, st);
         if (ix->timing) cudaEventRecord(ix->ev[3], st);
     }

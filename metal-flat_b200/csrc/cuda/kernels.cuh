@@ -32,6 +32,7 @@ constexpr int kBN = 256;          // database rows per tile (UMMA N)
 constexpr int kBK = 32;           // fp32 elements per k-block (128 bytes)
 constexpr int kMaxDPadResident = 128;   // A (queries) kept resident in smem up to this
 constexpr int kMaxChunks = 128;   // db chunks per query (select kernel fan-in)
+constexpr int kFbChunks = 64;     // database chunks of the exact fallback scan
 
 enum Metric : int { kL2 = 0, kIP = 1, kCosine = 2 };
 
@@ -49,12 +50,16 @@ struct ScreenParams {
     float* part_score;     // [n_chunks][m_pad][KP]
     int32_t* part_id;
     int* err;              // device error word (0 = ok)
+    // Per query row: key (score_key) of a floor under which no row can enter
+    // that query's global top-KP; raised by every finished work unit.
+    uint32_t* thr;
     // SIMT path only
     const float* q_hi; const float* q_lo;
     const float* db_hi; const float* db_lo;
 };
 
 struct SelectParams {
+    double* fb_s; int32_t* fb_i;          // exact fallback scratch [m][kFbChunks][k_out]
     int m, m_pad, dim, d_pad, k_out, n_chunks, metric;
     int64_t n;
     const float* part_score; const int32_t* part_id;

@@ -177,6 +177,36 @@ __device__ __forceinline__ void tmem_wait_ld() {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// Wait for outstanding tcgen05.ld and tie the destination registers to the
+// wait: the asm of tcgen05.ld declares its outputs as if they were ready at
+// once, so without this the compiler could schedule a use above the wait.
+__device__ __forceinline__ void tmem_wait_ld_regs(uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.wait::ld.sync.aligned;"
+        : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]),
+          "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]),
+          "+r"(r[13]), "+r"(r[14]), "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]),
+          "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]), "+r"(r[24]),
+          "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]),
+          "+r"(r[31])
+        :
+        : "memory");
+}
+
+// Order-preserving map float -> uint32 (larger float -> larger key), so a
+// per-query score floor can be raised with atomicMax.  Key 0 means "none".
+__device__ __forceinline__ uint32_t score_key(float f) {
+    const uint32_t u = __float_as_uint(f);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+// Largest float strictly below the score encoded by `key` (-inf for none):
+// admitting s > floor_below(key) admits exactly s >= decoded score.
+__device__ __forceinline__ float floor_below(uint32_t key) {
+    if (key == 0u) return -__int_as_float(0x7f800000);
+    const uint32_t u = (key & 0x80000000u) ? (key & 0x7fffffffu) : ~key;
+    return nextafterf(__uint_as_float(u), -__int_as_float(0x7f800000));
+}
+
 // Shared-memory matrix descriptor for a K-major operand tile written by TMA
 // with 128-byte swizzle: rows of 128 bytes, 8-row swizzle atoms 1024 bytes
 // apart (SBO = 1024), leading-byte offset unused for swizzled K-major,

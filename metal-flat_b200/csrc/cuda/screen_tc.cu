@@ -77,6 +77,49 @@ __device__ inline SmemLayout carve(uint8_t* base, int kb, int stages) {
     return L;
 }
 
+// Eight float4 of the per-row score bias for 32 columns.  Every lane of the
+// warp reads the same addresses (an L1 broadcast).
+__device__ __forceinline__ void load_bias(float4 (&cb)[8], const float* src) {
+    const float4* s4 = reinterpret_cast<const float4*>(src);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) cb[q] = __ldg(s4 + q);
+}
+
+// Scores of one 32-column chunk: s = alpha * dot + bias.  Hot path: 32 FFMA
+// and a 31-FMNMX max tree, one compare.  Only when some score beats the gate
+// (the list's worst entry or the published floor) are the scores spilled to
+// a small local array and inserted one by one, in ascending id order.
+template <int KP>
+__device__ __forceinline__ void scan_chunk(const uint32_t (&r)[32], const float4 (&cb)[8],
+                                           float alpha, float floor_adj, TopList<KP>& L, int id0) {
+    float sc[32];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+        sc[4 * q + 0] = fmaf(alpha, __uint_as_float(r[4 * q + 0]), cb[q].x);
+        sc[4 * q + 1] = fmaf(alpha, __uint_as_float(r[4 * q + 1]), cb[q].y);
+        sc[4 * q + 2] = fmaf(alpha, __uint_as_float(r[4 * q + 2]), cb[q].z);
+        sc[4 * q + 3] = fmaf(alpha, __uint_as_float(r[4 * q + 3]), cb[q].w);
+    }
+    float m16[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) m16[i] = fmaxf(sc[2 * i], sc[2 * i + 1]);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) m16[i] = fmaxf(m16[2 * i], m16[2 * i + 1]);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) m16[i] = fmaxf(m16[2 * i], m16[2 * i + 1]);
+    const float mx = fmaxf(fmaxf(m16[0], m16[1]), fmaxf(m16[2], m16[3]));
+    if (mx > fmaxf(L.worst(), floor_adj)) {
+        float tmp[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) tmp[j] = sc[j];
+#pragma unroll 1
+        for (int j = 0; j < 32; ++j) {
+            const float v = tmp[j];
+            if (v > fmaxf(L.worst(), floor_adj)) L.insert(v, id0 + j);
+        }
+    }
+}
+
 template <int KP>
 __global__ void __launch_bounds__(kThreads, 1)
 screen_tf32x3_kernel(const __grid_constant__ CUtensorMap tm_a_hi,
@@ -246,48 +289,47 @@ screen_tf32x3_kernel(const __grid_constant__ CUtensorMap tm_a_hi,
             const int ch = u / p.n_qtiles;
             const int t0 = ch * p.tiles_per_chunk;
             const int t1 = min(t0 + p.tiles_per_chunk, p.n_tiles);
+            const int row = qt * kBM + row_in_tile;
+            const bool live = row < p.m;
             TopList<KP> L;
             L.init();
             for (int t = t0; t < t1; ++t, ++tcount) {
                 const uint32_t b = tcount & 1u;
                 const uint32_t ph = (tcount >> 1) & 1u;
                 if (!mbar_wait(&S.acc_full[b], ph, abort_flag)) { ok = false; break; }
+                // floor published by finished units of the same query (monotone)
+                const float floor_adj =
+                    live ? floor_below(__ldcg(p.thr + row)) : __int_as_float(0x7f800000);
+                const float* cb_tile = p.colbias + static_cast<int64_t>(t) * kBN;
+                const uint32_t taddr = lane_addr + b * kBN;
+                const int id_tile = t * kBN;
+                uint32_t ra[32], rb[32];
+                float4 ca[8], cbv[8];
                 __syncwarp();
                 tc_fence_after();
-                const float* cb_tile = p.colbias + static_cast<int64_t>(t) * kBN;
+                tmem_ld_32x32b_x32(taddr, ra);
+                load_bias(ca, cb_tile);
 #pragma unroll 1
-                for (int c = 0; c < kBN / 32; ++c) {
-                    uint32_t r[32];
-                    __syncwarp();   // tcgen05.ld is .sync.aligned
-                    tmem_ld_32x32b_x32(lane_addr + b * kBN + c * 32, r);
-                    tmem_wait_ld();
-                    const float4* cb4 = reinterpret_cast<const float4*>(cb_tile + c * 32);
-                    float sc[32];
-                    uint32_t mask = 0;
-                    const float worst = L.worst();
-#pragma unroll
-                    for (int q4 = 0; q4 < 8; ++q4) {
-                        const float4 cb = __ldg(cb4 + q4);
-                        sc[q4 * 4 + 0] = fmaf(p.alpha, __uint_as_float(r[q4 * 4 + 0]), cb.x);
-                        sc[q4 * 4 + 1] = fmaf(p.alpha, __uint_as_float(r[q4 * 4 + 1]), cb.y);
-                        sc[q4 * 4 + 2] = fmaf(p.alpha, __uint_as_float(r[q4 * 4 + 2]), cb.z);
-                        sc[q4 * 4 + 3] = fmaf(p.alpha, __uint_as_float(r[q4 * 4 + 3]), cb.w);
+                for (int c = 0; c < kBN / 32; c += 2) {
+                    tmem_wait_ld_regs(ra);
+                    __syncwarp();
+                    tmem_ld_32x32b_x32(taddr + (c + 1) * 32, rb);
+                    load_bias(cbv, cb_tile + (c + 1) * 32);
+                    scan_chunk<KP>(ra, ca, p.alpha, floor_adj, L, id_tile + c * 32);
+                    tmem_wait_ld_regs(rb);
+                    if (c + 2 < kBN / 32) {
+                        __syncwarp();
+                        tmem_ld_32x32b_x32(taddr + (c + 2) * 32, ra);
+                        load_bias(ca, cb_tile + (c + 2) * 32);
                     }
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) mask |= (sc[j] > worst ? 1u : 0u) << j;
-                    if (mask) {
-                        const int id0 = t * kBN + c * 32;
-#pragma unroll
-                        for (int j = 0; j < 32; ++j)
-                            if (((mask >> j) & 1u) && sc[j] > L.worst()) L.insert(sc[j], id0 + j);
-                    }
+                    scan_chunk<KP>(rb, cbv, p.alpha, floor_adj, L, id_tile + (c + 1) * 32);
                 }
+                __syncwarp();
                 tc_fence_before();
                 mbar_arrive(&S.acc_empty[b]);
             }
             if (!ok) break;
-            const int row = qt * kBM + row_in_tile;
-            if (row < p.m) {
+            if (live) {
                 const int64_t o = (static_cast<int64_t>(ch) * p.m_pad + row) * KP;
                 float4* ps = reinterpret_cast<float4*>(p.part_score + o);
                 int4* pi = reinterpret_cast<int4*>(p.part_id + o);
@@ -296,6 +338,9 @@ screen_tf32x3_kernel(const __grid_constant__ CUtensorMap tm_a_hi,
                     ps[i] = make_float4(L.s[4 * i], L.s[4 * i + 1], L.s[4 * i + 2], L.s[4 * i + 3]);
                     pi[i] = make_int4(L.id[4 * i], L.id[4 * i + 1], L.id[4 * i + 2], L.id[4 * i + 3]);
                 }
+                // A full list's KP-th score is a lower bound of the query's
+                // global KP-th best: no row below it can matter any more.
+                if (L.id[KP - 1] >= 0) atomicMax(p.thr + row, score_key(L.s[KP - 1]));
             }
         }
     }

@@ -166,24 +166,32 @@ __global__ void __launch_bounds__(128) select_exact_kernel(const SelectParams p)
     }
 }
 
-// Exact fp64 full scan for the queries the proof rejected.  Each thread keeps
-// its own best-k list (rows visited in ascending order, strict '>'), then the
-// block merges the 256 lists by a k-round tournament.
+// Exact fp64 full scan for the queries the proof rejected, in two stages.
+// Stage 1: every block takes (flagged query, database chunk) pairs, chunk-major
+// so that concurrently running blocks read the same rows; each thread keeps a
+// best-k list of its rows (visited in ascending order, strict '>'), the block
+// merges its 256 lists by a k-round tournament and stores the chunk's best k.
+// Stage 2: one block per flagged query merges the kFbChunks chunk lists.
 constexpr int kFbThreads = 256;
 constexpr int kFbMaxK = 32;
 
-__global__ void __launch_bounds__(kFbThreads) fallback_exact_kernel(const SelectParams p) {
+__global__ void __launch_bounds__(kFbThreads) fallback_scan_kernel(const SelectParams p) {
     __shared__ Cand red[33];
     const int nflag = *p.flag_count;
-    for (int f = blockIdx.x; f < nflag; f += gridDim.x) {
+    const int k = p.k_out;
+    const int64_t per = (p.n + kFbChunks - 1) / kFbChunks;
+    for (int pair = blockIdx.x; pair < nflag * kFbChunks; pair += gridDim.x) {
+        const int c = pair / nflag;
+        const int f = pair % nflag;
         const int qi = p.flag_list[f];
         const float* qh = p.q_hi + static_cast<int64_t>(qi) * p.d_pad;
         const float* ql = p.q_lo + static_cast<int64_t>(qi) * p.d_pad;
+        const int64_t r0 = c * per;
+        const int64_t r1 = min(p.n, r0 + per);
         double bs[kFbMaxK];
         int bi[kFbMaxK];
-        const int k = p.k_out;
         for (int i = 0; i < k; ++i) { bs[i] = -DBL_MAX; bi[i] = -1; }   // sorted desc
-        for (int64_t j = threadIdx.x; j < p.n; j += blockDim.x) {
+        for (int64_t j = r0 + threadIdx.x; j < r1; j += blockDim.x) {
             const double s = exact_score(p.metric, qh, ql, p.db_hi + j * p.d_pad,
                                          p.db_lo + j * p.d_pad, p.dim);
             if (bi[k - 1] < 0 || s > bs[k - 1]) {
@@ -198,11 +206,34 @@ __global__ void __launch_bounds__(kFbThreads) fallback_exact_kernel(const Select
             }
         }
         int head = 0;
+        const int64_t ob = (static_cast<int64_t>(f) * kFbChunks + c) * k;
         for (int r = 0; r < k; ++r) {
-            Cand c{-DBL_MAX, -1, static_cast<int>(threadIdx.x)};
-            if (head < k && bi[head] >= 0) { c.s = bs[head]; c.id = bi[head]; }
-            const Cand w = block_best(c, red);
+            Cand cd{-DBL_MAX, -1, static_cast<int>(threadIdx.x)};
+            if (head < k && bi[head] >= 0) { cd.s = bs[head]; cd.id = bi[head]; }
+            const Cand w = block_best(cd, red);
             if (threadIdx.x == 0) {
+                p.fb_s[ob + r] = w.s;
+                p.fb_i[ob + r] = w.id;
+            }
+            if (w.id >= 0 && w.owner == static_cast<int>(threadIdx.x)) ++head;
+        }
+    }
+}
+
+__global__ void __launch_bounds__(128) fallback_merge_kernel(const SelectParams p) {
+    __shared__ Cand red[33];
+    const int nflag = *p.flag_count;
+    const int k = p.k_out;
+    const int t = threadIdx.x;
+    for (int f = blockIdx.x; f < nflag; f += gridDim.x) {
+        const int qi = p.flag_list[f];
+        int head = 0;
+        const int64_t ob = (static_cast<int64_t>(f) * kFbChunks + t) * k;
+        for (int r = 0; r < k; ++r) {
+            Cand cd{-DBL_MAX, -1, t};
+            if (t < kFbChunks && head < k) { cd.s = p.fb_s[ob + head]; cd.id = p.fb_i[ob + head]; }
+            const Cand w = block_best(cd, red);
+            if (t == 0) {
                 const int64_t o = static_cast<int64_t>(qi) * k + r;
                 if (w.id >= 0) {
                     p.out_ids[o] = static_cast<int32_t>(w.id + p.id_base);
@@ -213,7 +244,7 @@ __global__ void __launch_bounds__(kFbThreads) fallback_exact_kernel(const Select
                                                     : -__int_as_float(0x7f800000);
                 }
             }
-            if (w.id >= 0 && w.owner == static_cast<int>(threadIdx.x)) ++head;
+            if (w.id >= 0 && w.owner == t) ++head;
         }
     }
 }
@@ -361,7 +392,10 @@ cudaError_t launch_kmeans_select(const SelectParams& p, int32_t* out, int grid_f
 
 cudaError_t launch_fallback_exact(const SelectParams& p, int grid, cudaStream_t stream) {
     if (p.k_out > kFbMaxK || p.k_out < 1) return cudaErrorInvalidValue;
-    fallback_exact_kernel<<<grid, kFbThreads, 0, stream>>>(p);
+    fallback_scan_kernel<<<grid * 2, kFbThreads, 0, stream>>>(p);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    fallback_merge_kernel<<<grid, 128, 0, stream>>>(p);
     return cudaGetLastError();
 }
 
