@@ -123,6 +123,27 @@ MFLAT_API mflat_status_t mflat_flat_add_device(mflat_flat_index_t*, const float*
 MFLAT_API mflat_status_t mflat_flat_search_device(mflat_flat_index_t*, const float* d_queries,
         int m, int k, int32_t* d_out_ids, float* d_out_distances, int* out_k_used, void* stream);
 
+/* Allocation-free search.  No counterpart in the reference: some callers cannot
+ * call cudaMalloc -- a serving process whose device memory is already reserved
+ * by a framework's caching allocator, or a latency-critical loop that cannot
+ * afford the device-wide synchronisation of cudaMalloc / cudaFree.  Same
+ * arguments and results as mflat_flat_search_device, but every per-call
+ * scratch buffer lives in one fixed array inside the library
+ * (MFLAT_NOALLOC_SCRATCH_BYTES per GPU, held until the process exits).
+ * Limits: m <= MFLAT_NOALLOC_MAX_QUERIES, dim <= MFLAT_NOALLOC_MAX_DIM,
+ * k <= MFLAT_NOALLOC_MAX_K, FP32 storage, unsharded; larger sizes return
+ * MFLAT_ERR_BAD_ARG (no clamping) and log the limit.  All calls on one GPU
+ * share the array: calls that overlap on the GPU (other streams, other
+ * indexes) race and must be serialised by the caller.  The first call on a
+ * device looks up the array's device address; make it before any stream
+ * capture. */
+#define MFLAT_NOALLOC_MAX_QUERIES 128
+#define MFLAT_NOALLOC_MAX_DIM 128
+#define MFLAT_NOALLOC_MAX_K 21
+#define MFLAT_NOALLOC_SCRATCH_BYTES (4u << 20)
+MFLAT_API mflat_status_t mflat_flat_search_noalloc(mflat_flat_index_t*, const float* d_queries,
+        int m, int k, int32_t* d_out_ids, float* d_out_distances, int* out_k_used, void* stream);
+
 /* Device-side timing of the most recent search (milliseconds, CUDA events
  * on the launching stream) once enabled with mflat_flat_set_timing(h, 1). */
 typedef struct {

@@ -271,6 +271,29 @@ void plan_chunks(int n_qtiles, int n_tiles, int num_sms, int max_chunks, int& n_
 
 }  // namespace
 
+// Entry points for other translation units of this library (noalloc.cu).
+bool encode_map_f32(CUtensorMap* map, const float* base, uint64_t inner, uint64_t rows,
+                    uint32_t box_rows) {
+    return make_map_f32(map, base, inner, rows, box_rows);
+}
+
+cudaError_t launch_prep_queries(const float* src, int m, int m_pad, int dim, int d_pad, int metric,
+                                float* q_hi, float* q_lo, float* qnorm, cudaStream_t st) {
+    prep_queries_kernel<<<blocks_for(m_pad, 128), 128, 0, st>>>(src, m, m_pad, dim, d_pad, metric,
+                                                                q_hi, q_lo, qnorm);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_fill_empty(int32_t* ids, float* dist, int64_t n, float v, cudaStream_t st) {
+    fill_empty_kernel<<<blocks_for(n, 256), 256, 0, st>>>(ids, dist, n, v);
+    return cudaGetLastError();
+}
+
+void plan_screen_chunks(int n_qtiles, int n_tiles, int num_sms, int max_chunks, int& n_chunks,
+                        int& tiles_per_chunk) {
+    plan_chunks(n_qtiles, n_tiles, num_sms, max_chunks, n_chunks, tiles_per_chunk);
+}
+
 int check_device_error(mflat_cu_index* ix) {
     if (ix->host_words[0] != 0) {
         const int code = ix->host_words[0];

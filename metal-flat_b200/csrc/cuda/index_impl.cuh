@@ -95,5 +95,12 @@ int shard_merge(mflat_cu_index* ix, int m, int k_out, int32_t* ids, float* dist,
 // Synchronise `st`; with a communicator attached, watch it for peer failure.
 int wait_stream_checked(mflat_cu_index* ix, cudaStream_t st);
 const char* last_error_message();
+bool encode_map_f32(CUtensorMap* map, const float* base, uint64_t inner, uint64_t rows,
+                    uint32_t box_rows);
+cudaError_t launch_prep_queries(const float* src, int m, int m_pad, int dim, int d_pad, int metric,
+                                float* q_hi, float* q_lo, float* qnorm, cudaStream_t st);
+cudaError_t launch_fill_empty(int32_t* ids, float* dist, int64_t n, float v, cudaStream_t st);
+void plan_screen_chunks(int n_qtiles, int n_tiles, int num_sms, int max_chunks, int& n_chunks,
+                        int& tiles_per_chunk);
 
 }  // namespace mflat_cu

@@ -47,6 +47,12 @@ MFLAT_CU_API int mflat_cu_index_reset(mflat_cu_index_t* ix);
 MFLAT_CU_API int mflat_cu_index_search(mflat_cu_index_t* ix, const float* queries, int m,
                                        int k_out, int32_t* out_ids, float* out_dist,
                                        int on_device, void* stream);
+/* Same search with device pointers, but every per-call scratch buffer comes
+ * from one fixed per-device array inside the library (no device allocation);
+ * m <= 128, dim <= 128, k <= 21, fp32 storage.  See noalloc.cu. */
+MFLAT_CU_API int mflat_cu_index_search_noalloc(mflat_cu_index_t* ix, const float* d_queries, int m,
+                                               int k_out, int32_t* d_ids, float* d_dist,
+                                               void* stream);
 MFLAT_CU_API int mflat_cu_index_set_timing(mflat_cu_index_t* ix, int enable);
 MFLAT_CU_API int mflat_cu_index_last_timing(const mflat_cu_index_t* ix, mflat_cu_timing_t* out);
 

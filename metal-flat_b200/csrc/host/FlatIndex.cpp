@@ -129,6 +129,14 @@ int FlatIndex::searchDevice(const float* d_queries, int m, int k, int32_t* d_ids
     return k;
 }
 
+int FlatIndex::searchDeviceNoAlloc(const float* d_queries, int m, int k, int32_t* d_ids,
+                                   float* d_dist, void* stream) {
+    if (m <= 0 || mImpl->dim <= 0) return 0;
+    raise_status(mflat_cu_index_search_noalloc(mImpl->need(), d_queries, m, k, d_ids, d_dist, stream),
+                 "search (no-alloc)");
+    return k;
+}
+
 void FlatIndex::setTiming(bool enable) {
     raise_status(mflat_cu_index_set_timing(mImpl->need(), enable ? 1 : 0), "timing");
 }

@@ -215,6 +215,20 @@ MFLAT_API mflat_status_t mflat_flat_search_device(mflat_flat_index_t* h, const f
     });
 }
 
+MFLAT_API mflat_status_t mflat_flat_search_noalloc(mflat_flat_index_t* h, const float* q, int m,
+                                                   int k, int32_t* oi, float* od, int* ok,
+                                                   void* stream) {
+    if (!h || !q) return MFLAT_ERR_NULL_ARG;
+    if (m < 0 || k < 1) return MFLAT_ERR_BAD_ARG;
+    if (m > 0 && (!oi || !od)) return MFLAT_ERR_NULL_ARG;
+    return guarded([&] {
+        std::lock_guard<std::mutex> lk(h->mu);
+        const int used = h->idx.searchDeviceNoAlloc(q, m, k, oi, od, stream);
+        if (ok) *ok = used;
+        return MFLAT_OK;
+    });
+}
+
 MFLAT_API mflat_status_t mflat_flat_set_timing(mflat_flat_index_t* h, int enable) {
     if (!h) return MFLAT_ERR_NULL_ARG;
     return guarded([&] {

@@ -71,6 +71,12 @@ public:
     // (outputs are written at that row stride).
     int  searchDevice(const float* d_queries, int m, int k, int32_t* d_ids, float* d_dist,
                       void* stream);
+    // As searchDevice, but allocates no device memory: the scratch is a fixed
+    // array inside the library (m <= 128, dim <= 128, k <= 21; no clamping --
+    // larger sizes throw std::invalid_argument).  For callers that cannot call
+    // cudaMalloc; calls that overlap on one GPU race on that array.
+    int  searchDeviceNoAlloc(const float* d_queries, int m, int k, int32_t* d_ids, float* d_dist,
+                             void* stream);
     void setTiming(bool enable);
     SearchTiming lastTiming() const;
     // Row sharding: this index holds global rows [id_base, id_base + size());

@@ -30,7 +30,7 @@ EXPORTS = [
     "mflat_flat_create_ex", "mflat_flat_storage", "mflat_flat_device",
     "mflat_flat_add_device", "mflat_flat_search_device", "mflat_flat_set_timing",
     "mflat_flat_last_timing", "mflat_kmeans_assign", "mflat_kmeans_assign_device",
-    "mflat_comm_unique_id", "mflat_flat_set_shard",
+    "mflat_comm_unique_id", "mflat_flat_set_shard", "mflat_flat_search_noalloc",
 ]
 
 
@@ -82,6 +82,7 @@ def lib() -> ctypes.CDLL:
         "mflat_flat_reset": ([vp], ci),
         "mflat_flat_search": ([vp, f32p, ci, ci, i32p, f32p, ctypes.POINTER(ci)], ci),
         "mflat_flat_search_device": ([vp, vp, ci, ci, vp, vp, ctypes.POINTER(ci), vp], ci),
+        "mflat_flat_search_noalloc": ([vp, vp, ci, ci, vp, vp, ctypes.POINTER(ci), vp], ci),
         "mflat_flat_set_timing": ([vp, ci], ci),
         "mflat_flat_last_timing": ([vp, ctypes.POINTER(Timing)], ci),
         "mflat_kmeans_assign": ([f32p, ci, f32p, ci, ci, i32p, ci], ci),
@@ -204,6 +205,17 @@ class FlatIndex:
                                                   ctypes.c_void_p(ids_ptr),
                                                   ctypes.c_void_p(dist_ptr), ctypes.byref(used),
                                                   ctypes.c_void_p(stream)), "search_device")
+        return used.value
+
+    def search_noalloc(self, q_ptr: int, m: int, k: int, ids_ptr: int, dist_ptr: int,
+                       stream: int = 0) -> int:
+        """Device-pointer search that allocates no device memory (m <= 128,
+        dim <= 128, k <= 21); see mflat_flat_search_noalloc in include/mflat.h."""
+        used = ctypes.c_int(0)
+        _check(self._lib.mflat_flat_search_noalloc(self._h, ctypes.c_void_p(q_ptr), m, k,
+                                                   ctypes.c_void_p(ids_ptr),
+                                                   ctypes.c_void_p(dist_ptr), ctypes.byref(used),
+                                                   ctypes.c_void_p(stream)), "search_noalloc")
         return used.value
 
     def set_timing(self, on: bool = True) -> None:
