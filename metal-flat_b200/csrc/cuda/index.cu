@@ -354,6 +354,8 @@ int run_screen(mflat_cu_index* ix, const float* queries, int m, int kp, int on_d
     sp.part_id = ix->part_i.as<int32_t>();
     sp.err = ix->err;
     sp.thr = ix->thr.as<uint32_t>();
+    sp.tile_stride = 1;
+    sp.use_floor = 1;
     sp.q_hi = ix->q_hi.as<float>();
     sp.q_lo = ix->q_lo.as<float>();
     sp.db_hi = ix->db_hi;
@@ -387,6 +389,191 @@ int run_screen(mflat_cu_index* ix, const float* queries, int m, int kp, int on_d
     out.part_s = sp.part_score;
     out.part_i = sp.part_id;
     out.launches = 2;
+    return ST_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Large k (22..1024) on fp32 storage: strided-sample floor pre-pass (list
+// mode), buffer-mode screen over every row, radix select + exact window
+// re-rank (select_large.cu).  Queries are processed in batches sized so the
+// candidate buffers stay within a fixed budget.
+namespace {
+
+constexpr int64_t kAllRowsBuffered = 32768;        // below this, no pre-pass
+constexpr size_t kBufferBudget = size_t(6) << 30;  // bytes of candidate buffers
+
+struct LargePlan {
+    bool prepass = false;
+    int stride = 1, lists = 0, sample_tiles = 0;
+    uint32_t cap = 0;
+    int batch = 0;
+};
+
+LargePlan plan_large(int64_t n, int k, int m, int kp1) {
+    LargePlan P;
+    const int n_tiles = static_cast<int>((n + kBN - 1) / kBN);
+    if (n <= kAllRowsBuffered) {
+        P.cap = static_cast<uint32_t>((n + 255) / 256 * 256);
+    } else {
+        P.prepass = true;
+        P.lists = std::max(1, (2 * k + kp1 - 1) / kp1);      // lists * kp1 >= 2k
+        P.stride = 16;
+        while (P.stride > 1 && (n_tiles + P.stride - 1) / P.stride < 2 * P.lists) P.stride /= 2;
+        P.sample_tiles = (n_tiles + P.stride - 1) / P.stride;
+        if (P.sample_tiles < P.lists) {                      // too small to sample: buffer all
+            P.prepass = false;
+            P.cap = static_cast<uint32_t>((n + 255) / 256 * 256);
+        } else {
+            const int64_t expect = static_cast<int64_t>(P.lists) * kp1 * P.stride;
+            int64_t cap = std::max<int64_t>(4 * expect, 4096);
+            cap = std::min<int64_t>((cap + 255) / 256 * 256, (n + 255) / 256 * 256);
+            P.cap = static_cast<uint32_t>(cap);
+        }
+    }
+    const size_t per_q = static_cast<size_t>(P.cap) * 8 + 64;
+    P.batch = static_cast<int>(std::max<size_t>(kBM, std::min<size_t>(m, kBufferBudget / per_q)));
+    P.batch = std::min(P.batch, m);
+    return P;
+}
+
+cudaError_t launch_pass(mflat_cu_index* ix, const ScreenParams& sp, int kp, cudaStream_t st) {
+    if (ix->force_simt || sp.d_pad > kMaxDPadResident) return launch_screen_simt(kp, sp, st);
+    CUtensorMap ta_hi, ta_lo, tb_hi, tb_lo;
+    if (!make_map_f32(&ta_hi, sp.q_hi, sp.d_pad, sp.m_pad, kBM) ||
+        !make_map_f32(&ta_lo, sp.q_lo, sp.d_pad, sp.m_pad, kBM) ||
+        !make_map_f32(&tb_hi, ix->db_hi, sp.d_pad, ix->n, kBN) ||
+        !make_map_f32(&tb_lo, ix->db_lo, sp.d_pad, ix->n, kBN))
+        return cudaErrorInvalidValue;
+    const int64_t units = static_cast<int64_t>(sp.n_qtiles) * sp.n_chunks;
+    const int grid = static_cast<int>(std::min<int64_t>(units, ix->num_sms));
+    return launch_screen_tf32x3(kp, ta_hi, ta_lo, tb_hi, tb_lo, sp, grid, st);
+}
+
+}  // namespace
+
+int search_large(mflat_cu_index* ix, const float* queries, int m, int k_out, int32_t* d_ids,
+                 float* d_dist, int on_device, cudaStream_t st) {
+    constexpr int kKP1 = 32;
+    const LargePlan P = plan_large(ix->n, k_out, m, kKP1);
+    const int d_pad = ix->d_pad;
+    const int n_tiles = static_cast<int>((ix->n + kBN - 1) / kBN);
+    const float* qsrc = queries;
+    if (!on_device) {
+        CU_TRY(ix->q_in.ensure(static_cast<size_t>(m) * ix->dim * sizeof(float)), "query buffer");
+        CU_TRY(cudaMemcpyAsync(ix->q_in.p, queries, static_cast<size_t>(m) * ix->dim * sizeof(float),
+                               cudaMemcpyHostToDevice, st),
+               "query upload");
+        qsrc = ix->q_in.as<float>();
+    }
+    const int bm_pad = (P.batch + kBM - 1) / kBM * kBM;
+    CU_TRY(ix->q_hi.ensure(static_cast<size_t>(bm_pad) * d_pad * sizeof(float)), "query split");
+    CU_TRY(ix->q_lo.ensure(static_cast<size_t>(bm_pad) * d_pad * sizeof(float)), "query split");
+    CU_TRY(ix->qnorm.ensure(static_cast<size_t>(bm_pad) * sizeof(float)), "query norms");
+    CU_TRY(ix->thr.ensure(static_cast<size_t>(bm_pad) * sizeof(uint32_t)), "floors");
+    CU_TRY(ix->buf_cnt.ensure(static_cast<size_t>(bm_pad) * sizeof(uint32_t)), "buffer counts");
+    CU_TRY(ix->buf_s.ensure(static_cast<size_t>(bm_pad) * P.cap * sizeof(float)), "candidate buffer");
+    CU_TRY(ix->buf_i.ensure(static_cast<size_t>(bm_pad) * P.cap * sizeof(int32_t)), "candidate buffer");
+    CU_TRY(ix->flag_list.ensure(static_cast<size_t>(bm_pad) * sizeof(int)), "flag list");
+    CU_TRY(ix->lk_words.ensure(2 * sizeof(int)), "status words");
+    if (P.prepass) {
+        const size_t parts = static_cast<size_t>(P.lists) * bm_pad * kKP1;
+        CU_TRY(ix->part_s.ensure(parts * sizeof(float)), "pre-pass lists");
+        CU_TRY(ix->part_i.ensure(parts * sizeof(int32_t)), "pre-pass lists");
+    }
+    int* words = ix->lk_words.as<int>();      // [0] overflow, [1] proof failures
+    CU_TRY(cudaMemsetAsync(words, 0, 2 * sizeof(int), st), "status words");
+    if (ix->timing) cudaEventRecord(ix->ev[0], st);
+
+    for (int b0 = 0; b0 < m; b0 += P.batch) {
+        const int mb = std::min(P.batch, m - b0);
+        const int mb_pad = (mb + kBM - 1) / kBM * kBM;
+        CU_TRY(launch_prep_queries(qsrc + static_cast<int64_t>(b0) * ix->dim, mb, mb_pad, ix->dim,
+                                   d_pad, ix->metric, ix->q_hi.as<float>(), ix->q_lo.as<float>(),
+                                   ix->qnorm.as<float>(), st),
+               "query prep launch");
+        CU_TRY(cudaMemsetAsync(ix->thr.p, 0, static_cast<size_t>(mb_pad) * sizeof(uint32_t), st), "floors");
+        CU_TRY(cudaMemsetAsync(ix->buf_cnt.p, 0, static_cast<size_t>(mb_pad) * sizeof(uint32_t), st), "counts");
+        CU_TRY(cudaMemsetAsync(ix->flag_count, 0, sizeof(int), st), "flag count");
+
+        ScreenParams sp{};
+        sp.m = mb;
+        sp.m_pad = mb_pad;
+        sp.d_pad = d_pad;
+        sp.n = ix->n;
+        sp.n_qtiles = mb_pad / kBM;
+        sp.alpha = ix->metric == kL2 ? 2.0f : 1.0f;
+        sp.colbias = ix->colbias;
+        sp.err = ix->err;
+        sp.thr = ix->thr.as<uint32_t>();
+        sp.q_hi = ix->q_hi.as<float>();
+        sp.q_lo = ix->q_lo.as<float>();
+        sp.db_hi = ix->db_hi;
+        sp.db_lo = ix->db_lo;
+        if (P.prepass) {
+            ScreenParams pp = sp;
+            pp.use_floor = 0;
+            pp.tile_stride = P.stride;
+            pp.n_tiles = P.sample_tiles;
+            pp.tiles_per_chunk = (P.sample_tiles + P.lists - 1) / P.lists;
+            pp.n_chunks = (P.sample_tiles + pp.tiles_per_chunk - 1) / pp.tiles_per_chunk;
+            pp.part_score = ix->part_s.as<float>();
+            pp.part_id = ix->part_i.as<int32_t>();
+            CU_TRY(launch_pass(ix, pp, kKP1, st), "floor pre-pass launch");
+            CU_TRY(launch_prepass_floor(pp.part_score, pp.part_id, pp.n_chunks, mb, mb_pad, kKP1,
+                                        sp.thr, st),
+                   "floor launch");
+        }
+        sp.use_floor = 1;
+        sp.tile_stride = 1;
+        sp.n_tiles = n_tiles;
+        int n_chunks = 1, tpc = n_tiles;
+        plan_chunks(sp.n_qtiles, n_tiles, ix->num_sms, kMaxChunks, n_chunks, tpc);
+        sp.n_chunks = n_chunks;
+        sp.tiles_per_chunk = tpc;
+        sp.buf_cnt = ix->buf_cnt.as<uint32_t>();
+        sp.buf_s = ix->buf_s.as<float>();
+        sp.buf_i = ix->buf_i.as<int32_t>();
+        sp.cap = P.cap;
+        if (ix->timing && b0 == 0) cudaEventRecord(ix->ev[1], st);
+        CU_TRY(launch_pass(ix, sp, 0, st), "buffer screen launch");
+        if (ix->timing && b0 == 0) cudaEventRecord(ix->ev[2], st);
+
+        LargeSelectParams ls{};
+        ls.m = mb;
+        ls.m_pad = mb_pad;
+        ls.dim = ix->dim;
+        ls.d_pad = d_pad;
+        ls.k_out = k_out;
+        ls.metric = ix->metric == kL2 ? kL2 : kIP;
+        ls.cnt = sp.buf_cnt;
+        ls.buf_s = sp.buf_s;
+        ls.buf_i = sp.buf_i;
+        ls.cap = P.cap;
+        ls.thr = sp.thr;
+        ls.exact = 1;
+        ls.q_hi = sp.q_hi;
+        ls.q_lo = sp.q_lo;
+        ls.qnorm = ix->qnorm.as<float>();
+        ls.db_hi = ix->db_hi;
+        ls.db_lo = ix->db_lo;
+        ls.xmax_bits = ix->xmax_bits;
+        ls.gamma = static_cast<float>((3.0 * d_pad + 16.0) * std::ldexp(1.0, -21));
+        ls.id_base = ix->world > 1 ? ix->id_base : 0;
+        ls.out_ids = d_ids + static_cast<int64_t>(b0) * k_out;
+        ls.out_dist = d_dist + static_cast<int64_t>(b0) * k_out;
+        ls.flag_count = words + 1;
+        ls.flag_list = ix->flag_list.as<int>();
+        ls.overflow = words;
+        CU_TRY(launch_select_large(ls, st), "large select launch");
+    }
+    if (ix->timing) cudaEventRecord(ix->ev[3], st);
+    // Overflows and unproven queries are rare; surface them as errors.
+    CU_TRY(cudaMemcpyAsync(&ix->host_words[2], words, 2 * sizeof(int), cudaMemcpyDeviceToHost, st), "status");
+    CU_TRY(cudaStreamSynchronize(st), "large-k search");
+    if (ix->host_words[2] > 0) return fail(ST_INTERNAL, "candidate buffer overflow (too many rows tie with the k-th best)");
+    if (ix->host_words[3] > 0) return fail(ST_INTERNAL, "exactness could not be proven for some queries (near-ties)");
+    ix->last.screen_launches = 1;
+    ix->last.launches = (P.prepass ? 5 : 3) * ((m + P.batch - 1) / P.batch);
     return ST_OK;
 }
 
@@ -471,7 +658,7 @@ void mflat_cu_index_destroy(mflat_cu_index_t* ix) {
     for (DevBuf* b : {&ix->stage_in, &ix->q_in, &ix->q_hi, &ix->q_lo, &ix->qnorm, &ix->part_s,
                       &ix->part_i, &ix->flag_list, &ix->out_ids, &ix->out_dist, &ix->gather_ids,
                       &ix->gather_dist, &ix->merge_tmp_ids, &ix->merge_tmp_dist, &ix->thr, &ix->fb_s,
-                      &ix->fb_i})
+                      &ix->fb_i, &ix->buf_cnt, &ix->buf_s, &ix->buf_i, &ix->lk_words})
         b->release();
     for (auto& ev : ix->ev)
         if (ev) cudaEventDestroy(ev);
@@ -569,7 +756,26 @@ int mflat_cu_index_search(mflat_cu_index_t* ix, const float* queries, int m, int
         CU_TRY(cudaGetLastError(), "fill");
     } else {
         const int kp = kp_for(k_out);
-        if (kp == 0) return fail(ST_BAD_ARG, "k above the exact-path limit of this build");
+        if (kp == 0) {
+            const int rc = search_large(ix, queries, m, k_out, d_ids, d_dist, on_device, st);
+            if (rc != ST_OK) return rc;
+            if (ix->world > 1) {
+                const int rc2 = shard_merge(ix, m, k_out, d_ids, d_dist, st);
+                if (rc2 != ST_OK) return rc2;
+            }
+            if (!on_device) {
+                CU_TRY(cudaMemcpyAsync(out_ids, d_ids, mk * sizeof(int32_t), cudaMemcpyDeviceToHost, st), "download");
+                CU_TRY(cudaMemcpyAsync(out_dist, d_dist, mk * sizeof(float), cudaMemcpyDeviceToHost, st), "download");
+                const int rc3 = wait_stream_checked(ix, st);
+                if (rc3 != ST_OK) return rc3;
+            }
+            if (ix->timing) {
+                cudaEventElapsedTime(&ix->last.total_ms, ix->ev[0], ix->ev[3]);
+                cudaEventElapsedTime(&ix->last.screen_ms, ix->ev[1], ix->ev[2]);
+                cudaEventElapsedTime(&ix->last.select_ms, ix->ev[2], ix->ev[3]);
+            }
+            return check_device_error(ix);
+        }
         ScreenRun run;
         int rc = run_screen(ix, queries, m, kp, on_device, st, run);
         if (rc != ST_OK) return rc;

@@ -53,6 +53,15 @@ struct ScreenParams {
     // Per query row: key (score_key) of a floor under which no row can enter
     // that query's global top-KP; raised by every finished work unit.
     uint32_t* thr;
+    int use_floor;         // 0: ignore and never raise thr (floor pre-pass)
+    // Database tiles visited are t * tile_stride for t in [0, n_tiles): a
+    // stride > 1 screens an evenly spread sample (the floor pre-pass).
+    int tile_stride;
+    // Buffer mode (large k): per-query candidate buffers [m_pad][cap].
+    uint32_t* buf_cnt;
+    float* buf_s;
+    int32_t* buf_i;
+    uint32_t cap;
     // SIMT path only
     const float* q_hi; const float* q_lo;
     const float* db_hi; const float* db_lo;
@@ -71,6 +80,22 @@ struct SelectParams {
     int32_t* out_ids; float* out_dist;    // [m][k_out]
     int* flag_count; int* flag_list;      // queries needing the exact full scan
     int* err;
+};
+
+// Large-k selection over the candidate buffers (select_large.cu).
+struct LargeSelectParams {
+    int m, m_pad, dim, d_pad, k_out, metric;
+    const uint32_t* cnt; const float* buf_s; const int32_t* buf_i; uint32_t cap;
+    const uint32_t* thr;                  // floor keys used by the screen
+    int exact;                            // 1: fp64 re-rank of the proven window
+    const float* q_hi; const float* q_lo; const float* qnorm;
+    const float* db_hi; const float* db_lo;
+    const unsigned* xmax_bits; float gamma;
+    const float* qsq;                     // recall path: ||q||^2 for L2 distances
+    int64_t id_base;
+    int32_t* out_ids; float* out_dist;
+    int* flag_count; int* flag_list;      // proof failures (exact path)
+    int* overflow;                        // buffers that overflowed / too many ties
 };
 
 // ---------------------------------------------------------------------------
@@ -110,6 +135,7 @@ __device__ __forceinline__ bool cand_better(float sa, int ia, float sb, int ib) 
 
 // ------------------------------------------------------------- launchers
 // All launchers enqueue on `stream` and return the launch status.
+// kp = 0 selects buffer mode (append every score above the floor).
 cudaError_t launch_screen_tf32x3(int kp, const CUtensorMap& a_hi, const CUtensorMap& a_lo,
                                  const CUtensorMap& b_hi, const CUtensorMap& b_lo,
                                  const ScreenParams& p, int grid, cudaStream_t stream);
@@ -117,6 +143,9 @@ cudaError_t launch_screen_simt(int kp, const ScreenParams& p, cudaStream_t strea
 cudaError_t launch_select_exact(int kp, const SelectParams& p, cudaStream_t stream);
 cudaError_t launch_fallback_exact(const SelectParams& p, int grid, cudaStream_t stream);
 int screen_tf32x3_smem_bytes(int d_pad);
+cudaError_t launch_select_large(const LargeSelectParams& p, cudaStream_t stream);
+cudaError_t launch_prepass_floor(const float* part_s, const int32_t* part_i, int n_lists, int m,
+                                 int m_pad, int kp1, uint32_t* thr, cudaStream_t stream);
 cudaError_t launch_kmeans_select(const SelectParams& p, int32_t* out, int grid_fallback,
                                  cudaStream_t stream);
 

@@ -152,6 +152,8 @@ extern "C" int mflat_cu_index_search_noalloc(mflat_cu_index_t* ix, const float* 
     sp.part_id = part_i;
     sp.err = ix->err;
     sp.thr = thr;
+    sp.tile_stride = 1;
+    sp.use_floor = 1;
     CUtensorMap ta_hi, ta_lo, tb_hi, tb_lo;
     if (!encode_map_f32(&ta_hi, q_hi, d_pad, m_pad, kBM) ||
         !encode_map_f32(&ta_lo, q_lo, d_pad, m_pad, kBM) ||

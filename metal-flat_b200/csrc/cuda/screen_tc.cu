@@ -25,6 +25,7 @@
 //              ring stage.
 //   warp 5     TMEM allocator + MMA issuer (one thread), M=128 N=256 K=8,
 //              double-buffered accumulators (2 x 256 TMEM columns).
+#include "epilogue.cuh"
 #include "kernels.cuh"
 #include "ptx.cuh"
 
@@ -77,50 +78,7 @@ __device__ inline SmemLayout carve(uint8_t* base, int kb, int stages) {
     return L;
 }
 
-// Eight float4 of the per-row score bias for 32 columns.  Every lane of the
-// warp reads the same addresses (an L1 broadcast).
-__device__ __forceinline__ void load_bias(float4 (&cb)[8], const float* src) {
-    const float4* s4 = reinterpret_cast<const float4*>(src);
-#pragma unroll
-    for (int q = 0; q < 8; ++q) cb[q] = __ldg(s4 + q);
-}
-
-// Scores of one 32-column chunk: s = alpha * dot + bias.  Hot path: 32 FFMA
-// and a 31-FMNMX max tree, one compare.  Only when some score beats the gate
-// (the list's worst entry or the published floor) are the scores spilled to
-// a small local array and inserted one by one, in ascending id order.
-template <int KP>
-__device__ __forceinline__ void scan_chunk(const uint32_t (&r)[32], const float4 (&cb)[8],
-                                           float alpha, float floor_adj, TopList<KP>& L, int id0) {
-    float sc[32];
-#pragma unroll
-    for (int q = 0; q < 8; ++q) {
-        sc[4 * q + 0] = fmaf(alpha, __uint_as_float(r[4 * q + 0]), cb[q].x);
-        sc[4 * q + 1] = fmaf(alpha, __uint_as_float(r[4 * q + 1]), cb[q].y);
-        sc[4 * q + 2] = fmaf(alpha, __uint_as_float(r[4 * q + 2]), cb[q].z);
-        sc[4 * q + 3] = fmaf(alpha, __uint_as_float(r[4 * q + 3]), cb[q].w);
-    }
-    float m16[16];
-#pragma unroll
-    for (int i = 0; i < 16; ++i) m16[i] = fmaxf(sc[2 * i], sc[2 * i + 1]);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) m16[i] = fmaxf(m16[2 * i], m16[2 * i + 1]);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) m16[i] = fmaxf(m16[2 * i], m16[2 * i + 1]);
-    const float mx = fmaxf(fmaxf(m16[0], m16[1]), fmaxf(m16[2], m16[3]));
-    if (mx > fmaxf(L.worst(), floor_adj)) {
-        float tmp[32];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) tmp[j] = sc[j];
-#pragma unroll 1
-        for (int j = 0; j < 32; ++j) {
-            const float v = tmp[j];
-            if (v > fmaxf(L.worst(), floor_adj)) L.insert(v, id0 + j);
-        }
-    }
-}
-
-template <int KP>
+template <int KP, bool kBuf>
 __global__ void __launch_bounds__(kThreads, 1)
 screen_tf32x3_kernel(const __grid_constant__ CUtensorMap tm_a_hi,
                      const __grid_constant__ CUtensorMap tm_a_lo,
@@ -202,7 +160,8 @@ screen_tf32x3_kernel(const __grid_constant__ CUtensorMap tm_a_hi,
                             if (!mbar_wait(&S.empty[stage], sphase ^ 1u, abort_flag)) { ok = false; break; }
                             mbar_arrive_expect_tx(&S.full[stage], kStageBytes);
                             tma_load_2d(plane ? &tm_b_lo : &tm_b_hi, &S.full[stage],
-                                        S.b + stage * kStageBytes, kb * kBK, t * kBN);
+                                        S.b + stage * kStageBytes, kb * kBK,
+                                        t * p.tile_stride * kBN);
                             issued_mask |= 1u << stage;
                             issued_phase = (issued_phase & ~(1u << stage)) | (sphase << stage);
                             if (++stage == stages) { stage = 0; sphase ^= 1u; }
@@ -293,16 +252,23 @@ screen_tf32x3_kernel(const __grid_constant__ CUtensorMap tm_a_hi,
             const bool live = row < p.m;
             TopList<KP> L;
             L.init();
+            BufferRow br{};
+            if constexpr (kBuf) {
+                const int rr = live ? row : 0;
+                br = BufferRow{p.buf_cnt + rr, p.buf_s + static_cast<int64_t>(rr) * p.cap,
+                               p.buf_i + static_cast<int64_t>(rr) * p.cap, p.cap};
+            }
             for (int t = t0; t < t1; ++t, ++tcount) {
                 const uint32_t b = tcount & 1u;
                 const uint32_t ph = (tcount >> 1) & 1u;
                 if (!mbar_wait(&S.acc_full[b], ph, abort_flag)) { ok = false; break; }
                 // floor published by finished units of the same query (monotone)
                 const float floor_adj =
-                    live ? floor_below(__ldcg(p.thr + row)) : __int_as_float(0x7f800000);
-                const float* cb_tile = p.colbias + static_cast<int64_t>(t) * kBN;
+                    !live ? __int_as_float(0x7f800000)
+                          : (p.use_floor ? floor_below(__ldcg(p.thr + row)) : -__int_as_float(0x7f800000));
+                const int id_tile = t * p.tile_stride * kBN;
+                const float* cb_tile = p.colbias + id_tile;
                 const uint32_t taddr = lane_addr + b * kBN;
-                const int id_tile = t * kBN;
                 uint32_t ra[32], rb[32];
                 float4 ca[8], cbv[8];
                 __syncwarp();
@@ -315,21 +281,24 @@ screen_tf32x3_kernel(const __grid_constant__ CUtensorMap tm_a_hi,
                     __syncwarp();
                     tmem_ld_32x32b_x32(taddr + (c + 1) * 32, rb);
                     load_bias(cbv, cb_tile + (c + 1) * 32);
-                    scan_chunk<KP>(ra, ca, p.alpha, floor_adj, L, id_tile + c * 32);
+                    if constexpr (kBuf) buffer_chunk(ra, ca, p.alpha, floor_adj, br, id_tile + c * 32);
+                    else scan_chunk<KP>(ra, ca, p.alpha, floor_adj, L, id_tile + c * 32);
                     tmem_wait_ld_regs(rb);
                     if (c + 2 < kBN / 32) {
                         __syncwarp();
                         tmem_ld_32x32b_x32(taddr + (c + 2) * 32, ra);
                         load_bias(ca, cb_tile + (c + 2) * 32);
                     }
-                    scan_chunk<KP>(rb, cbv, p.alpha, floor_adj, L, id_tile + (c + 1) * 32);
+                    if constexpr (kBuf)
+                        buffer_chunk(rb, cbv, p.alpha, floor_adj, br, id_tile + (c + 1) * 32);
+                    else scan_chunk<KP>(rb, cbv, p.alpha, floor_adj, L, id_tile + (c + 1) * 32);
                 }
                 __syncwarp();
                 tc_fence_before();
                 mbar_arrive(&S.acc_empty[b]);
             }
             if (!ok) break;
-            if (live) {
+            if (!kBuf && live) {
                 const int64_t o = (static_cast<int64_t>(ch) * p.m_pad + row) * KP;
                 float4* ps = reinterpret_cast<float4*>(p.part_score + o);
                 int4* pi = reinterpret_cast<int4*>(p.part_id + o);
@@ -340,7 +309,7 @@ screen_tf32x3_kernel(const __grid_constant__ CUtensorMap tm_a_hi,
                 }
                 // A full list's KP-th score is a lower bound of the query's
                 // global KP-th best: no row below it can matter any more.
-                if (L.id[KP - 1] >= 0) atomicMax(p.thr + row, score_key(L.s[KP - 1]));
+                if (p.use_floor && L.id[KP - 1] >= 0) atomicMax(p.thr + row, score_key(L.s[KP - 1]));
             }
         }
     }
@@ -352,15 +321,15 @@ screen_tf32x3_kernel(const __grid_constant__ CUtensorMap tm_a_hi,
     if (threadIdx.x == 0 && *abort_flag) atomicExch(p.err, *abort_flag);
 }
 
-template <int KP>
+template <int KP, bool kBuf = false>
 cudaError_t launch_kp(const CUtensorMap& a_hi, const CUtensorMap& a_lo, const CUtensorMap& b_hi,
                       const CUtensorMap& b_lo, const ScreenParams& p, int grid,
                       cudaStream_t stream) {
     const int smem = screen_tf32x3_smem_bytes(p.d_pad);
-    cudaError_t e = cudaFuncSetAttribute(screen_tf32x3_kernel<KP>,
+    cudaError_t e = cudaFuncSetAttribute(screen_tf32x3_kernel<KP, kBuf>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
-    screen_tf32x3_kernel<KP><<<grid, kThreads, smem, stream>>>(a_hi, a_lo, b_hi, b_lo, p);
+    screen_tf32x3_kernel<KP, kBuf><<<grid, kThreads, smem, stream>>>(a_hi, a_lo, b_hi, b_lo, p);
     return cudaGetLastError();
 }
 
@@ -376,6 +345,7 @@ cudaError_t launch_screen_tf32x3(int kp, const CUtensorMap& a_hi, const CUtensor
                                  const ScreenParams& p, int grid, cudaStream_t stream) {
     if (p.d_pad % kBK != 0 || p.d_pad > kMaxDPadResident || p.d_pad < kBK) return cudaErrorInvalidValue;
     switch (kp) {
+        case 0: return launch_kp<4, true>(a_hi, a_lo, b_hi, b_lo, p, grid, stream);
         case 4: return launch_kp<4>(a_hi, a_lo, b_hi, b_lo, p, grid, stream);
         case 8: return launch_kp<8>(a_hi, a_lo, b_hi, b_lo, p, grid, stream);
         case 16: return launch_kp<16>(a_hi, a_lo, b_hi, b_lo, p, grid, stream);

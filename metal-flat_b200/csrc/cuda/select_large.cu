@@ -1,0 +1,290 @@
+// select_large.cu -- selection for large k (up to 1024): floor from the
+// sampling pre-pass, then per-query top-k from the candidate buffers that the
+// buffer-mode screen filled.
+//
+// Floor.  The pre-pass screens an evenly spread sample of database tiles in
+// list mode and leaves, per query, L lists of the KP1 best sampled rows.  The
+// minimum over the lists of their KP1-th score is met by at least L*KP1 sampled
+// rows, so it is <= the global (L*KP1)-th best score: with L*KP1 >= KP no row of
+// the query's global top-KP scores below it (the screen then keeps s >= floor).
+//
+// Select.  Per query, a block radix-selects over the buffer (4 passes of 8 bits
+// on order-preserving keys), gathers the winners (ties at the threshold broken
+// by lowest id), sorts them by (score desc, id asc) and writes the results.
+//   recall path (fp16 / bf16 storage): the top-k by screen score, distances
+//     from the screen (L2: max(0, ||q||^2 - s), reference Distance.h:79-81).
+//   exact path (fp32 storage): the k-th screen score s'_(k) gives the window
+//     [s'_(k) - 2E, inf) that must hold the true top-k (see select.cu); it lies
+//     inside the buffer when the floor is below it, and every buffered row in
+//     it is re-scored in fp64 and sorted by (distance, id).
+#include <cfloat>
+#include <climits>
+
+#include "kernels.cuh"
+#include "ptx.cuh"
+
+namespace mflat_cu {
+namespace {
+
+constexpr int kSelThreads = 512;
+constexpr int kSelMax = 2048;       // winners sorted in shared memory
+
+__device__ __forceinline__ float key_to_score(uint32_t key) {
+    const uint32_t u = (key & 0x80000000u) ? (key & 0x7fffffffu) : ~key;
+    return __uint_as_float(u);
+}
+
+// Key of the want-th largest key among s[0..n) (want in [1, n]) and how many
+// entries equal to it belong to the top-want.
+__device__ void radix_select(const float* __restrict__ s, int n, int want, uint32_t* hist,
+                             uint32_t* sh_prefix, int* sh_remaining) {
+    if (threadIdx.x == 0) { *sh_prefix = 0; *sh_remaining = want; }
+    uint32_t mask = 0;
+    for (int shift = 24; shift >= 0; shift -= 8) {
+        for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
+        __syncthreads();
+        const uint32_t prefix = *sh_prefix;
+        for (int i = threadIdx.x; i < n; i += blockDim.x) {
+            const uint32_t key = score_key(s[i]);
+            if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            int rem = *sh_remaining;
+            uint32_t acc = 0;
+            int d = 255;
+            for (; d > 0; --d) {
+                if (acc + hist[d] >= static_cast<uint32_t>(rem)) break;
+                acc += hist[d];
+            }
+            *sh_prefix = prefix | (static_cast<uint32_t>(d) << shift);
+            *sh_remaining = rem - static_cast<int>(acc);
+        }
+        mask |= 255u << shift;
+        __syncthreads();
+    }
+}
+
+// Bitonic sort of cnt (<= kSelMax) entries: key descending, then id ascending.
+__device__ void bitonic_sort(double* key, int* id, int cnt) {
+    int P = 1;
+    while (P < cnt) P <<= 1;
+    for (int i = cnt + threadIdx.x; i < P; i += blockDim.x) { key[i] = -DBL_MAX; id[i] = INT_MAX; }
+    __syncthreads();
+    for (int size = 2; size <= P; size <<= 1) {
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            for (int i = threadIdx.x; i < P; i += blockDim.x) {
+                const int j = i ^ stride;
+                if (j > i) {
+                    const bool desc = (i & size) == 0;
+                    const bool i_first = key[i] > key[j] || (key[i] == key[j] && id[i] < id[j]);
+                    if (i_first != desc) {
+                        const double tk = key[i]; key[i] = key[j]; key[j] = tk;
+                        const int ti = id[i]; id[i] = id[j]; id[j] = ti;
+                    }
+                }
+            }
+            __syncthreads();
+        }
+    }
+}
+
+// Bitonic sort of cnt (<= kSelMax) ints ascending.
+__device__ void bitonic_sort_int(int* a, int cnt) {
+    int P = 1;
+    while (P < cnt) P <<= 1;
+    for (int i = cnt + threadIdx.x; i < P; i += blockDim.x) a[i] = INT_MAX;
+    __syncthreads();
+    for (int size = 2; size <= P; size <<= 1) {
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            for (int i = threadIdx.x; i < P; i += blockDim.x) {
+                const int j = i ^ stride;
+                if (j > i) {
+                    const bool asc = (i & size) == 0;
+                    if ((a[i] > a[j]) == asc) { const int t = a[i]; a[i] = a[j]; a[j] = t; }
+                }
+            }
+            __syncthreads();
+        }
+    }
+}
+
+__device__ __forceinline__ double exact_score_l(int metric, const float* qh, const float* ql,
+                                                const float* xh, const float* xl, int dim) {
+    double acc = 0.0;
+    if (metric == kL2) {
+        for (int c = 0; c < dim; ++c) {
+            const double e = static_cast<double>(qh[c] + ql[c]) - static_cast<double>(xh[c] + xl[c]);
+            acc += e * e;
+        }
+        return -acc;
+    }
+    for (int c = 0; c < dim; ++c)
+        acc += static_cast<double>(qh[c] + ql[c]) * static_cast<double>(xh[c] + xl[c]);
+    return acc;
+}
+
+__device__ __forceinline__ double bound_e(int metric, double qn, double xmax, double gamma) {
+    const double u = 1.0 / 8388608.0;
+    if (metric == kL2) return 2.0 * gamma * qn * xmax + u * xmax * xmax + u * qn * xmax + 1e-30;
+    return gamma * qn * xmax + 1e-30;
+}
+
+__global__ void __launch_bounds__(kSelThreads) select_large_kernel(const LargeSelectParams p) {
+    const int qi = blockIdx.x;
+    if (qi >= p.m) return;
+    __shared__ uint32_t hist[256];
+    __shared__ uint32_t sh_prefix;
+    __shared__ int sh_remaining, sh_pos, sh_tpos, sh_status;
+    __shared__ double key[kSelMax];
+    __shared__ int ids[kSelMax];
+    __shared__ int ties[kSelMax];
+
+    const uint32_t n_raw = p.cnt[qi];
+    const float* bs = p.buf_s + static_cast<int64_t>(qi) * p.cap;
+    const int32_t* bi = p.buf_i + static_cast<int64_t>(qi) * p.cap;
+    const float empty = p.metric == kL2 ? __int_as_float(0x7f800000) : -__int_as_float(0x7f800000);
+    int64_t orow = static_cast<int64_t>(qi) * p.k_out;
+
+    if (n_raw > p.cap) {                                  // buffer overflow: report, write nothing
+        if (threadIdx.x == 0) atomicAdd(p.overflow, 1);
+        return;
+    }
+    const int n = static_cast<int>(n_raw);
+    const int k = p.k_out;
+    const int want = min(k, n);
+    if (threadIdx.x == 0) { sh_pos = 0; sh_tpos = 0; sh_status = 0; }
+    int cnt = 0;     // entries gathered into key/ids
+
+    if (want > 0) {
+        radix_select(bs, n, want, hist, &sh_prefix, &sh_remaining);
+        const uint32_t T = sh_prefix;
+        if (!p.exact) {
+            // winners: keys > T, plus the lowest-id entries equal to T
+            const int need_eq = sh_remaining;
+            for (int i = threadIdx.x; i < n; i += blockDim.x) {
+                const uint32_t kk = score_key(bs[i]);
+                if (kk > T) {
+                    const int slot = atomicAdd(&sh_pos, 1);
+                    key[slot] = bs[i];
+                    ids[slot] = bi[i];
+                } else if (kk == T) {
+                    const int slot = atomicAdd(&sh_tpos, 1);
+                    if (slot < kSelMax) ties[slot] = bi[i];
+                }
+            }
+            __syncthreads();
+            const int ngt = sh_pos, nt = sh_tpos;
+            if (nt > kSelMax) {
+                if (threadIdx.x == 0) atomicAdd(p.overflow, 1);
+                return;
+            }
+            bitonic_sort_int(ties, nt);                  // lowest ids first
+            const float tsc = key_to_score(T);
+            for (int i = threadIdx.x; i < need_eq; i += blockDim.x) {
+                key[ngt + i] = tsc;
+                ids[ngt + i] = ties[i];
+            }
+            __syncthreads();
+            cnt = ngt + need_eq;
+            bitonic_sort(key, ids, cnt);
+            for (int pos = threadIdx.x; pos < k; pos += blockDim.x) {
+                if (pos < cnt) {
+                    const double s = key[pos];
+                    float d;
+                    if (p.metric == kL2) d = fmaxf(0.0f, static_cast<float>(static_cast<double>(p.qsq[qi]) - s));
+                    else d = static_cast<float>(s);
+                    p.out_ids[orow + pos] = static_cast<int32_t>(ids[pos] + p.id_base);
+                    p.out_dist[orow + pos] = d;
+                } else {
+                    p.out_ids[orow + pos] = -1;
+                    p.out_dist[orow + pos] = empty;
+                }
+            }
+            return;
+        }
+        // ---- exact path: window [s'_(k) - 2E, inf) must lie above the floor
+        const double sk = key_to_score(T);
+        const double xmax = static_cast<double>(__uint_as_float(*p.xmax_bits));
+        const double E = bound_e(p.metric, p.qnorm[qi], xmax, p.gamma);
+        const double W = sk - 2.0 * E;
+        const double floor_s = (p.thr[qi] == 0u) ? -DBL_MAX : static_cast<double>(key_to_score(p.thr[qi]));
+        if (!(W >= floor_s)) {                    // window reaches below the floor
+            if (threadIdx.x == 0) sh_status = 1;
+        } else {
+            for (int i = threadIdx.x; i < n; i += blockDim.x) {
+                if (static_cast<double>(bs[i]) >= W) {
+                    const int slot = atomicAdd(&sh_pos, 1);
+                    if (slot < kSelMax) ids[slot] = bi[i];
+                }
+            }
+        }
+        __syncthreads();
+        if (threadIdx.x == 0 && sh_status == 0 && sh_pos > kSelMax) sh_status = 1;   // too many near-ties
+        __syncthreads();
+        if (sh_status) {
+            if (threadIdx.x == 0) {
+                const int slot = atomicAdd(p.flag_count, 1);
+                p.flag_list[slot] = qi;
+            }
+            return;
+        }
+        cnt = sh_pos;
+        const float* qh = p.q_hi + static_cast<int64_t>(qi) * p.d_pad;
+        const float* ql = p.q_lo + static_cast<int64_t>(qi) * p.d_pad;
+        for (int i = threadIdx.x; i < cnt; i += blockDim.x) {
+            const int64_t id = ids[i];
+            key[i] = exact_score_l(p.metric, qh, ql, p.db_hi + id * p.d_pad, p.db_lo + id * p.d_pad, p.dim);
+        }
+        __syncthreads();
+        bitonic_sort(key, ids, cnt);
+        for (int pos = threadIdx.x; pos < k; pos += blockDim.x) {
+            if (pos < cnt) {
+                p.out_ids[orow + pos] = static_cast<int32_t>(ids[pos] + p.id_base);
+                p.out_dist[orow + pos] = static_cast<float>(p.metric == kL2 ? -key[pos] : key[pos]);
+            } else {
+                p.out_ids[orow + pos] = -1;
+                p.out_dist[orow + pos] = empty;
+            }
+        }
+        return;
+    }
+    for (int pos = threadIdx.x; pos < k; pos += blockDim.x) {
+        p.out_ids[orow + pos] = -1;
+        p.out_dist[orow + pos] = empty;
+    }
+}
+
+// thr[q] = key of min over the L pre-pass lists of their KP1-th score (0 when a
+// list is not full: then no floor is known and every row is admitted).
+__global__ void prepass_floor_kernel(const float* __restrict__ part_s, const int32_t* __restrict__ part_i,
+                                     int n_lists, int m, int m_pad, int kp1, uint32_t* thr) {
+    const int q = blockIdx.x * blockDim.x + threadIdx.x;
+    if (q >= m_pad) return;
+    if (q >= m) { thr[q] = 0u; return; }
+    float mn = __int_as_float(0x7f800000);
+    bool full = true;
+    for (int l = 0; l < n_lists; ++l) {
+        const int64_t o = (static_cast<int64_t>(l) * m_pad + q) * kp1 + (kp1 - 1);
+        if (part_i[o] < 0) { full = false; break; }
+        mn = fminf(mn, part_s[o]);
+    }
+    thr[q] = full ? score_key(mn) : 0u;
+}
+
+}  // namespace
+
+cudaError_t launch_select_large(const LargeSelectParams& p, cudaStream_t stream) {
+    if (p.k_out < 1 || p.k_out > kSelMax) return cudaErrorInvalidValue;
+    select_large_kernel<<<p.m, kSelThreads, 0, stream>>>(p);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_prepass_floor(const float* part_s, const int32_t* part_i, int n_lists, int m,
+                                 int m_pad, int kp1, uint32_t* thr, cudaStream_t stream) {
+    prepass_floor_kernel<<<(m_pad + 127) / 128, 128, 0, stream>>>(part_s, part_i, n_lists, m, m_pad,
+                                                                   kp1, thr);
+    return cudaGetLastError();
+}
+
+}  // namespace mflat_cu

@@ -72,8 +72,6 @@ def test_golden_cases(golden_dir):
     mname = {0: "l2", 1: "ip", 2: "cosine"}
     for nm in names:
         n, dim, m, k, metric = (int(x) for x in c[nm + "_meta"])
-        if k > 21:
-            continue                                # large-k path covered elsewhere
         db, q = c[nm + "_db"], c[nm + "_q"]
         ids, dist = search(db, q, k, mname[metric])
         assert_exact(ids, dist, db, q, k, mname[metric])
@@ -186,3 +184,30 @@ def test_device_pointer_api():
     assert used == 10
     torch.cuda.synchronize()
     assert_exact(d_ids.cpu().numpy(), d_dist.cpu().numpy(), db, q, 10, "ip")
+
+
+LARGE = [  # n, dim, m, k   (n <= 32768: every row buffered; larger: floor pre-pass)
+    (3000, 40, 30, 22), (3000, 128, 17, 300), (150_000, 128, 40, 64),
+    (150_000, 64, 33, 1024), (200_003, 17, 20, 100), (60_000, 160, 9, 50),
+]
+
+
+@pytest.mark.parametrize("metric", ["l2", "ip", "cosine"])
+@pytest.mark.parametrize("shape", LARGE, ids=lambda s: "n%d_d%d_m%d_k%d" % s)
+def test_large_k_exact(metric, shape):
+    n, dim, m, k = shape
+    rng = np.random.default_rng(hash(("large", metric) + shape) % 2**32)
+    db = rng.standard_normal((n, dim)).astype(np.float32)
+    q = rng.standard_normal((m, dim)).astype(np.float32)
+    ids, dist = search(db, q, k, metric)
+    assert_exact(ids, dist, db, q, k, metric)
+
+
+def test_large_k_clamp_and_uniform():
+    """k above 1024 is clamped (one-time warning); uniform data, 1M rows."""
+    rng = np.random.default_rng(21)
+    db = rng.random((1_000_000, 128), dtype=np.float32)
+    q = rng.random((12, 128), dtype=np.float32)
+    ids, dist = search(db, q, 5000, "l2")
+    assert ids.shape == (12, 1024)
+    assert_exact(ids, dist, db, q, 1024, "l2")
