@@ -416,7 +416,8 @@ LargePlan plan_large(int64_t n, int k, int m, int kp1) {
         P.cap = static_cast<uint32_t>((n + 255) / 256 * 256);
     } else {
         P.prepass = true;
-        P.lists = std::max(1, (2 * k + kp1 - 1) / kp1);      // lists * kp1 >= 2k
+        // union of lists * kp1 >= 4k sampled scores; floor = its 2k-th best
+        P.lists = std::min(4096 / kp1, std::max(1, (4 * k + kp1 - 1) / kp1));
         P.stride = 16;
         while (P.stride > 1 && (n_tiles + P.stride - 1) / P.stride < 2 * P.lists) P.stride /= 2;
         P.sample_tiles = (n_tiles + P.stride - 1) / P.stride;
@@ -424,7 +425,9 @@ LargePlan plan_large(int64_t n, int k, int m, int kp1) {
             P.prepass = false;
             P.cap = static_cast<uint32_t>((n + 255) / 256 * 256);
         } else {
-            const int64_t expect = static_cast<int64_t>(P.lists) * kp1 * P.stride;
+            // the floor is the want-th best sampled score (want = 2k): about
+            // want * stride rows of the whole database score above it
+            const int64_t expect = static_cast<int64_t>(2) * k * P.stride;
             int64_t cap = std::max<int64_t>(4 * expect, 4096);
             cap = std::min<int64_t>((cap + 255) / 256 * 256, (n + 255) / 256 * 256);
             P.cap = static_cast<uint32_t>(cap);
@@ -520,7 +523,7 @@ int search_large(mflat_cu_index* ix, const float* queries, int m, int k_out, int
             pp.part_id = ix->part_i.as<int32_t>();
             CU_TRY(launch_pass(ix, pp, kKP1, st), "floor pre-pass launch");
             CU_TRY(launch_prepass_floor(pp.part_score, pp.part_id, pp.n_chunks, mb, mb_pad, kKP1,
-                                        sp.thr, st),
+                                        2 * k_out, sp.thr, st),
                    "floor launch");
         }
         sp.use_floor = 1;

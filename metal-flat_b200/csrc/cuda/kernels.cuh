@@ -145,7 +145,7 @@ cudaError_t launch_fallback_exact(const SelectParams& p, int grid, cudaStream_t 
 int screen_tf32x3_smem_bytes(int d_pad);
 cudaError_t launch_select_large(const LargeSelectParams& p, cudaStream_t stream);
 cudaError_t launch_prepass_floor(const float* part_s, const int32_t* part_i, int n_lists, int m,
-                                 int m_pad, int kp1, uint32_t* thr, cudaStream_t stream);
+                                 int m_pad, int kp1, int want, uint32_t* thr, cudaStream_t stream);
 cudaError_t launch_kmeans_select(const SelectParams& p, int32_t* out, int grid_fallback,
                                  cudaStream_t stream);
 

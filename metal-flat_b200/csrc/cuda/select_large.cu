@@ -255,21 +255,45 @@ __global__ void __launch_bounds__(kSelThreads) select_large_kernel(const LargeSe
     }
 }
 
-// thr[q] = key of min over the L pre-pass lists of their KP1-th score (0 when a
-// list is not full: then no floor is known and every row is admitted).
-__global__ void prepass_floor_kernel(const float* __restrict__ part_s, const int32_t* __restrict__ part_i,
-                                     int n_lists, int m, int m_pad, int kp1, uint32_t* thr) {
-    const int q = blockIdx.x * blockDim.x + threadIdx.x;
+// Floor of one query from the pre-pass lists: the want-th largest score in the
+// union of its L lists (each the KP1 best rows of one sample chunk).  At least
+// `want` sampled rows score at or above it, so it is <= the global want-th
+// best.  thr[q] = 0 (no floor) when the union holds fewer than `want` rows.
+constexpr int kFloorMax = 4096;
+
+__global__ void __launch_bounds__(256) prepass_floor_kernel(const float* __restrict__ part_s,
+                                                            const int32_t* __restrict__ part_i,
+                                                            int n_lists, int m, int m_pad, int kp1,
+                                                            int want, uint32_t* thr) {
+    const int q = blockIdx.x;
     if (q >= m_pad) return;
-    if (q >= m) { thr[q] = 0u; return; }
-    float mn = __int_as_float(0x7f800000);
-    bool full = true;
-    for (int l = 0; l < n_lists; ++l) {
-        const int64_t o = (static_cast<int64_t>(l) * m_pad + q) * kp1 + (kp1 - 1);
-        if (part_i[o] < 0) { full = false; break; }
-        mn = fminf(mn, part_s[o]);
+    if (q >= m) {
+        if (threadIdx.x == 0) thr[q] = 0u;
+        return;
     }
-    thr[q] = full ? score_key(mn) : 0u;
+    __shared__ float vals[kFloorMax];
+    __shared__ uint32_t hist[256];
+    __shared__ uint32_t sh_prefix;
+    __shared__ int sh_remaining, sh_valid;
+    if (threadIdx.x == 0) sh_valid = 0;
+    __syncthreads();
+    const int total = n_lists * kp1;
+    int valid = 0;
+    for (int e = threadIdx.x; e < total; e += blockDim.x) {
+        const int l = e / kp1, j = e % kp1;
+        const int64_t o = (static_cast<int64_t>(l) * m_pad + q) * kp1 + j;
+        const bool ok = part_i[o] >= 0;
+        vals[e] = ok ? part_s[o] : -__int_as_float(0x7f800000);
+        valid += ok ? 1 : 0;
+    }
+    atomicAdd(&sh_valid, valid);
+    __syncthreads();
+    if (sh_valid < want) {
+        if (threadIdx.x == 0) thr[q] = 0u;
+        return;
+    }
+    radix_select(vals, total, want, hist, &sh_prefix, &sh_remaining);
+    if (threadIdx.x == 0) thr[q] = sh_prefix;
 }
 
 }  // namespace
@@ -281,9 +305,9 @@ cudaError_t launch_select_large(const LargeSelectParams& p, cudaStream_t stream)
 }
 
 cudaError_t launch_prepass_floor(const float* part_s, const int32_t* part_i, int n_lists, int m,
-                                 int m_pad, int kp1, uint32_t* thr, cudaStream_t stream) {
-    prepass_floor_kernel<<<(m_pad + 127) / 128, 128, 0, stream>>>(part_s, part_i, n_lists, m, m_pad,
-                                                                   kp1, thr);
+                                 int m_pad, int kp1, int want, uint32_t* thr, cudaStream_t stream) {
+    if (n_lists * kp1 > kFloorMax || want < 1) return cudaErrorInvalidValue;
+    prepass_floor_kernel<<<m_pad, 256, 0, stream>>>(part_s, part_i, n_lists, m, m_pad, kp1, want, thr);
     return cudaGetLastError();
 }
 
