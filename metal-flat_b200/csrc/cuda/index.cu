@@ -11,6 +11,8 @@
 // (src/Distance.h:40-60).
 #include <cudaTypedefs.h>
 #include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -110,7 +112,89 @@ bool make_map_f32(CUtensorMap* map, const float* base, uint64_t inner, uint64_t 
     return r == CUDA_SUCCESS;
 }
 
+// 16-bit rows [rows][inner] (fp16 / bf16 bits): box [box_rows][64 halves].
+bool make_map_u16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows,
+                  uint32_t box_rows) {
+    if (!get_encoder()) return false;
+    cuuint64_t dims[2] = {inner, rows};
+    cuuint64_t strides[1] = {inner * 2};
+    cuuint32_t box[2] = {64u, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(base), dims,
+                          strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
 // ------------------------------------------------------------- kernels
+// fp32 -> 16-bit storage bits, round to nearest even.
+__device__ __forceinline__ uint16_t to_half_bits(float x, bool bf16) {
+    if (bf16) return __bfloat16_as_ushort(__float2bfloat16_rn(x));
+    return __half_as_ushort(__float2half_rn(x));
+}
+__device__ __forceinline__ float from_half_bits(uint16_t u, bool bf16) {
+    return bf16 ? __bfloat162float(__ushort_as_bfloat16(u)) : __half2float(__ushort_as_half(u));
+}
+
+// 16-bit storage ingest: Cosine normalisation as for fp32 (Distance.h:50-60),
+// then conversion; the norm term is that of the stored 16-bit row.
+__global__ void ingest_rows_half_kernel(const float* __restrict__ src, int64_t n, int dim, int d_pad,
+                                        int metric, bool bf16, int64_t row0, uint16_t* __restrict__ db,
+                                        float* __restrict__ colbias, float* __restrict__ dnorm) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const float* row = src + i * dim;
+    uint16_t* o = db + (row0 + i) * d_pad;
+    float inv = 1.0f;
+    bool scale = false;
+    if (metric == kCosine) {
+        double s = 0.0;
+        for (int c = 0; c < dim; ++c) s += static_cast<double>(row[c]) * row[c];
+        if (s > 0.0) { inv = static_cast<float>(1.0 / sqrt(s)); scale = true; }
+    }
+    double s2 = 0.0;
+    for (int c = 0; c < dim; ++c) {
+        const uint16_t h = to_half_bits(scale ? row[c] * inv : row[c], bf16);
+        const float x = from_half_bits(h, bf16);
+        s2 += static_cast<double>(x) * x;
+        o[c] = h;
+    }
+    for (int c = dim; c < d_pad; ++c) o[c] = 0;
+    dnorm[row0 + i] = static_cast<float>(s2);
+    colbias[row0 + i] = metric == kL2 ? -static_cast<float>(s2) : 0.0f;
+}
+
+__global__ void prep_queries_half_kernel(const float* __restrict__ src, int m, int m_pad, int dim,
+                                         int d_pad, int metric, bool bf16, uint16_t* __restrict__ q,
+                                         float* __restrict__ qsq) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= m_pad) return;
+    uint16_t* o = q + static_cast<int64_t>(i) * d_pad;
+    if (i >= m) {
+        for (int c = 0; c < d_pad; ++c) o[c] = 0;
+        qsq[i] = 0.0f;
+        return;
+    }
+    const float* row = src + static_cast<int64_t>(i) * dim;
+    float inv = 1.0f;
+    bool scale = false;
+    if (metric == kCosine) {
+        double s = 0.0;
+        for (int c = 0; c < dim; ++c) s += static_cast<double>(row[c]) * row[c];
+        if (s > 0.0) { inv = static_cast<float>(1.0 / sqrt(s)); scale = true; }
+    }
+    double s2 = 0.0;
+    for (int c = 0; c < dim; ++c) {
+        const uint16_t h = to_half_bits(scale ? row[c] * inv : row[c], bf16);
+        const float x = from_half_bits(h, bf16);
+        s2 += static_cast<double>(x) * x;
+        o[c] = h;
+    }
+    for (int c = dim; c < d_pad; ++c) o[c] = 0;
+    qsq[i] = static_cast<float>(s2);
+}
+
 __device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
     hi = __uint_as_float(f32_to_tf32_rna(x));
     lo = x - hi;   // exact: lo = x - tf32(x) has at most 13 significant bits
@@ -203,25 +287,27 @@ cudaError_t grow(mflat_cu_index* ix, int64_t need) {
     int64_t cap = std::max<int64_t>(need, ix->cap + ix->cap / 2);
     cap = (cap + kBN - 1) / kBN * kBN;
     float *h = nullptr, *l = nullptr, *cb = nullptr, *dn = nullptr;
-    const size_t rowb = static_cast<size_t>(ix->d_pad) * sizeof(float);
+    const bool half = ix->storage != 0;
+    const size_t rowb = static_cast<size_t>(ix->d_pad) * (half ? 2 : sizeof(float));
     cudaError_t e;
     if ((e = cudaMalloc(&h, cap * rowb)) != cudaSuccess) goto bad;
-    if ((e = cudaMalloc(&l, cap * rowb)) != cudaSuccess) goto bad;
+    if (!half && (e = cudaMalloc(&l, cap * rowb)) != cudaSuccess) goto bad;
     if ((e = cudaMalloc(&cb, cap * sizeof(float))) != cudaSuccess) goto bad;
     if ((e = cudaMalloc(&dn, cap * sizeof(float))) != cudaSuccess) goto bad;
     if (ix->n > 0) {
-        cudaMemcpyAsync(h, ix->db_hi, ix->n * rowb, cudaMemcpyDeviceToDevice, st);
-        cudaMemcpyAsync(l, ix->db_lo, ix->n * rowb, cudaMemcpyDeviceToDevice, st);
+        cudaMemcpyAsync(h, half ? ix->db16 : static_cast<void*>(ix->db_hi), ix->n * rowb,
+                        cudaMemcpyDeviceToDevice, st);
+        if (!half) cudaMemcpyAsync(l, ix->db_lo, ix->n * rowb, cudaMemcpyDeviceToDevice, st);
         cudaMemcpyAsync(cb, ix->colbias, ix->n * sizeof(float), cudaMemcpyDeviceToDevice, st);
         cudaMemcpyAsync(dn, ix->dnorm, ix->n * sizeof(float), cudaMemcpyDeviceToDevice, st);
     }
     fill_f32_kernel<<<blocks_for(cap - ix->n, 256), 256, 0, st>>>(cb + ix->n, cap - ix->n, -kInf);
     if ((e = cudaStreamSynchronize(st)) != cudaSuccess) goto bad;
-    cudaFree(ix->db_hi);
+    cudaFree(half ? ix->db16 : static_cast<void*>(ix->db_hi));
     cudaFree(ix->db_lo);
     cudaFree(ix->colbias);
     cudaFree(ix->dnorm);
-    ix->db_hi = h;
+    if (half) ix->db16 = h; else ix->db_hi = h;
     ix->db_lo = l;
     ix->colbias = cb;
     ix->dnorm = dn;
@@ -580,6 +666,166 @@ int search_large(mflat_cu_index* ix, const float* queries, int m, int k_out, int
     return ST_OK;
 }
 
+// ---------------------------------------------------------------------------
+// fp16 / bf16 storage (recall path).  k <= 16: list-mode screen (two lists per
+// chunk) + recall select.  k > 16: strided floor pre-pass (list mode, 16 per
+// list), buffer-mode screen, radix select.
+int search_half(mflat_cu_index* ix, const float* queries, int m, int k_out, int32_t* d_ids,
+                float* d_dist, int on_device, cudaStream_t st) {
+    const bool bf16 = ix->storage == 2;
+    const int d_pad = ix->d_pad;
+    const int n_tiles = static_cast<int>((ix->n + kBN - 1) / kBN);
+    const float* qsrc = queries;
+    if (!on_device) {
+        CU_TRY(ix->q_in.ensure(static_cast<size_t>(m) * ix->dim * sizeof(float)), "query buffer");
+        CU_TRY(cudaMemcpyAsync(ix->q_in.p, queries, static_cast<size_t>(m) * ix->dim * sizeof(float),
+                               cudaMemcpyHostToDevice, st),
+               "query upload");
+        qsrc = ix->q_in.as<float>();
+    }
+    const bool list_mode = k_out <= 16;
+    const int kp = k_out <= 4 ? 4 : (k_out <= 8 ? 8 : 16);
+    constexpr int kKP1 = 16;
+    LargePlan P;
+    if (list_mode) {
+        P.batch = m;
+    } else {
+        P = plan_large(ix->n, k_out, m, kKP1);
+        // two lists (half tiles) per pre-pass chunk: halve the chunk count
+        P.lists = std::max(1, (P.lists + 1) / 2);
+    }
+    const int bm_pad = (P.batch + kBM - 1) / kBM * kBM;
+    CU_TRY(ix->q16.ensure(static_cast<size_t>(bm_pad) * d_pad * 2), "query conversion");
+    CU_TRY(ix->qsq.ensure(static_cast<size_t>(bm_pad) * sizeof(float)), "query norms");
+    CU_TRY(ix->thr.ensure(static_cast<size_t>(bm_pad) * sizeof(uint32_t)), "floors");
+    if (!list_mode) {
+        CU_TRY(ix->buf_cnt.ensure(static_cast<size_t>(bm_pad) * sizeof(uint32_t)), "buffer counts");
+        CU_TRY(ix->buf_s.ensure(static_cast<size_t>(bm_pad) * P.cap * sizeof(float)), "candidate buffer");
+        CU_TRY(ix->buf_i.ensure(static_cast<size_t>(bm_pad) * P.cap * sizeof(int32_t)), "candidate buffer");
+        CU_TRY(ix->lk_words.ensure(2 * sizeof(int)), "status words");
+        CU_TRY(cudaMemsetAsync(ix->lk_words.p, 0, 2 * sizeof(int), st), "status words");
+    }
+    const int max_lists = list_mode ? kMaxChunks / 2 : P.lists;
+    const int lk = list_mode ? kp : kKP1;
+    const size_t parts = static_cast<size_t>(2 * std::max(max_lists, 1)) * bm_pad * lk;
+    CU_TRY(ix->part_s.ensure(parts * sizeof(float)), "candidate lists");
+    CU_TRY(ix->part_i.ensure(parts * sizeof(int32_t)), "candidate lists");
+    CUtensorMap tb;
+    if (!make_map_u16(&tb, ix->db16, d_pad, ix->n, kBN)) return fail(ST_DEVICE, "tensor map encoding failed");
+    if (ix->timing) cudaEventRecord(ix->ev[0], st);
+
+    for (int b0 = 0; b0 < m; b0 += P.batch) {
+        const int mb = std::min(P.batch, m - b0);
+        const int mb_pad = (mb + kBM - 1) / kBM * kBM;
+        prep_queries_half_kernel<<<blocks_for(mb_pad, 128), 128, 0, st>>>(
+            qsrc + static_cast<int64_t>(b0) * ix->dim, mb, mb_pad, ix->dim, d_pad, ix->metric, bf16,
+            ix->q16.as<uint16_t>(), ix->qsq.as<float>());
+        CU_TRY(cudaGetLastError(), "query prep launch");
+        CU_TRY(cudaMemsetAsync(ix->thr.p, 0, static_cast<size_t>(mb_pad) * sizeof(uint32_t), st), "floors");
+        CUtensorMap ta;
+        if (!make_map_u16(&ta, ix->q16.p, d_pad, mb_pad, kBM)) return fail(ST_DEVICE, "tensor map encoding failed");
+        ScreenParams sp{};
+        sp.m = mb;
+        sp.m_pad = mb_pad;
+        sp.d_pad = d_pad;
+        sp.n = ix->n;
+        sp.n_qtiles = mb_pad / kBM;
+        sp.alpha = ix->metric == kL2 ? 2.0f : 1.0f;
+        sp.colbias = ix->colbias;
+        sp.err = ix->err;
+        sp.thr = ix->thr.as<uint32_t>();
+        sp.part_score = ix->part_s.as<float>();
+        sp.part_id = ix->part_i.as<int32_t>();
+        auto launch = [&](const ScreenParams& q, int kpp) {
+            const int64_t units = static_cast<int64_t>(q.n_qtiles) * q.n_chunks;
+            const int grid = static_cast<int>(std::min<int64_t>(units, ix->num_sms));
+            return launch_screen_f16(kpp, bf16, ta, tb, q, grid, st);
+        };
+        if (list_mode) {
+            sp.use_floor = 1;
+            sp.tile_stride = 1;
+            sp.n_tiles = n_tiles;
+            int n_chunks = 1, tpc = n_tiles;
+            plan_chunks(sp.n_qtiles, n_tiles, ix->num_sms, kMaxChunks / 2, n_chunks, tpc);
+            sp.n_chunks = n_chunks;
+            sp.tiles_per_chunk = tpc;
+            if (ix->timing) cudaEventRecord(ix->ev[1], st);
+            CU_TRY(launch(sp, kp), "screen launch");
+            if (ix->timing) cudaEventRecord(ix->ev[2], st);
+            SelectParams sel{};
+            sel.m = mb;
+            sel.m_pad = mb_pad;
+            sel.k_out = k_out;
+            sel.n_chunks = 2 * n_chunks;
+            sel.metric = ix->metric == kL2 ? kL2 : kIP;
+            sel.part_score = sp.part_score;
+            sel.part_id = sp.part_id;
+            sel.id_base = ix->world > 1 ? ix->id_base : 0;
+            sel.out_ids = d_ids + static_cast<int64_t>(b0) * k_out;
+            sel.out_dist = d_dist + static_cast<int64_t>(b0) * k_out;
+            CU_TRY(launch_select_recall(kp, sel, ix->qsq.as<float>(), st), "select launch");
+            continue;
+        }
+        CU_TRY(cudaMemsetAsync(ix->buf_cnt.p, 0, static_cast<size_t>(mb_pad) * sizeof(uint32_t), st), "counts");
+        if (P.prepass) {
+            ScreenParams pp = sp;
+            pp.use_floor = 0;
+            pp.tile_stride = P.stride;
+            pp.n_tiles = P.sample_tiles;
+            pp.tiles_per_chunk = (P.sample_tiles + P.lists - 1) / P.lists;
+            pp.n_chunks = (P.sample_tiles + pp.tiles_per_chunk - 1) / pp.tiles_per_chunk;
+            CU_TRY(launch(pp, kKP1), "floor pre-pass launch");
+            CU_TRY(launch_prepass_floor(pp.part_score, pp.part_id, 2 * pp.n_chunks, mb, mb_pad, kKP1,
+                                        k_out, sp.thr, st),
+                   "floor launch");
+        }
+        sp.use_floor = 1;
+        sp.tile_stride = 1;
+        sp.n_tiles = n_tiles;
+        int n_chunks = 1, tpc = n_tiles;
+        plan_chunks(sp.n_qtiles, n_tiles, ix->num_sms, kMaxChunks, n_chunks, tpc);
+        sp.n_chunks = n_chunks;
+        sp.tiles_per_chunk = tpc;
+        sp.buf_cnt = ix->buf_cnt.as<uint32_t>();
+        sp.buf_s = ix->buf_s.as<float>();
+        sp.buf_i = ix->buf_i.as<int32_t>();
+        sp.cap = P.cap;
+        if (ix->timing && b0 == 0) cudaEventRecord(ix->ev[1], st);
+        CU_TRY(launch(sp, 0), "buffer screen launch");
+        if (ix->timing && b0 == 0) cudaEventRecord(ix->ev[2], st);
+        LargeSelectParams ls{};
+        ls.m = mb;
+        ls.m_pad = mb_pad;
+        ls.k_out = k_out;
+        ls.metric = ix->metric == kL2 ? kL2 : kIP;
+        ls.cnt = sp.buf_cnt;
+        ls.buf_s = sp.buf_s;
+        ls.buf_i = sp.buf_i;
+        ls.cap = P.cap;
+        ls.thr = sp.thr;
+        ls.exact = 0;
+        ls.qsq = ix->qsq.as<float>();
+        ls.id_base = ix->world > 1 ? ix->id_base : 0;
+        ls.out_ids = d_ids + static_cast<int64_t>(b0) * k_out;
+        ls.out_dist = d_dist + static_cast<int64_t>(b0) * k_out;
+        ls.flag_count = ix->lk_words.as<int>() + 1;
+        ls.flag_list = nullptr;
+        ls.overflow = ix->lk_words.as<int>();
+        CU_TRY(launch_select_large(ls, st), "large select launch");
+    }
+    if (ix->timing) cudaEventRecord(ix->ev[3], st);
+    ix->last.screen_launches = 1;
+    ix->last.launches = list_mode ? 3 : (P.prepass ? 5 : 3);
+    if (!list_mode) {
+        CU_TRY(cudaMemcpyAsync(&ix->host_words[2], ix->lk_words.p, 2 * sizeof(int), cudaMemcpyDeviceToHost, st),
+               "status");
+        CU_TRY(cudaStreamSynchronize(st), "large-k search");
+        if (ix->host_words[2] > 0)
+            return fail(ST_INTERNAL, "candidate buffer overflow (too many rows tie with the k-th best)");
+    }
+    return ST_OK;
+}
+
 }  // namespace mflat_cu
 
 using namespace mflat_cu;
@@ -609,7 +855,7 @@ int mflat_cu_index_create(int device, int dim, int metric, int storage, mflat_cu
     const int ndev = mflat_cu_device_count();
     if (ndev <= 0) return fail(ST_DEVICE, "no CUDA device");
     if (device >= ndev) return fail(ST_BAD_ARG, "device index out of range");
-    if (storage != 0) return fail(ST_BAD_ARG, "storage precision not supported by this build");
+    if (storage < 0 || storage > 2) return fail(ST_BAD_ARG, "unknown storage precision");
     DeviceGuard g(device);
     int major = 0;
     cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device);
@@ -618,7 +864,8 @@ int mflat_cu_index_create(int device, int dim, int metric, int storage, mflat_cu
     if (!ix) return fail(ST_ALLOC, "host allocation failed");
     ix->device = device;
     ix->dim = dim;
-    ix->d_pad = (dim + kBK - 1) / kBK * kBK;
+    // one 128-byte k-block = 32 fp32 or 64 16-bit elements
+    ix->d_pad = storage == 0 ? (dim + kBK - 1) / kBK * kBK : (dim + 63) / 64 * 64;
     ix->metric = (metric == kIP || metric == kCosine) ? metric : kL2;
     ix->storage = storage;
     cudaDeviceGetAttribute(&ix->num_sms, cudaDevAttrMultiProcessorCount, device);
@@ -650,6 +897,7 @@ void mflat_cu_index_destroy(mflat_cu_index_t* ix) {
     DeviceGuard g(ix->device);
     if (ix->stream) cudaStreamSynchronize(ix->stream);
     comm_release(ix);
+    cudaFree(ix->db16);
     cudaFree(ix->db_hi);
     cudaFree(ix->db_lo);
     cudaFree(ix->colbias);
@@ -661,7 +909,8 @@ void mflat_cu_index_destroy(mflat_cu_index_t* ix) {
     for (DevBuf* b : {&ix->stage_in, &ix->q_in, &ix->q_hi, &ix->q_lo, &ix->qnorm, &ix->part_s,
                       &ix->part_i, &ix->flag_list, &ix->out_ids, &ix->out_dist, &ix->gather_ids,
                       &ix->gather_dist, &ix->merge_tmp_ids, &ix->merge_tmp_dist, &ix->thr, &ix->fb_s,
-                      &ix->fb_i, &ix->buf_cnt, &ix->buf_s, &ix->buf_i, &ix->lk_words})
+                      &ix->fb_i, &ix->buf_cnt, &ix->buf_s, &ix->buf_i, &ix->lk_words,
+                      &ix->q16, &ix->qsq})
         b->release();
     for (auto& ev : ix->ev)
         if (ev) cudaEventDestroy(ev);
@@ -693,9 +942,14 @@ int mflat_cu_index_add(mflat_cu_index_t* ix, const float* vectors, int64_t n, in
             CU_TRY(cudaMemcpyAsync(ix->stage_in.p, src, bytes, cudaMemcpyHostToDevice, ix->stream), "upload");
             src = ix->stage_in.as<float>();
         }
-        ingest_rows_kernel<<<blocks_for(cnt, 128), 128, 0, ix->stream>>>(
-            src, cnt, ix->dim, ix->d_pad, ix->metric, ix->n + off, ix->db_hi, ix->db_lo,
-            ix->colbias, ix->dnorm, ix->xmax_bits);
+        if (ix->storage != 0)
+            ingest_rows_half_kernel<<<blocks_for(cnt, 128), 128, 0, ix->stream>>>(
+                src, cnt, ix->dim, ix->d_pad, ix->metric, ix->storage == 2, ix->n + off,
+                static_cast<uint16_t*>(ix->db16), ix->colbias, ix->dnorm);
+        else
+            ingest_rows_kernel<<<blocks_for(cnt, 128), 128, 0, ix->stream>>>(
+                src, cnt, ix->dim, ix->d_pad, ix->metric, ix->n + off, ix->db_hi, ix->db_lo,
+                ix->colbias, ix->dnorm, ix->xmax_bits);
         CU_TRY(cudaGetLastError(), "ingest launch");
         if (!on_device) CU_TRY(cudaStreamSynchronize(ix->stream), "ingest");
     }
@@ -757,6 +1011,26 @@ int mflat_cu_index_search(mflat_cu_index_t* ix, const float* queries, int m, int
         fill_empty_kernel<<<blocks_for(mk, 256), 256, 0, st>>>(d_ids, d_dist, mk, empty);
         ++launches;
         CU_TRY(cudaGetLastError(), "fill");
+    } else if (ix->storage != 0) {
+        const int rc = search_half(ix, queries, m, k_out, d_ids, d_dist, on_device, st);
+        if (rc != ST_OK) return rc;
+        if (ix->world > 1) {
+            const int rc2 = shard_merge(ix, m, k_out, d_ids, d_dist, st);
+            if (rc2 != ST_OK) return rc2;
+        }
+        if (!on_device) {
+            CU_TRY(cudaMemcpyAsync(out_ids, d_ids, mk * sizeof(int32_t), cudaMemcpyDeviceToHost, st), "download");
+            CU_TRY(cudaMemcpyAsync(out_dist, d_dist, mk * sizeof(float), cudaMemcpyDeviceToHost, st), "download");
+            const int rc3 = wait_stream_checked(ix, st);
+            if (rc3 != ST_OK) return rc3;
+        }
+        if (ix->timing) {
+            CU_TRY(cudaEventSynchronize(ix->ev[3]), "timing");
+            cudaEventElapsedTime(&ix->last.total_ms, ix->ev[0], ix->ev[3]);
+            cudaEventElapsedTime(&ix->last.screen_ms, ix->ev[1], ix->ev[2]);
+            cudaEventElapsedTime(&ix->last.select_ms, ix->ev[2], ix->ev[3]);
+        }
+        return check_device_error(ix);
     } else {
         const int kp = kp_for(k_out);
         if (kp == 0) {

@@ -62,6 +62,7 @@ struct mflat_cu_index {
     int num_sms = 148;
     cudaStream_t stream = nullptr;
     int64_t n = 0, cap = 0;
+    void* db16 = nullptr;         // fp16 / bf16 storage: [cap][d_pad] 16-bit
     float* db_hi = nullptr;       // [cap][d_pad]
     float* db_lo = nullptr;
     float* colbias = nullptr;     // [cap], -inf past n
@@ -73,6 +74,7 @@ struct mflat_cu_index {
     mflat_cu::DevBuf stage_in, q_in, q_hi, q_lo, qnorm, part_s, part_i, flag_list, out_ids, out_dist;
     mflat_cu::DevBuf thr, fb_s, fb_i;
     mflat_cu::DevBuf buf_cnt, buf_s, buf_i, lk_words;   // large-k candidate buffers
+    mflat_cu::DevBuf q16, qsq;                          // 16-bit queries, ||q||^2
     bool timing = false;
     cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
     mflat_cu_timing_t last{};

@@ -140,10 +140,18 @@ cudaError_t launch_screen_tf32x3(int kp, const CUtensorMap& a_hi, const CUtensor
                                  const CUtensorMap& b_hi, const CUtensorMap& b_lo,
                                  const ScreenParams& p, int grid, cudaStream_t stream);
 cudaError_t launch_screen_simt(int kp, const ScreenParams& p, cudaStream_t stream);
+// fp16 / bf16 storage (q and db in 16-bit, d_pad a multiple of 64); kp 0 =
+// buffer mode; list mode writes two lists per (query, chunk).
+cudaError_t launch_screen_f16(int kp, bool bf16, const CUtensorMap& a, const CUtensorMap& b,
+                              const ScreenParams& p, int grid, cudaStream_t stream);
+int screen_f16_smem_bytes(int d_pad);
 cudaError_t launch_select_exact(int kp, const SelectParams& p, cudaStream_t stream);
 cudaError_t launch_fallback_exact(const SelectParams& p, int grid, cudaStream_t stream);
 int screen_tf32x3_smem_bytes(int d_pad);
 cudaError_t launch_select_large(const LargeSelectParams& p, cudaStream_t stream);
+// Recall path, list mode: merge n_lists lists per query, write the top k_out
+// with screen distances (L2: max(0, ||q||^2 - s); IP / Cosine: s).
+cudaError_t launch_select_recall(int kp, const SelectParams& p, const float* qsq, cudaStream_t stream);
 cudaError_t launch_prepass_floor(const float* part_s, const int32_t* part_i, int n_lists, int m,
                                  int m_pad, int kp1, int want, uint32_t* thr, cudaStream_t stream);
 cudaError_t launch_kmeans_select(const SelectParams& p, int32_t* out, int grid_fallback,

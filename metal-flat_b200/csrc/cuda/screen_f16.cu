@@ -1,0 +1,317 @@
+// screen_f16.cu -- tcgen05 kind::f16 distance GEMM with fused selection, for
+// fp16 / bf16 database storage (the recall path: no fp32 rows are kept, the
+// screen's own scores are the result).
+//
+// Same structure as screen_tc.cu, with these differences:
+//   * one operand plane (no hi/lo split): tcgen05.mma.kind::f16, M=128 N=256
+//     K=16, fp32 accumulation in TMEM; a 128-byte k-block holds 64 halves;
+//   * the query tile stays resident in shared memory when it fits
+//     (d <= 384); otherwise it is streamed with the database tile, one
+//     k-block of each per ring stage (d = 768 for config 2);
+//   * two epilogue warpgroups split each tile's 256 columns (the MMA of a
+//     d = 128 tile lasts only ~1k cycles); in list mode each keeps its own
+//     top-KP, written as two lists per (query, chunk) for the select stage.
+#include "epilogue.cuh"
+#include "kernels.cuh"
+#include "ptx.cuh"
+
+namespace mflat_cu {
+namespace {
+
+constexpr int kThreadsH = 320;                    // 8 epilogue warps + producer + MMA
+constexpr int kEpiThreadsH = 256;
+constexpr int kProducerWarpH = 8;
+constexpr int kMmaWarpH = 9;
+constexpr int kBKH = 64;                          // halves per 128-byte k-block
+constexpr int kATileBytesH = kBM * 128;           // 16 KB
+constexpr int kBTileBytesH = kBN * 128;           // 32 KB
+constexpr int kMaxStagesH = 6;
+constexpr int kSmemBudgetH = 7 * kBTileBytesH;    // 224 KB for A + ring
+constexpr int kMaxResidentKb = 6;                 // d_pad <= 384 keeps A resident
+
+__host__ __device__ inline bool a_streamed(int kb) { return kb > kMaxResidentKb; }
+__host__ __device__ inline int stage_bytes_h(int kb) {
+    return a_streamed(kb) ? kATileBytesH + kBTileBytesH : kBTileBytesH;
+}
+__host__ __device__ inline int n_stages_h(int kb) {
+    const int a = a_streamed(kb) ? 0 : kb * kATileBytesH;
+    const int s = (kSmemBudgetH - a) / stage_bytes_h(kb);
+    return s > kMaxStagesH ? kMaxStagesH : s;
+}
+
+struct SmemH {
+    uint8_t* a;         // resident A [kb][16 KB] (resident mode)
+    uint8_t* ring;      // [stages][stage bytes]: ([A 16 KB]) [B 32 KB]
+    uint64_t *full, *empty, *a_full, *a_empty, *acc_full, *acc_empty, *drain;
+    uint32_t* tmem_slot;
+    int* abort_flag;
+};
+
+__device__ inline SmemH carve_h(uint8_t* base, int kb, int stages) {
+    SmemH S;
+    S.a = base;
+    S.ring = base + (a_streamed(kb) ? 0 : kb * kATileBytesH);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(S.ring + stages * stage_bytes_h(kb));
+    S.full = bars;
+    S.empty = bars + kMaxStagesH;
+    S.a_full = bars + 2 * kMaxStagesH;
+    S.a_empty = S.a_full + 1;
+    S.acc_full = S.a_full + 2;
+    S.acc_empty = S.a_full + 4;
+    S.drain = S.a_full + 6;
+    S.tmem_slot = reinterpret_cast<uint32_t*>(S.a_full + 7);
+    S.abort_flag = reinterpret_cast<int*>(S.tmem_slot + 1);
+    return S;
+}
+
+template <int KP, bool kBuf, bool kBF16>
+__global__ void __launch_bounds__(kThreadsH, 1)
+screen_f16_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
+                  const ScreenParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* base = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    const int kb_count = p.d_pad / kBKH;
+    if (kb_count < 1 || kb_count * kBKH != p.d_pad) {
+        if (threadIdx.x == 0) atomicExch(p.err, kErrConfig);
+        return;
+    }
+    const bool stream_a = a_streamed(kb_count);
+    const int stages = n_stages_h(kb_count);
+    const int sbytes = stage_bytes_h(kb_count);
+    SmemH S = carve_h(base, kb_count, stages);
+    constexpr uint32_t kIdesc = make_idesc(kBF16 ? 1u : 0u, kBM, kBN);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kMaxStagesH; ++s) {
+            mbar_init(&S.full[s], 1);
+            mbar_init(&S.empty[s], 1);
+        }
+        mbar_init(S.a_full, 1);
+        mbar_init(S.a_empty, 1);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&S.acc_full[b], 1);
+            mbar_init(&S.acc_empty[b], kEpiThreadsH);
+        }
+        mbar_init(S.drain, 1);
+        *S.abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == kMmaWarpH) {
+        tmem_alloc(S.tmem_slot, 512);
+        tmem_relinquish();
+    }
+    if (warp == kProducerWarpH && lane == 0) {
+        tma_prefetch_desc(&tm_a);
+        tma_prefetch_desc(&tm_b);
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *S.tmem_slot;
+    volatile int* abort_flag = S.abort_flag;
+    const int n_units = p.n_qtiles * p.n_chunks;
+
+    if (warp == kProducerWarpH) {
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t sphase = 0, a_phase = 0;
+            uint32_t issued_mask = 0, issued_phase = 0;
+            bool a_issued = false;
+            uint32_t a_issue_phase = 0;
+            bool ok = true;
+            for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+                const int qt = u % p.n_qtiles;
+                const int ch = u / p.n_qtiles;
+                const int t0 = ch * p.tiles_per_chunk;
+                const int t1 = min(t0 + p.tiles_per_chunk, p.n_tiles);
+                if (!stream_a) {
+                    if (!mbar_wait(S.a_empty, a_phase ^ 1u, abort_flag)) { ok = false; break; }
+                    mbar_arrive_expect_tx(S.a_full, static_cast<uint32_t>(kb_count * kATileBytesH));
+                    for (int kb = 0; kb < kb_count; ++kb)
+                        tma_load_2d(&tm_a, S.a_full, S.a + kb * kATileBytesH, kb * kBKH, qt * kBM);
+                    a_issued = true;
+                    a_issue_phase = a_phase;
+                    a_phase ^= 1u;
+                }
+                for (int t = t0; t < t1 && ok; ++t) {
+                    for (int kb = 0; kb < kb_count; ++kb) {
+                        if (!mbar_wait(&S.empty[stage], sphase ^ 1u, abort_flag)) { ok = false; break; }
+                        uint8_t* st = S.ring + stage * sbytes;
+                        mbar_arrive_expect_tx(&S.full[stage], static_cast<uint32_t>(sbytes));
+                        if (stream_a) {
+                            tma_load_2d(&tm_a, &S.full[stage], st, kb * kBKH, qt * kBM);
+                            st += kATileBytesH;
+                        }
+                        tma_load_2d(&tm_b, &S.full[stage], st, kb * kBKH, t * p.tile_stride * kBN);
+                        issued_mask |= 1u << stage;
+                        issued_phase = (issued_phase & ~(1u << stage)) | (sphase << stage);
+                        if (++stage == stages) { stage = 0; sphase ^= 1u; }
+                    }
+                }
+            }
+            if (*abort_flag) {
+                for (int s = 0; s < stages; ++s)
+                    if (issued_mask & (1u << s))
+                        mbar_wait_drain(&S.full[s], (issued_phase >> s) & 1u, 200000000ull);
+                if (a_issued) mbar_wait_drain(S.a_full, a_issue_phase, 200000000ull);
+            }
+        }
+    } else if (warp == kMmaWarpH) {
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t sphase = 0, a_phase = 0, tcount = 0;
+            bool ok = true, issued_any = false;
+            for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+                const int ch = u / p.n_qtiles;
+                const int t0 = ch * p.tiles_per_chunk;
+                const int t1 = min(t0 + p.tiles_per_chunk, p.n_tiles);
+                if (!stream_a) {
+                    if (!mbar_wait(S.a_full, a_phase, abort_flag)) { ok = false; break; }
+                    a_phase ^= 1u;
+                    tc_fence_after();
+                }
+                for (int t = t0; t < t1 && ok; ++t, ++tcount) {
+                    const uint32_t b = tcount & 1u;
+                    const uint32_t ph = (tcount >> 1) & 1u;
+                    if (!mbar_wait(&S.acc_empty[b], ph ^ 1u, abort_flag)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t d_tmem = tmem_base + b * kBN;
+                    for (int kb = 0; kb < kb_count; ++kb) {
+                        if (!mbar_wait(&S.full[stage], sphase, abort_flag)) { ok = false; break; }
+                        tc_fence_after();
+                        const uint32_t st = smem_u32(S.ring + stage * sbytes);
+                        const uint64_t ad = smem_desc_k_sw128(
+                            stream_a ? st : smem_u32(S.a + kb * kATileBytesH));
+                        const uint64_t bd = smem_desc_k_sw128(stream_a ? st + kATileBytesH : st);
+#pragma unroll
+                        for (int ks = 0; ks < kBKH / 16; ++ks) {
+                            const uint64_t o = static_cast<uint64_t>(ks * 2);   // 32 B >> 4
+                            tc_mma_f16(d_tmem, ad + o, bd + o, kIdesc, (kb | ks) != 0 ? 1u : 0u);
+                        }
+                        issued_any = true;
+                        tc_commit(&S.empty[stage]);
+                        if (++stage == stages) { stage = 0; sphase ^= 1u; }
+                    }
+                    if (ok) tc_commit(&S.acc_full[b]);
+                }
+                if (ok && !stream_a) tc_commit(S.a_empty);
+            }
+            if (*abort_flag && issued_any) {
+                tc_commit(S.drain);
+                mbar_wait_drain(S.drain, 0u, 200000000ull);
+            }
+        }
+    } else {
+        // ---------------- epilogue: warpgroup g = warp / 4 owns columns [128g, 128g + 128)
+        const int g = warp >> 2;
+        const int wq = warp & 3;
+        const int row_in_tile = wq * 32 + lane;
+        const uint32_t lane_addr = tmem_base + (static_cast<uint32_t>(wq * 32) << 16);
+        uint32_t tcount = 0;
+        bool ok = true;
+        for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+            const int qt = u % p.n_qtiles;
+            const int ch = u / p.n_qtiles;
+            const int t0 = ch * p.tiles_per_chunk;
+            const int t1 = min(t0 + p.tiles_per_chunk, p.n_tiles);
+            const int row = qt * kBM + row_in_tile;
+            const bool live = row < p.m;
+            TopList<KP> L;
+            L.init();
+            BufferRow br{};
+            if constexpr (kBuf) {
+                const int rr = live ? row : 0;
+                br = BufferRow{p.buf_cnt + rr, p.buf_s + static_cast<int64_t>(rr) * p.cap,
+                               p.buf_i + static_cast<int64_t>(rr) * p.cap, p.cap};
+            }
+            for (int t = t0; t < t1; ++t, ++tcount) {
+                const uint32_t b = tcount & 1u;
+                const uint32_t ph = (tcount >> 1) & 1u;
+                if (!mbar_wait(&S.acc_full[b], ph, abort_flag)) { ok = false; break; }
+                const float floor_adj =
+                    !live ? __int_as_float(0x7f800000)
+                          : (p.use_floor ? floor_below(__ldcg(p.thr + row)) : -__int_as_float(0x7f800000));
+                const int id_tile = t * p.tile_stride * kBN + g * 128;
+                const float* cb_tile = p.colbias + id_tile;
+                const uint32_t taddr = lane_addr + b * kBN + g * 128;
+                __syncwarp();
+                tc_fence_after();
+#pragma unroll 1
+                for (int c = 0; c < 4; ++c) {
+                    uint32_t r[32];
+                    float4 cb[8];
+                    __syncwarp();
+                    tmem_ld_32x32b_x32(taddr + c * 32, r);
+                    load_bias(cb, cb_tile + c * 32);
+                    tmem_wait_ld_regs(r);
+                    if constexpr (kBuf) buffer_chunk(r, cb, p.alpha, floor_adj, br, id_tile + c * 32);
+                    else scan_chunk<KP>(r, cb, p.alpha, floor_adj, L, id_tile + c * 32);
+                }
+                __syncwarp();
+                tc_fence_before();
+                mbar_arrive(&S.acc_empty[b]);
+            }
+            if (!ok) break;
+            if (!kBuf && live) {
+                const int64_t o = (static_cast<int64_t>(ch * 2 + g) * p.m_pad + row) * KP;
+                float4* ps = reinterpret_cast<float4*>(p.part_score + o);
+                int4* pi = reinterpret_cast<int4*>(p.part_id + o);
+#pragma unroll
+                for (int i = 0; i < KP / 4; ++i) {
+                    ps[i] = make_float4(L.s[4 * i], L.s[4 * i + 1], L.s[4 * i + 2], L.s[4 * i + 3]);
+                    pi[i] = make_int4(L.id[4 * i], L.id[4 * i + 1], L.id[4 * i + 2], L.id[4 * i + 3]);
+                }
+                if (p.use_floor && L.id[KP - 1] >= 0) atomicMax(p.thr + row, score_key(L.s[KP - 1]));
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == kMmaWarpH) tmem_dealloc(tmem_base, 512);
+    if (threadIdx.x == 0 && *abort_flag) atomicExch(p.err, *abort_flag);
+}
+
+template <int KP, bool kBuf, bool kBF16>
+cudaError_t launch_h(const CUtensorMap& a, const CUtensorMap& b, const ScreenParams& p, int grid,
+                     cudaStream_t stream) {
+    const int smem = screen_f16_smem_bytes(p.d_pad);
+    cudaError_t e = cudaFuncSetAttribute(screen_f16_kernel<KP, kBuf, kBF16>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    screen_f16_kernel<KP, kBuf, kBF16><<<grid, kThreadsH, smem, stream>>>(a, b, p);
+    return cudaGetLastError();
+}
+
+template <bool kBF16>
+cudaError_t launch_h_kp(int kp, const CUtensorMap& a, const CUtensorMap& b, const ScreenParams& p,
+                        int grid, cudaStream_t stream) {
+    switch (kp) {
+        case 0: return launch_h<4, true, kBF16>(a, b, p, grid, stream);
+        case 4: return launch_h<4, false, kBF16>(a, b, p, grid, stream);
+        case 8: return launch_h<8, false, kBF16>(a, b, p, grid, stream);
+        case 16: return launch_h<16, false, kBF16>(a, b, p, grid, stream);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+}  // namespace
+
+int screen_f16_smem_bytes(int d_pad) {
+    const int kb = d_pad / kBKH;
+    const int a = a_streamed(kb) ? 0 : kb * kATileBytesH;
+    return 1024 + a + n_stages_h(kb) * stage_bytes_h(kb) + 256;
+}
+
+cudaError_t launch_screen_f16(int kp, bool bf16, const CUtensorMap& a, const CUtensorMap& b,
+                              const ScreenParams& p, int grid, cudaStream_t stream) {
+    if (p.d_pad % kBKH != 0 || p.d_pad < kBKH) return cudaErrorInvalidValue;
+    return bf16 ? launch_h_kp<true>(kp, a, b, p, grid, stream)
+                : launch_h_kp<false>(kp, a, b, p, grid, stream);
+}
+
+}  // namespace mflat_cu

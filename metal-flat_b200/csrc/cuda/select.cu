@@ -361,6 +361,39 @@ __global__ void __launch_bounds__(128) kmeans_fallback_kernel(const SelectParams
     }
 }
 
+// Recall path (fp16 / bf16 storage): the screen's scores are the answer.
+template <int KP>
+__global__ void __launch_bounds__(128) select_recall_kernel(const SelectParams p, const float* qsq) {
+    const int qi = blockIdx.x;
+    if (qi >= p.m) return;
+    __shared__ Cand red[33];
+    const int t = threadIdx.x;
+    int head = 0;
+    const int64_t base = (static_cast<int64_t>(t) * p.m_pad + qi) * KP;
+    const float empty = p.metric == kL2 ? __int_as_float(0x7f800000) : -__int_as_float(0x7f800000);
+    for (int r = 0; r < p.k_out; ++r) {
+        Cand c{-DBL_MAX, -1, t};
+        if (t < p.n_chunks && head < KP) {
+            c.s = p.part_score[base + head];
+            c.id = p.part_id[base + head];
+        }
+        const Cand w = block_best(c, red);
+        if (t == 0) {
+            const int64_t o = static_cast<int64_t>(qi) * p.k_out + r;
+            if (w.id >= 0) {
+                p.out_ids[o] = static_cast<int32_t>(w.id + p.id_base);
+                p.out_dist[o] = p.metric == kL2
+                                    ? fmaxf(0.0f, static_cast<float>(static_cast<double>(qsq[qi]) - w.s))
+                                    : static_cast<float>(w.s);
+            } else {
+                p.out_ids[o] = -1;
+                p.out_dist[o] = empty;
+            }
+        }
+        if (w.id >= 0 && w.owner == t) ++head;
+    }
+}
+
 template <int KP>
 cudaError_t launch_select_kp(const SelectParams& p, cudaStream_t stream) {
     select_exact_kernel<KP><<<p.m, 128, 0, stream>>>(p);
@@ -387,6 +420,17 @@ cudaError_t launch_kmeans_select(const SelectParams& p, int32_t* out, int grid_f
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     kmeans_fallback_kernel<<<grid_fallback, 128, 0, stream>>>(p, out);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_select_recall(int kp, const SelectParams& p, const float* qsq, cudaStream_t stream) {
+    if (p.n_chunks > kMaxChunks || p.n_chunks < 1 || p.k_out > kp) return cudaErrorInvalidValue;
+    switch (kp) {
+        case 4: select_recall_kernel<4><<<p.m, 128, 0, stream>>>(p, qsq); break;
+        case 8: select_recall_kernel<8><<<p.m, 128, 0, stream>>>(p, qsq); break;
+        case 16: select_recall_kernel<16><<<p.m, 128, 0, stream>>>(p, qsq); break;
+        default: return cudaErrorInvalidValue;
+    }
     return cudaGetLastError();
 }
 

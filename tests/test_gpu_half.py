@@ -1,0 +1,75 @@
+"""fp16 / bf16 storage (tcgen05 kind::f16 screen), through the C ABI.
+
+North-star criterion: recall@k >= 0.99 against the exact fp32-data oracle.
+Kernel check: on the 16-bit-rounded vectors themselves the result must equal
+the fp64 oracle's ids except inside near-ties (the screen accumulates in fp32,
+1e-4 relative window)."""
+import numpy as np
+import pytest
+import torch
+
+import mflat_b200 as M
+import oracle as O
+
+pytestmark = pytest.mark.gpu
+MET = {"l2": O.L2, "ip": O.IP, "cosine": O.COSINE}
+
+
+def rounded(a, storage, metric):
+    a = np.ascontiguousarray(a, np.float32)
+    if metric == "cosine":
+        a = O.normalize_rows(a)
+    t = torch.from_numpy(a).to(torch.bfloat16 if storage == "bf16" else torch.float16)
+    return t.float().numpy()
+
+
+def recall(got, ref):
+    hits = sum(len(set(g[g >= 0]) & set(r[r >= 0])) for g, r in zip(got, ref))
+    return hits / max(1, (ref >= 0).sum())
+
+
+def run(db, q, k, metric, storage):
+    idx = M.FlatIndex(db.shape[1], metric, storage)
+    idx.add(db)
+    return idx.search(q, k)
+
+
+CASES = [  # n, dim, m, k
+    (50_000, 128, 200, 10), (20_000, 96, 64, 16), (30_000, 768, 40, 4),
+    (40_000, 128, 50, 100), (300_000, 128, 16, 1024), (4_000, 33, 20, 40),
+]
+
+
+@pytest.mark.parametrize("storage", ["fp16", "bf16"])
+@pytest.mark.parametrize("metric", ["l2", "ip", "cosine"])
+@pytest.mark.parametrize("case", CASES, ids=lambda c: "n%d_d%d_m%d_k%d" % c)
+def test_half_storage(storage, metric, case):
+    n, dim, m, k = case
+    rng = np.random.default_rng(hash((storage, metric) + case) % 2**32)
+    db = rng.standard_normal((n, dim)).astype(np.float32)
+    q = rng.standard_normal((m, dim)).astype(np.float32)
+    ids, dist = run(db, q, k, metric, storage)
+    assert ids.shape == (m, k)
+    # kernel check on the rounded data (what the device stores)
+    dbr, qr = rounded(db, storage, metric), rounded(q, storage, metric)
+    ref_i, ref_d = O.flat_search_f64(dbr, qr, k + 1, O.IP if metric == "cosine" else MET[metric])
+    assert O.exact_ids_match(ids, dist, ref_i, ref_d, rel=1e-4) == 0
+    scale = np.maximum(np.abs(ref_d[:, :k]), 1e-3)
+    assert np.all(np.abs(dist - ref_d[:, :k]) <= 1e-4 * scale + 1e-3)
+    # north-star criterion against the fp32 data
+    tru_i, _ = O.flat_search_f64(db, q, k, MET[metric])
+    assert recall(ids, tru_i) >= 0.99
+
+
+def test_config2_like_mixture_fp16():
+    """BASELINE config 2 shape at reduced N: 1,000-component mixture (centres
+    N(0,1), sigma 0.3), L2-normalised, d = 768, inner product, k = 100."""
+    rng = np.random.default_rng(3)
+    centres = rng.standard_normal((1000, 768)).astype(np.float32)
+    def draw(n):
+        x = centres[rng.integers(0, 1000, size=n)] + 0.3 * rng.standard_normal((n, 768)).astype(np.float32)
+        return x / np.linalg.norm(x, axis=1, keepdims=True)
+    db, q = draw(100_000).astype(np.float32), draw(64).astype(np.float32)
+    ids, dist = run(db, q, 100, "ip", "fp16")
+    tru_i, _ = O.flat_search_f64(db, q, 100, O.IP)
+    assert recall(ids, tru_i) >= 0.99
