@@ -13,6 +13,9 @@
 
 #include <climits>
 #include <cmath>
+#include <map>
+#include <mutex>
+#include <utility>
 
 #include "index_impl.cuh"
 #include "kernels.cuh"
@@ -27,13 +30,25 @@ extern "C" int mflat_cu_kmeans_assign(const float* points, int64_t n, const floa
     if (n == 0) return ST_OK;
     if (!points || !centroids || !out_assign) return fail(ST_BAD_ARG, "null argument");
     if (n > INT_MAX - kBM) return fail(ST_BAD_ARG, "too many points for one call");
-    mflat_cu_index* ix = nullptr;
-    int rc = mflat_cu_index_create(device, dim, kL2, 0, &ix);
-    if (rc != ST_OK) return rc;
-    struct Free {
-        mflat_cu_index* p;
-        ~Free() { mflat_cu_index_destroy(p); }
-    } guard{ix};
+    // One assignment index per (device, dim), reused across calls so that
+    // repeated k-means iterations do not re-allocate their scratch; calls on
+    // the same device are serialised by the cache mutex.
+    device = mflat_cu_default_device(device);
+    static std::mutex cache_mu;
+    static std::map<std::pair<int, int>, mflat_cu_index*> cache;
+    std::lock_guard<std::mutex> lk(cache_mu);
+    mflat_cu_index*& ix = cache[{device, dim}];
+    int rc;
+    if (!ix) {
+        rc = mflat_cu_index_create(device, dim, kL2, 0, &ix);
+        if (rc != ST_OK) {
+            ix = nullptr;
+            return rc;
+        }
+    } else {
+        rc = mflat_cu_index_reset(ix);
+        if (rc != ST_OK) return rc;
+    }
     DeviceGuard g(ix->device);
     cudaStream_t st = on_device ? static_cast<cudaStream_t>(stream) : ix->stream;
     rc = mflat_cu_index_add(ix, centroids, ncentroids, on_device, stream);
@@ -78,7 +93,7 @@ extern "C" int mflat_cu_kmeans_assign(const float* points, int64_t n, const floa
         CU_TRY(cudaMemcpyAsync(out_assign, d_out, static_cast<size_t>(m) * sizeof(int32_t),
                                cudaMemcpyDeviceToHost, st),
                "download");
-    // The temporary index owns the scratch the kernels read: finish first.
+    // The cached index's scratch is reused by the next call: finish first.
     CU_TRY(cudaStreamSynchronize(st), "assignment");
     return check_device_error(ix);
 }
