@@ -270,8 +270,11 @@ def main():
     ap.add_argument("--n-db", type=int, default=None,
                     help="profiling only: smaller database (rows) for ncu captures")
     ap.add_argument("--n-q", type=int, default=None, help="profiling only: fewer queries")
+    ap.add_argument("--k", type=int, default=None, help="profiling only: other k")
     args = ap.parse_args()
     wl = Workload(CONFIGS[args.config], args.n_db, args.n_q)
+    if args.k:
+        wl.k = wl.cfg["k"] = args.k
     rank, world, local = dist_env()
     if args.impl == "reference":
         run_reference(args, wl, args.config, rank, world)

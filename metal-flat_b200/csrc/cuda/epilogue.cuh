@@ -9,6 +9,52 @@
 
 namespace mflat_cu {
 
+// Two fp32 FMAs in one instruction (sm_100 packed f32x2), each lane rounded
+// to nearest exactly like fmaf.
+__device__ __forceinline__ void ffma2(float a, float x0, float x1, float c0, float c1, float& d0,
+                                      float& d1) {
+    asm("{\n\t.reg .b64 ra, rx, rc, rd;\n\t"
+        "mov.b64 ra, {%2, %2};\n\t"
+        "mov.b64 rx, {%3, %4};\n\t"
+        "mov.b64 rc, {%5, %6};\n\t"
+        "fma.rn.f32x2 rd, ra, rx, rc;\n\t"
+        "mov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d0), "=f"(d1)
+        : "f"(a), "f"(x0), "f"(x1), "f"(c0), "f"(c1));
+}
+
+// Three-input fp32 maximum (one instruction on sm_100).
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+    float r;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
+
+// Maximum of 32 scores in 17 max instructions.
+__device__ __forceinline__ float max_tree32(const float (&sc)[32]) {
+    float t[11];
+#pragma unroll
+    for (int i = 0; i < 10; ++i) t[i] = max3f(sc[3 * i], sc[3 * i + 1], sc[3 * i + 2]);
+    t[10] = fmaxf(sc[30], sc[31]);
+    const float u0 = max3f(t[0], t[1], t[2]);
+    const float u1 = max3f(t[3], t[4], t[5]);
+    const float u2 = max3f(t[6], t[7], t[8]);
+    const float u3 = fmaxf(t[9], t[10]);
+    return fmaxf(max3f(u0, u1, u2), u3);
+}
+
+// s = alpha * acc + bias for 32 columns, as 16 packed FMAs.
+__device__ __forceinline__ void chunk_scores(const uint32_t (&r)[32], const float4 (&cb)[8],
+                                             float alpha, float (&sc)[32]) {
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+        ffma2(alpha, __uint_as_float(r[4 * q + 0]), __uint_as_float(r[4 * q + 1]), cb[q].x, cb[q].y,
+              sc[4 * q + 0], sc[4 * q + 1]);
+        ffma2(alpha, __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3]), cb[q].z, cb[q].w,
+              sc[4 * q + 2], sc[4 * q + 3]);
+    }
+}
+
 // Eight float4 of the per-row score bias for 32 columns.  Every lane of the
 // warp reads the same addresses (an L1 broadcast).
 __device__ __forceinline__ void load_bias(float4 (&cb)[8], const float* src) {
@@ -25,22 +71,8 @@ template <int KP>
 __device__ __forceinline__ void scan_chunk(const uint32_t (&r)[32], const float4 (&cb)[8],
                                            float alpha, float floor_adj, TopList<KP>& L, int id0) {
     float sc[32];
-#pragma unroll
-    for (int q = 0; q < 8; ++q) {
-        sc[4 * q + 0] = fmaf(alpha, __uint_as_float(r[4 * q + 0]), cb[q].x);
-        sc[4 * q + 1] = fmaf(alpha, __uint_as_float(r[4 * q + 1]), cb[q].y);
-        sc[4 * q + 2] = fmaf(alpha, __uint_as_float(r[4 * q + 2]), cb[q].z);
-        sc[4 * q + 3] = fmaf(alpha, __uint_as_float(r[4 * q + 3]), cb[q].w);
-    }
-    float m16[16];
-#pragma unroll
-    for (int i = 0; i < 16; ++i) m16[i] = fmaxf(sc[2 * i], sc[2 * i + 1]);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) m16[i] = fmaxf(m16[2 * i], m16[2 * i + 1]);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) m16[i] = fmaxf(m16[2 * i], m16[2 * i + 1]);
-    const float mx = fmaxf(fmaxf(m16[0], m16[1]), fmaxf(m16[2], m16[3]));
-    if (mx > fmaxf(L.worst(), floor_adj)) {
+    chunk_scores(r, cb, alpha, sc);
+    if (max_tree32(sc) > fmaxf(L.worst(), floor_adj)) {
         float tmp[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) tmp[j] = sc[j];
@@ -53,8 +85,11 @@ __device__ __forceinline__ void scan_chunk(const uint32_t (&r)[32], const float4
 }
 
 // Buffer mode: every score above the query's floor is appended to that
-// query's candidate buffer (slot from an atomic counter; slots past `cap` are
-// counted but not stored, so the select stage can detect an overflow).
+// query's candidate buffer (slots past `cap` are counted but not stored, so the
+// select stage can detect an overflow).  The passing columns of a chunk are
+// collected in a bit mask, one atomic reserves their slots, and a short loop
+// over the set bits writes them: a lane with a candidate costs one atomic per
+// chunk instead of one per element.
 struct BufferRow {
     uint32_t* cnt;
     float* s;
@@ -62,35 +97,59 @@ struct BufferRow {
     uint32_t cap;
 };
 
+__device__ __forceinline__ void append_passing(const float (&sc)[32], float floor_adj,
+                                               const BufferRow& br, int id0) {
+    uint32_t mask = 0;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) mask |= (sc[j] > floor_adj ? 1u : 0u) << j;
+    if (mask == 0u) return;
+    uint32_t slot = atomicAdd(br.cnt, static_cast<uint32_t>(__popc(mask)));
+    float tmp[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) tmp[j] = sc[j];
+    while (mask) {
+        const int j = __ffs(mask) - 1;
+        mask &= mask - 1u;
+        if (slot < br.cap) {
+            br.s[slot] = tmp[j];
+            br.id[slot] = id0 + j;
+        }
+        ++slot;
+    }
+}
+
 __device__ __forceinline__ void buffer_chunk(const uint32_t (&r)[32], const float4 (&cb)[8],
                                              float alpha, float floor_adj, const BufferRow& br,
                                              int id0) {
     float sc[32];
+    chunk_scores(r, cb, alpha, sc);
+    if (max_tree32(sc) > floor_adj) append_passing(sc, floor_adj, br, id0);
+}
+
+// Inner-product variant for chunks wholly inside the database: the bias is 0,
+// so the accumulator is the score (no bias load, no FFMA).
+__device__ __forceinline__ void buffer_chunk_raw(const uint32_t (&r)[32], float floor_adj,
+                                                 const BufferRow& br, int id0) {
+    float sc[32];
 #pragma unroll
-    for (int q = 0; q < 8; ++q) {
-        sc[4 * q + 0] = fmaf(alpha, __uint_as_float(r[4 * q + 0]), cb[q].x);
-        sc[4 * q + 1] = fmaf(alpha, __uint_as_float(r[4 * q + 1]), cb[q].y);
-        sc[4 * q + 2] = fmaf(alpha, __uint_as_float(r[4 * q + 2]), cb[q].z);
-        sc[4 * q + 3] = fmaf(alpha, __uint_as_float(r[4 * q + 3]), cb[q].w);
-    }
-    float m16[16];
+    for (int j = 0; j < 32; ++j) sc[j] = __uint_as_float(r[j]);
+    if (max_tree32(sc) > floor_adj) append_passing(sc, floor_adj, br, id0);
+}
+
+template <int KP>
+__device__ __forceinline__ void scan_chunk_raw(const uint32_t (&r)[32], float floor_adj,
+                                               TopList<KP>& L, int id0) {
+    float sc[32];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) m16[i] = fmaxf(sc[2 * i], sc[2 * i + 1]);
+    for (int j = 0; j < 32; ++j) sc[j] = __uint_as_float(r[j]);
+    if (max_tree32(sc) > fmaxf(L.worst(), floor_adj)) {
+        float tmp[32];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) m16[i] = fmaxf(m16[2 * i], m16[2 * i + 1]);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) m16[i] = fmaxf(m16[2 * i], m16[2 * i + 1]);
-    const float mx = fmaxf(fmaxf(m16[0], m16[1]), fmaxf(m16[2], m16[3]));
-    if (mx > floor_adj) {
-#pragma unroll
+        for (int j = 0; j < 32; ++j) tmp[j] = sc[j];
+#pragma unroll 1
         for (int j = 0; j < 32; ++j) {
-            if (sc[j] > floor_adj) {
-                const uint32_t slot = atomicAdd(br.cnt, 1u);
-                if (slot < br.cap) {
-                    br.s[slot] = sc[j];
-                    br.id[slot] = id0 + j;
-                }
-            }
+            const float v = tmp[j];
+            if (v > fmaxf(L.worst(), floor_adj)) L.insert(v, id0 + j);
         }
     }
 }

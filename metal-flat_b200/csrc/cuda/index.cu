@@ -495,15 +495,16 @@ struct LargePlan {
     int batch = 0;
 };
 
-LargePlan plan_large(int64_t n, int k, int m, int kp1) {
+// want: rank whose sampled score becomes the floor (2k exact path, k recall).
+LargePlan plan_large(int64_t n, int k, int m, int kp1, int want) {
     LargePlan P;
     const int n_tiles = static_cast<int>((n + kBN - 1) / kBN);
     if (n <= kAllRowsBuffered) {
         P.cap = static_cast<uint32_t>((n + 255) / 256 * 256);
     } else {
         P.prepass = true;
-        // union of lists * kp1 >= 4k sampled scores; floor = its 2k-th best
-        P.lists = std::min(4096 / kp1, std::max(1, (4 * k + kp1 - 1) / kp1));
+        // union of lists * kp1 >= 2 * want sampled scores; floor = its want-th best
+        P.lists = std::min(4096 / kp1, std::max(1, (2 * want + kp1 - 1) / kp1));
         P.stride = 16;
         while (P.stride > 1 && (n_tiles + P.stride - 1) / P.stride < 2 * P.lists) P.stride /= 2;
         P.sample_tiles = (n_tiles + P.stride - 1) / P.stride;
@@ -511,9 +512,9 @@ LargePlan plan_large(int64_t n, int k, int m, int kp1) {
             P.prepass = false;
             P.cap = static_cast<uint32_t>((n + 255) / 256 * 256);
         } else {
-            // the floor is the want-th best sampled score (want = 2k): about
-            // want * stride rows of the whole database score above it
-            const int64_t expect = static_cast<int64_t>(2) * k * P.stride;
+            // the floor is the want-th best sampled score: about want * stride
+            // rows of the whole database score above it
+            const int64_t expect = static_cast<int64_t>(want) * P.stride;
             int64_t cap = std::max<int64_t>(4 * expect, 4096);
             cap = std::min<int64_t>((cap + 255) / 256 * 256, (n + 255) / 256 * 256);
             P.cap = static_cast<uint32_t>(cap);
@@ -543,7 +544,7 @@ cudaError_t launch_pass(mflat_cu_index* ix, const ScreenParams& sp, int kp, cuda
 int search_large(mflat_cu_index* ix, const float* queries, int m, int k_out, int32_t* d_ids,
                  float* d_dist, int on_device, cudaStream_t st) {
     constexpr int kKP1 = 32;
-    const LargePlan P = plan_large(ix->n, k_out, m, kKP1);
+    const LargePlan P = plan_large(ix->n, k_out, m, kKP1, 2 * k_out);
     const int d_pad = ix->d_pad;
     const int n_tiles = static_cast<int>((ix->n + kBN - 1) / kBN);
     const float* qsrc = queries;
@@ -690,7 +691,7 @@ int search_half(mflat_cu_index* ix, const float* queries, int m, int k_out, int3
     if (list_mode) {
         P.batch = m;
     } else {
-        P = plan_large(ix->n, k_out, m, kKP1);
+        P = plan_large(ix->n, k_out, m, kKP1, k_out);
         // two lists (half tiles) per pre-pass chunk: halve the chunk count
         P.lists = std::max(1, (P.lists + 1) / 2);
     }

@@ -18,10 +18,12 @@
 namespace mflat_cu {
 namespace {
 
-constexpr int kThreadsH = 320;                    // 8 epilogue warps + producer + MMA
-constexpr int kEpiThreadsH = 256;
-constexpr int kProducerWarpH = 8;
-constexpr int kMmaWarpH = 9;
+// Epilogue warpgroups: 2 in list mode (per-thread lists need the registers),
+// 4 in buffer mode (4 warps per SMSP hide the TMEM-load / FMA latency of a
+// d = 128 tile, whose MMA lasts only ~1.5k cycles).  Producer and MMA warps
+// follow the epilogue warps.
+__host__ __device__ constexpr int epi_wg(bool buf) { return buf ? 4 : 2; }
+__host__ __device__ constexpr int threads_h(bool buf) { return epi_wg(buf) * 128 + 64; }
 constexpr int kBKH = 64;                          // halves per 128-byte k-block
 constexpr int kATileBytesH = kBM * 128;           // 16 KB
 constexpr int kBTileBytesH = kBN * 128;           // 32 KB
@@ -65,7 +67,7 @@ __device__ inline SmemH carve_h(uint8_t* base, int kb, int stages) {
 }
 
 template <int KP, bool kBuf, bool kBF16>
-__global__ void __launch_bounds__(kThreadsH, 1)
+__global__ void __launch_bounds__(threads_h(kBuf), 1)
 screen_f16_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                   const ScreenParams p) {
     extern __shared__ uint8_t smem_raw[];
@@ -82,6 +84,10 @@ screen_f16_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
     SmemH S = carve_h(base, kb_count, stages);
     constexpr uint32_t kIdesc = make_idesc(kBF16 ? 1u : 0u, kBM, kBN);
 
+    constexpr int kEpiWG = epi_wg(kBuf);
+    constexpr int kProducerWarpH = kEpiWG * 4;
+    constexpr int kMmaWarpH = kProducerWarpH + 1;
+    constexpr int kCols = kBN / kEpiWG;          // accumulator columns per warpgroup
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
@@ -93,7 +99,7 @@ screen_f16_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
         mbar_init(S.a_empty, 1);
         for (int b = 0; b < 2; ++b) {
             mbar_init(&S.acc_full[b], 1);
-            mbar_init(&S.acc_empty[b], kEpiThreadsH);
+            mbar_init(&S.acc_empty[b], kEpiWG * 128);
         }
         mbar_init(S.drain, 1);
         *S.abort_flag = 0;
@@ -205,7 +211,7 @@ screen_f16_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
             }
         }
     } else {
-        // ---------------- epilogue: warpgroup g = warp / 4 owns columns [128g, 128g + 128)
+        // ---------------- epilogue: warpgroup g = warp / 4 owns columns [g*kCols, (g+1)*kCols)
         const int g = warp >> 2;
         const int wq = warp & 3;
         const int row_in_tile = wq * 32 + lane;
@@ -230,25 +236,75 @@ screen_f16_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
             for (int t = t0; t < t1; ++t, ++tcount) {
                 const uint32_t b = tcount & 1u;
                 const uint32_t ph = (tcount >> 1) & 1u;
+                // issue the floor load and the next tile's bias prefetch before
+                // waiting, so their latency overlaps the accumulator wait
+                const uint32_t fkey = (live && p.use_floor) ? __ldcg(p.thr + row) : 0u;
+                if (lane < kCols / 32 && t + 1 < t1)
+                    prefetch_l1(p.colbias + static_cast<int64_t>(t + 1) * p.tile_stride * kBN +
+                                g * kCols + lane * 32);
                 if (!mbar_wait(&S.acc_full[b], ph, abort_flag)) { ok = false; break; }
                 const float floor_adj =
                     !live ? __int_as_float(0x7f800000)
-                          : (p.use_floor ? floor_below(__ldcg(p.thr + row)) : -__int_as_float(0x7f800000));
-                const int id_tile = t * p.tile_stride * kBN + g * 128;
+                          : (p.use_floor ? floor_below(fkey) : -__int_as_float(0x7f800000));
+                const int id_tile = t * p.tile_stride * kBN + g * kCols;
                 const float* cb_tile = p.colbias + id_tile;
-                const uint32_t taddr = lane_addr + b * kBN + g * 128;
-                __syncwarp();
-                tc_fence_after();
+                const uint32_t taddr = lane_addr + b * kBN + g * kCols;
+                // inner product on columns wholly inside the database: bias 0
+                const bool raw = p.alpha == 1.0f && static_cast<int64_t>(id_tile) + kCols <= p.n;
+                if constexpr (kEpiWG == 4) {
+                    // 4 warps per SMSP: one chunk at a time, latency hidden by
+                    // the other warps (keeps the thread within 112 registers)
+                    __syncwarp();
+                    tc_fence_after();
 #pragma unroll 1
-                for (int c = 0; c < 4; ++c) {
-                    uint32_t r[32];
+                    for (int c = 0; c < kCols / 32; ++c) {
+                        uint32_t r[32];
+                        float4 cb[8];
+                        __syncwarp();
+                        tmem_ld_32x32b_x32(taddr + c * 32, r);
+                        if (!raw) load_bias(cb, cb_tile + c * 32);
+                        tmem_wait_ld_regs(r);
+                        if constexpr (kBuf) {
+                            if (raw) buffer_chunk_raw(r, floor_adj, br, id_tile + c * 32);
+                            else buffer_chunk(r, cb, p.alpha, floor_adj, br, id_tile + c * 32);
+                        } else {
+                            if (raw) scan_chunk_raw<KP>(r, floor_adj, L, id_tile + c * 32);
+                            else scan_chunk<KP>(r, cb, p.alpha, floor_adj, L, id_tile + c * 32);
+                        }
+                    }
+                } else {
+                    uint32_t ra[32], rb[32];
                     float4 cb[8];
                     __syncwarp();
-                    tmem_ld_32x32b_x32(taddr + c * 32, r);
-                    load_bias(cb, cb_tile + c * 32);
-                    tmem_wait_ld_regs(r);
-                    if constexpr (kBuf) buffer_chunk(r, cb, p.alpha, floor_adj, br, id_tile + c * 32);
-                    else scan_chunk<KP>(r, cb, p.alpha, floor_adj, L, id_tile + c * 32);
+                    tc_fence_after();
+                    tmem_ld_32x32b_x32(taddr, ra);
+    #pragma unroll 1
+                    for (int c = 0; c < kCols / 32; c += 2) {
+                        if (!raw) load_bias(cb, cb_tile + c * 32);
+                        tmem_wait_ld_regs(ra);
+                        __syncwarp();
+                        tmem_ld_32x32b_x32(taddr + (c + 1) * 32, rb);
+                        if constexpr (kBuf) {
+                            if (raw) buffer_chunk_raw(ra, floor_adj, br, id_tile + c * 32);
+                            else buffer_chunk(ra, cb, p.alpha, floor_adj, br, id_tile + c * 32);
+                        } else {
+                            if (raw) scan_chunk_raw<KP>(ra, floor_adj, L, id_tile + c * 32);
+                            else scan_chunk<KP>(ra, cb, p.alpha, floor_adj, L, id_tile + c * 32);
+                        }
+                        if (!raw) load_bias(cb, cb_tile + (c + 1) * 32);
+                        tmem_wait_ld_regs(rb);
+                        if (c + 2 < kCols / 32) {
+                            __syncwarp();
+                            tmem_ld_32x32b_x32(taddr + (c + 2) * 32, ra);
+                        }
+                        if constexpr (kBuf) {
+                            if (raw) buffer_chunk_raw(rb, floor_adj, br, id_tile + (c + 1) * 32);
+                            else buffer_chunk(rb, cb, p.alpha, floor_adj, br, id_tile + (c + 1) * 32);
+                        } else {
+                            if (raw) scan_chunk_raw<KP>(rb, floor_adj, L, id_tile + (c + 1) * 32);
+                            else scan_chunk<KP>(rb, cb, p.alpha, floor_adj, L, id_tile + (c + 1) * 32);
+                        }
+                    }
                 }
                 __syncwarp();
                 tc_fence_before();
@@ -256,7 +312,7 @@ screen_f16_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
             }
             if (!ok) break;
             if (!kBuf && live) {
-                const int64_t o = (static_cast<int64_t>(ch * 2 + g) * p.m_pad + row) * KP;
+                const int64_t o = (static_cast<int64_t>(ch * kEpiWG + g) * p.m_pad + row) * KP;
                 float4* ps = reinterpret_cast<float4*>(p.part_score + o);
                 int4* pi = reinterpret_cast<int4*>(p.part_id + o);
 #pragma unroll
@@ -283,7 +339,7 @@ cudaError_t launch_h(const CUtensorMap& a, const CUtensorMap& b, const ScreenPar
     cudaError_t e = cudaFuncSetAttribute(screen_f16_kernel<KP, kBuf, kBF16>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
-    screen_f16_kernel<KP, kBuf, kBF16><<<grid, kThreadsH, smem, stream>>>(a, b, p);
+    screen_f16_kernel<KP, kBuf, kBF16><<<grid, threads_h(kBuf), smem, stream>>>(a, b, p);
     return cudaGetLastError();
 }
 

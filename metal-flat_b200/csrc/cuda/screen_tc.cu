@@ -261,11 +261,16 @@ screen_tf32x3_kernel(const __grid_constant__ CUtensorMap tm_a_hi,
             for (int t = t0; t < t1; ++t, ++tcount) {
                 const uint32_t b = tcount & 1u;
                 const uint32_t ph = (tcount >> 1) & 1u;
+                // floor published by finished units of the same query (monotone);
+                // its load and the next tile's bias prefetch are issued before
+                // the accumulator wait so their latency overlaps it
+                const uint32_t fkey = (live && p.use_floor) ? __ldcg(p.thr + row) : 0u;
+                if (lane < 8 && t + 1 < t1)
+                    prefetch_l1(p.colbias + static_cast<int64_t>(t + 1) * p.tile_stride * kBN + lane * 32);
                 if (!mbar_wait(&S.acc_full[b], ph, abort_flag)) { ok = false; break; }
-                // floor published by finished units of the same query (monotone)
                 const float floor_adj =
                     !live ? __int_as_float(0x7f800000)
-                          : (p.use_floor ? floor_below(__ldcg(p.thr + row)) : -__int_as_float(0x7f800000));
+                          : (p.use_floor ? floor_below(fkey) : -__int_as_float(0x7f800000));
                 const int id_tile = t * p.tile_stride * kBN;
                 const float* cb_tile = p.colbias + id_tile;
                 const uint32_t taddr = lane_addr + b * kBN;
