@@ -489,34 +489,48 @@ constexpr int64_t kAllRowsBuffered = 32768;        // below this, no pre-pass
 constexpr size_t kBufferBudget = size_t(6) << 30;  // bytes of candidate buffers
 
 struct LargePlan {
-    bool prepass = false;
-    int stride = 1, lists = 0, sample_tiles = 0;
+    bool prepass = false;          // floor estimate before the main pass
+    bool two_stage = false;        // stage A (list, sparse) + stage B (buffer, denser)
+    int lists = 0;                 // stage-A lists (chunks)
+    int stride_a = 1, sample_a = 0;
+    int stride_b = 1, sample_b = 0;
     uint32_t cap = 0;
     int batch = 0;
 };
 
 // want: rank whose sampled score becomes the floor (2k exact path, k recall).
-LargePlan plan_large(int64_t n, int k, int m, int kp1, int want) {
+// lists_per_chunk: lists one list-mode chunk produces (f16 kernel: 2).
+LargePlan plan_large(int64_t n, int k, int m, int kp1, int want, int lists_per_chunk) {
     LargePlan P;
     const int n_tiles = static_cast<int>((n + kBN - 1) / kBN);
+    const int64_t n_round = (n + 255) / 256 * 256;
     if (n <= kAllRowsBuffered) {
-        P.cap = static_cast<uint32_t>((n + 255) / 256 * 256);
+        P.cap = static_cast<uint32_t>(n_round);
     } else {
-        P.prepass = true;
         // union of lists * kp1 >= 2 * want sampled scores; floor = its want-th best
-        P.lists = std::min(4096 / kp1, std::max(1, (2 * want + kp1 - 1) / kp1));
-        P.stride = 16;
-        while (P.stride > 1 && (n_tiles + P.stride - 1) / P.stride < 2 * P.lists) P.stride /= 2;
-        P.sample_tiles = (n_tiles + P.stride - 1) / P.stride;
-        if (P.sample_tiles < P.lists) {                      // too small to sample: buffer all
-            P.prepass = false;
-            P.cap = static_cast<uint32_t>((n + 255) / 256 * 256);
+        const int lists_total = std::min(4096 / kp1, std::max(1, (2 * want + kp1 - 1) / kp1));
+        P.lists = std::max(1, (lists_total + lists_per_chunk - 1) / lists_per_chunk);
+        P.stride_b = 16;
+        while (P.stride_b > 1 && (n_tiles + P.stride_b - 1) / P.stride_b < 2 * P.lists) P.stride_b /= 2;
+        P.sample_b = (n_tiles + P.stride_b - 1) / P.stride_b;
+        if (P.sample_b < P.lists) {                      // too small to sample: buffer all
+            P.cap = static_cast<uint32_t>(n_round);
         } else {
-            // the floor is the want-th best sampled score: about want * stride
-            // rows of the whole database score above it
-            const int64_t expect = static_cast<int64_t>(want) * P.stride;
+            P.prepass = true;
+            P.stride_a = P.stride_b;
+            P.sample_a = P.sample_b;
+            // a list-mode pass over 1/256 of the tiles, then a buffer-mode pass
+            // over 1/stride_b sharpens its floor, when the sparse sample is big enough
+            if ((n_tiles + 255) / 256 >= 2 * P.lists && P.stride_b == 16) {
+                P.two_stage = true;
+                P.stride_a = 256;
+                P.sample_a = (n_tiles + 255) / 256;
+            }
+            // the floor is about the (want * stride_b)-th best row overall; the
+            // stage-B buffer holds about want * stride_a / stride_b rows
+            const int64_t expect = static_cast<int64_t>(want) * P.stride_b;
             int64_t cap = std::max<int64_t>(4 * expect, 4096);
-            cap = std::min<int64_t>((cap + 255) / 256 * 256, (n + 255) / 256 * 256);
+            cap = std::min<int64_t>((cap + 255) / 256 * 256, n_round);
             P.cap = static_cast<uint32_t>(cap);
         }
     }
@@ -524,6 +538,40 @@ LargePlan plan_large(int64_t n, int k, int m, int kp1, int want) {
     P.batch = static_cast<int>(std::max<size_t>(kBM, std::min<size_t>(m, kBufferBudget / per_q)));
     P.batch = std::min(P.batch, m);
     return P;
+}
+
+// Floor estimate for one query batch (see plan_large): stage A list-mode
+// pass + union select, then (two-stage plans) stage B buffer-mode pass + the
+// want-th best of each buffer.  list_pass / buffer_pass launch the storage's
+// screen kernel; `base` carries the batch's queries and buffers.
+template <class ListPass, class BufferPass>
+int estimate_floor(mflat_cu_index* ix, const LargePlan& P, const ScreenParams& base, int want,
+                   int kp1, int lists_per_chunk, ListPass list_pass, BufferPass buffer_pass,
+                   cudaStream_t st) {
+    ScreenParams pa = base;
+    pa.use_floor = 0;
+    pa.tile_stride = P.stride_a;
+    pa.n_tiles = P.sample_a;
+    pa.tiles_per_chunk = (P.sample_a + P.lists - 1) / P.lists;
+    pa.n_chunks = (P.sample_a + pa.tiles_per_chunk - 1) / pa.tiles_per_chunk;
+    CU_TRY(list_pass(pa, kp1), "floor pre-pass launch");
+    CU_TRY(launch_prepass_floor(pa.part_score, pa.part_id, pa.n_chunks * lists_per_chunk, base.m,
+                                base.m_pad, kp1, want, base.thr, st),
+           "floor launch");
+    if (!P.two_stage) return ST_OK;
+    ScreenParams pb = base;
+    pb.use_floor = 1;
+    pb.tile_stride = P.stride_b;
+    pb.n_tiles = P.sample_b;
+    int n_chunks = 1, tpc = P.sample_b;
+    plan_chunks(pb.n_qtiles, P.sample_b, ix->num_sms, kMaxChunks, n_chunks, tpc);
+    pb.n_chunks = n_chunks;
+    pb.tiles_per_chunk = tpc;
+    CU_TRY(cudaMemsetAsync(base.buf_cnt, 0, static_cast<size_t>(base.m_pad) * sizeof(uint32_t), st), "counts");
+    CU_TRY(buffer_pass(pb), "floor buffer pass launch");
+    CU_TRY(launch_buffer_floor(base.buf_cnt, base.buf_s, base.cap, want, base.m, base.thr, st),
+           "floor select launch");
+    return ST_OK;
 }
 
 cudaError_t launch_pass(mflat_cu_index* ix, const ScreenParams& sp, int kp, cudaStream_t st) {
@@ -544,7 +592,7 @@ cudaError_t launch_pass(mflat_cu_index* ix, const ScreenParams& sp, int kp, cuda
 int search_large(mflat_cu_index* ix, const float* queries, int m, int k_out, int32_t* d_ids,
                  float* d_dist, int on_device, cudaStream_t st) {
     constexpr int kKP1 = 32;
-    const LargePlan P = plan_large(ix->n, k_out, m, kKP1, 2 * k_out);
+    const LargePlan P = plan_large(ix->n, k_out, m, kKP1, 2 * k_out, 1);
     const int d_pad = ix->d_pad;
     const int n_tiles = static_cast<int>((ix->n + kBN - 1) / kBN);
     const float* qsrc = queries;
@@ -569,6 +617,9 @@ int search_large(mflat_cu_index* ix, const float* queries, int m, int k_out, int
         const size_t parts = static_cast<size_t>(P.lists) * bm_pad * kKP1;
         CU_TRY(ix->part_s.ensure(parts * sizeof(float)), "pre-pass lists");
         CU_TRY(ix->part_i.ensure(parts * sizeof(int32_t)), "pre-pass lists");
+    } else {
+        CU_TRY(ix->part_s.ensure(sizeof(float)), "pre-pass lists");
+        CU_TRY(ix->part_i.ensure(sizeof(int32_t)), "pre-pass lists");
     }
     int* words = ix->lk_words.as<int>();      // [0] overflow, [1] proof failures
     CU_TRY(cudaMemsetAsync(words, 0, 2 * sizeof(int), st), "status words");
@@ -599,19 +650,20 @@ int search_large(mflat_cu_index* ix, const float* queries, int m, int k_out, int
         sp.q_lo = ix->q_lo.as<float>();
         sp.db_hi = ix->db_hi;
         sp.db_lo = ix->db_lo;
+        sp.buf_cnt = ix->buf_cnt.as<uint32_t>();
+        sp.buf_s = ix->buf_s.as<float>();
+        sp.buf_i = ix->buf_i.as<int32_t>();
+        sp.cap = P.cap;
+        sp.part_score = ix->part_s.as<float>();
+        sp.part_id = ix->part_i.as<int32_t>();
         if (P.prepass) {
-            ScreenParams pp = sp;
-            pp.use_floor = 0;
-            pp.tile_stride = P.stride;
-            pp.n_tiles = P.sample_tiles;
-            pp.tiles_per_chunk = (P.sample_tiles + P.lists - 1) / P.lists;
-            pp.n_chunks = (P.sample_tiles + pp.tiles_per_chunk - 1) / pp.tiles_per_chunk;
-            pp.part_score = ix->part_s.as<float>();
-            pp.part_id = ix->part_i.as<int32_t>();
-            CU_TRY(launch_pass(ix, pp, kKP1, st), "floor pre-pass launch");
-            CU_TRY(launch_prepass_floor(pp.part_score, pp.part_id, pp.n_chunks, mb, mb_pad, kKP1,
-                                        2 * k_out, sp.thr, st),
-                   "floor launch");
+            const int rc = estimate_floor(
+                ix, P, sp, 2 * k_out, kKP1, 1,
+                [&](const ScreenParams& q, int kp) { return launch_pass(ix, q, kp, st); },
+                [&](const ScreenParams& q) { return launch_pass(ix, q, 0, st); }, st);
+            if (rc != ST_OK) return rc;
+            CU_TRY(cudaMemsetAsync(ix->buf_cnt.p, 0, static_cast<size_t>(mb_pad) * sizeof(uint32_t), st),
+                   "counts");
         }
         sp.use_floor = 1;
         sp.tile_stride = 1;
@@ -663,7 +715,7 @@ int search_large(mflat_cu_index* ix, const float* queries, int m, int k_out, int
     if (ix->host_words[2] > 0) return fail(ST_INTERNAL, "candidate buffer overflow (too many rows tie with the k-th best)");
     if (ix->host_words[3] > 0) return fail(ST_INTERNAL, "exactness could not be proven for some queries (near-ties)");
     ix->last.screen_launches = 1;
-    ix->last.launches = (P.prepass ? 5 : 3) * ((m + P.batch - 1) / P.batch);
+    ix->last.launches = (P.prepass ? (P.two_stage ? 7 : 5) : 3) * ((m + P.batch - 1) / P.batch);
     return ST_OK;
 }
 
@@ -691,9 +743,7 @@ int search_half(mflat_cu_index* ix, const float* queries, int m, int k_out, int3
     if (list_mode) {
         P.batch = m;
     } else {
-        P = plan_large(ix->n, k_out, m, kKP1, k_out);
-        // two lists (half tiles) per pre-pass chunk: halve the chunk count
-        P.lists = std::max(1, (P.lists + 1) / 2);
+        P = plan_large(ix->n, k_out, m, kKP1, k_out, 2);   // two lists (column halves) per chunk
     }
     const int bm_pad = (P.batch + kBM - 1) / kBM * kBM;
     CU_TRY(ix->q16.ensure(static_cast<size_t>(bm_pad) * d_pad * 2), "query conversion");
@@ -767,19 +817,17 @@ int search_half(mflat_cu_index* ix, const float* queries, int m, int k_out, int3
             CU_TRY(launch_select_recall(kp, sel, ix->qsq.as<float>(), st), "select launch");
             continue;
         }
-        CU_TRY(cudaMemsetAsync(ix->buf_cnt.p, 0, static_cast<size_t>(mb_pad) * sizeof(uint32_t), st), "counts");
+        sp.buf_cnt = ix->buf_cnt.as<uint32_t>();
+        sp.buf_s = ix->buf_s.as<float>();
+        sp.buf_i = ix->buf_i.as<int32_t>();
+        sp.cap = P.cap;
         if (P.prepass) {
-            ScreenParams pp = sp;
-            pp.use_floor = 0;
-            pp.tile_stride = P.stride;
-            pp.n_tiles = P.sample_tiles;
-            pp.tiles_per_chunk = (P.sample_tiles + P.lists - 1) / P.lists;
-            pp.n_chunks = (P.sample_tiles + pp.tiles_per_chunk - 1) / pp.tiles_per_chunk;
-            CU_TRY(launch(pp, kKP1), "floor pre-pass launch");
-            CU_TRY(launch_prepass_floor(pp.part_score, pp.part_id, 2 * pp.n_chunks, mb, mb_pad, kKP1,
-                                        k_out, sp.thr, st),
-                   "floor launch");
+            const int rc = estimate_floor(
+                ix, P, sp, k_out, kKP1, 2, [&](const ScreenParams& q, int kpp) { return launch(q, kpp); },
+                [&](const ScreenParams& q) { return launch(q, 0); }, st);
+            if (rc != ST_OK) return rc;
         }
+        CU_TRY(cudaMemsetAsync(ix->buf_cnt.p, 0, static_cast<size_t>(mb_pad) * sizeof(uint32_t), st), "counts");
         sp.use_floor = 1;
         sp.tile_stride = 1;
         sp.n_tiles = n_tiles;
@@ -816,7 +864,7 @@ int search_half(mflat_cu_index* ix, const float* queries, int m, int k_out, int3
     }
     if (ix->timing) cudaEventRecord(ix->ev[3], st);
     ix->last.screen_launches = 1;
-    ix->last.launches = list_mode ? 3 : (P.prepass ? 5 : 3);
+    ix->last.launches = list_mode ? 3 : (P.prepass ? (P.two_stage ? 7 : 5) : 3);
     if (!list_mode) {
         CU_TRY(cudaMemcpyAsync(&ix->host_words[2], ix->lk_words.p, 2 * sizeof(int), cudaMemcpyDeviceToHost, st),
                "status");

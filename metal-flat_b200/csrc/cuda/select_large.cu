@@ -296,7 +296,33 @@ __global__ void __launch_bounds__(256) prepass_floor_kernel(const float* __restr
     if (threadIdx.x == 0) thr[q] = sh_prefix;
 }
 
+// Sharper floor from a buffer-mode pass over a sample: the want-th best score
+// among the rows the query's buffer kept (real rows, at or above the previous
+// floor) is met by `want` rows, hence <= the global want-th best.  That holds
+// for any subset, so an overflowed buffer (the first `cap` appends) still
+// gives a valid floor.  Leaves thr unchanged when fewer than `want` were kept.
+__global__ void __launch_bounds__(512) buffer_floor_kernel(const uint32_t* __restrict__ cnt,
+                                                           const float* __restrict__ buf_s, uint32_t cap,
+                                                           int want, int m, uint32_t* thr) {
+    const int q = blockIdx.x;
+    if (q >= m) return;
+    __shared__ uint32_t hist[256];
+    __shared__ uint32_t sh_prefix;
+    __shared__ int sh_remaining;
+    const uint32_t n = min(cnt[q], cap);
+    if (n < static_cast<uint32_t>(want)) return;
+    radix_select(buf_s + static_cast<int64_t>(q) * cap, static_cast<int>(n), want, hist, &sh_prefix,
+                 &sh_remaining);
+    if (threadIdx.x == 0 && sh_prefix > thr[q]) thr[q] = sh_prefix;
+}
+
 }  // namespace
+
+cudaError_t launch_buffer_floor(const uint32_t* cnt, const float* buf_s, uint32_t cap, int want, int m,
+                                uint32_t* thr, cudaStream_t stream) {
+    buffer_floor_kernel<<<m, 512, 0, stream>>>(cnt, buf_s, cap, want, m, thr);
+    return cudaGetLastError();
+}
 
 cudaError_t launch_select_large(const LargeSelectParams& p, cudaStream_t stream) {
     if (p.k_out < 1 || p.k_out > kSelMax) return cudaErrorInvalidValue;

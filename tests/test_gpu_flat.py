@@ -188,9 +188,11 @@ def test_device_pointer_api():
     assert_exact(d_ids.cpu().numpy(), d_dist.cpu().numpy(), db, q, 10, "ip")
 
 
-LARGE = [  # n, dim, m, k   (n <= 32768: every row buffered; larger: floor pre-pass)
+LARGE = [  # n, dim, m, k   (n <= 32768: every row buffered; larger: floor pre-pass;
+           #                 n >= 2M at these k: two-stage floor, sparse lists then a buffer pass)
     (3000, 40, 30, 22), (3000, 128, 17, 300), (150_000, 128, 40, 64),
     (150_000, 64, 33, 1024), (200_003, 17, 20, 100), (60_000, 160, 9, 50),
+    (2_000_000, 64, 12, 100), (2_100_001, 20, 9, 22),
 ]
 
 
@@ -203,6 +205,16 @@ def test_large_k_exact(metric, shape):
     q = rng.standard_normal((m, dim)).astype(np.float32)
     ids, dist = search(db, q, k, metric)
     assert_exact(ids, dist, db, q, k, metric)
+
+
+def test_large_k_two_stage_floor_k1024():
+    """17M rows at k = 1024: the floor comes from lists over 1/256 of the tiles,
+    sharpened by a buffer pass over 1/16 of them, before the full pass."""
+    rng = np.random.default_rng(zlib.crc32(b"two-stage-1024"))
+    db = rng.standard_normal((17_000_000, 8), dtype=np.float32)
+    q = rng.standard_normal((6, 8), dtype=np.float32)
+    ids, dist = search(db, q, 1024, "l2")
+    assert_exact(ids, dist, db, q, 1024, "l2")
 
 
 def test_large_k_clamp_and_uniform():

@@ -39,6 +39,7 @@ def run(db, q, k, metric, storage):
 CASES = [  # n, dim, m, k
     (50_000, 128, 200, 10), (20_000, 96, 64, 16), (30_000, 768, 40, 4),
     (40_000, 128, 50, 100), (300_000, 128, 16, 1024), (4_000, 33, 20, 40),
+    (1_000_000, 64, 12, 100),   # two-stage floor (sparse lists, then a buffer pass)
 ]
 
 
