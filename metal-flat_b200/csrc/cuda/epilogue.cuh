@@ -63,33 +63,69 @@ __device__ __forceinline__ void load_bias(float4 (&cb)[8], const float* src) {
     for (int q = 0; q < 8; ++q) cb[q] = __ldg(s4 + q);
 }
 
-// Scores of one 32-column chunk: s = alpha * dot + bias.  Hot path: 32 FFMA
-// and a 31-FMNMX max tree, one compare.  Only when some score beats the gate
-// (the list's worst entry or the published floor) are the scores spilled to
-// a small local array and inserted one by one, in ascending id order.
+// Bit mask of the columns scoring above `gate` (slow paths only).  The eight
+// 4-column groups are screened by their maxima (recomputed here rather than
+// kept live from the hot path's tree) and only passing groups are compared
+// column by column.
+__device__ __forceinline__ uint32_t passing_mask(const float (&sc)[32], float gate) {
+    uint32_t mask = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        if (fmaxf(max3f(sc[4 * i], sc[4 * i + 1], sc[4 * i + 2]), sc[4 * i + 3]) > gate) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) mask |= (sc[4 * i + e] > gate ? 1u : 0u) << (4 * i + e);
+        }
+    }
+    return mask;
+}
+
+// sc[j] for a run-time j, as a 5-level select tree over registers (a dynamic
+// index into a register array would place it in local memory).
+__device__ __forceinline__ float select32(const float (&sc)[32], uint32_t j) {
+    float a[16], b[8], c[4], d[2];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) a[i] = (j & 1u) ? sc[2 * i + 1] : sc[2 * i];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) b[i] = (j & 2u) ? a[2 * i + 1] : a[2 * i];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) c[i] = (j & 4u) ? b[2 * i + 1] : b[2 * i];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) d[i] = (j & 8u) ? c[2 * i + 1] : c[2 * i];
+    return (j & 16u) ? d[1] : d[0];
+}
+
+// List mode, slow path: insert the columns beating the gate (the list's worst
+// entry or the published floor) in ascending id order, re-testing each
+// against the raised gate.  One copy of the insertion network.
+template <int KP>
+__device__ __forceinline__ void insert_passing(const float (&sc)[32], float floor_adj, TopList<KP>& L,
+                                               int id0) {
+    uint32_t mask = passing_mask(sc, fmaxf(L.worst(), floor_adj));
+#pragma unroll 1
+    while (mask) {
+        const uint32_t j = __ffs(mask) - 1;
+        mask &= mask - 1u;
+        const float v = select32(sc, j);
+        if (v > fmaxf(L.worst(), floor_adj)) L.insert(v, id0 + static_cast<int>(j));
+    }
+}
+
+// Scores of one 32-column chunk: s = alpha * dot + bias.  Hot path: 16 packed
+// FMAs, a 17-instruction max tree and one compare; the slow path runs only
+// when some score beats the gate.
 template <int KP>
 __device__ __forceinline__ void scan_chunk(const uint32_t (&r)[32], const float4 (&cb)[8],
                                            float alpha, float floor_adj, TopList<KP>& L, int id0) {
     float sc[32];
     chunk_scores(r, cb, alpha, sc);
-    if (max_tree32(sc) > fmaxf(L.worst(), floor_adj)) {
-        float tmp[32];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) tmp[j] = sc[j];
-#pragma unroll 1
-        for (int j = 0; j < 32; ++j) {
-            const float v = tmp[j];
-            if (v > fmaxf(L.worst(), floor_adj)) L.insert(v, id0 + j);
-        }
-    }
+    if (max_tree32(sc) > fmaxf(L.worst(), floor_adj)) insert_passing<KP>(sc, floor_adj, L, id0);
 }
 
 // Buffer mode: every score above the query's floor is appended to that
 // query's candidate buffer (slots past `cap` are counted but not stored, so the
 // select stage can detect an overflow).  The passing columns of a chunk are
-// collected in a bit mask, one atomic reserves their slots, and a short loop
-// over the set bits writes them: a lane with a candidate costs one atomic per
-// chunk instead of one per element.
+// found group-wise, one atomic reserves their slots, and the passing groups
+// are visited again to write them, all from registers.
 struct BufferRow {
     uint32_t* cnt;
     float* s;
@@ -99,22 +135,23 @@ struct BufferRow {
 
 __device__ __forceinline__ void append_passing(const float (&sc)[32], float floor_adj,
                                                const BufferRow& br, int id0) {
-    uint32_t mask = 0;
-#pragma unroll
-    for (int j = 0; j < 32; ++j) mask |= (sc[j] > floor_adj ? 1u : 0u) << j;
-    if (mask == 0u) return;
+    const uint32_t mask = passing_mask(sc, floor_adj);
     uint32_t slot = atomicAdd(br.cnt, static_cast<uint32_t>(__popc(mask)));
-    float tmp[32];
 #pragma unroll
-    for (int j = 0; j < 32; ++j) tmp[j] = sc[j];
-    while (mask) {
-        const int j = __ffs(mask) - 1;
-        mask &= mask - 1u;
-        if (slot < br.cap) {
-            br.s[slot] = tmp[j];
-            br.id[slot] = id0 + j;
+    for (int i = 0; i < 8; ++i) {
+        if ((mask >> (4 * i)) & 0xFu) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int j = 4 * i + e;
+                if ((mask >> j) & 1u) {
+                    if (slot < br.cap) {
+                        br.s[slot] = sc[j];
+                        br.id[slot] = id0 + j;
+                    }
+                    ++slot;
+                }
+            }
         }
-        ++slot;
     }
 }
 
@@ -142,16 +179,7 @@ __device__ __forceinline__ void scan_chunk_raw(const uint32_t (&r)[32], float fl
     float sc[32];
 #pragma unroll
     for (int j = 0; j < 32; ++j) sc[j] = __uint_as_float(r[j]);
-    if (max_tree32(sc) > fmaxf(L.worst(), floor_adj)) {
-        float tmp[32];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) tmp[j] = sc[j];
-#pragma unroll 1
-        for (int j = 0; j < 32; ++j) {
-            const float v = tmp[j];
-            if (v > fmaxf(L.worst(), floor_adj)) L.insert(v, id0 + j);
-        }
-    }
+    if (max_tree32(sc) > fmaxf(L.worst(), floor_adj)) insert_passing<KP>(sc, floor_adj, L, id0);
 }
 
 }  // namespace mflat_cu

@@ -233,12 +233,15 @@ screen_f16_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
                 br = BufferRow{p.buf_cnt + rr, p.buf_s + static_cast<int64_t>(rr) * p.cap,
                                p.buf_i + static_cast<int64_t>(rr) * p.cap, p.cap};
             }
+            // Score floor: fixed during a buffer pass (one load per unit); in list
+            // mode raised by finished units (monotone), reloaded one tile ahead.
+            uint32_t fkey_next = (live && p.use_floor) ? __ldcg(p.thr + row) : 0u;
             for (int t = t0; t < t1; ++t, ++tcount) {
                 const uint32_t b = tcount & 1u;
                 const uint32_t ph = (tcount >> 1) & 1u;
-                // issue the floor load and the next tile's bias prefetch before
-                // waiting, so their latency overlaps the accumulator wait
-                const uint32_t fkey = (live && p.use_floor) ? __ldcg(p.thr + row) : 0u;
+                const uint32_t fkey = fkey_next;
+                if (!kBuf && live && p.use_floor && t + 1 < t1) fkey_next = __ldcg(p.thr + row);
+                // the next tile's bias prefetch overlaps the accumulator wait
                 if (lane < kCols / 32 && t + 1 < t1)
                     prefetch_l1(p.colbias + static_cast<int64_t>(t + 1) * p.tile_stride * kBN +
                                 g * kCols + lane * 32);

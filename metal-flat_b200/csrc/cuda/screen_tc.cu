@@ -258,13 +258,18 @@ screen_tf32x3_kernel(const __grid_constant__ CUtensorMap tm_a_hi,
                 br = BufferRow{p.buf_cnt + rr, p.buf_s + static_cast<int64_t>(rr) * p.cap,
                                p.buf_i + static_cast<int64_t>(rr) * p.cap, p.cap};
             }
+            // Score floor of the query.  A buffer pass reads a floor fixed before
+            // the launch: one load per unit.  In list mode finished units of the
+            // same query raise it (monotone), so any earlier value is a valid
+            // bound: it is reloaded one tile ahead, keeping the load's latency off
+            // the tile loop.
+            uint32_t fkey_next = (live && p.use_floor) ? __ldcg(p.thr + row) : 0u;
             for (int t = t0; t < t1; ++t, ++tcount) {
                 const uint32_t b = tcount & 1u;
                 const uint32_t ph = (tcount >> 1) & 1u;
-                // floor published by finished units of the same query (monotone);
-                // its load and the next tile's bias prefetch are issued before
-                // the accumulator wait so their latency overlaps it
-                const uint32_t fkey = (live && p.use_floor) ? __ldcg(p.thr + row) : 0u;
+                const uint32_t fkey = fkey_next;
+                if (!kBuf && live && p.use_floor && t + 1 < t1) fkey_next = __ldcg(p.thr + row);
+                // the next tile's bias prefetch overlaps the accumulator wait
                 if (lane < 8 && t + 1 < t1)
                     prefetch_l1(p.colbias + static_cast<int64_t>(t + 1) * p.tile_stride * kBN + lane * 32);
                 if (!mbar_wait(&S.acc_full[b], ph, abort_flag)) { ok = false; break; }
