@@ -736,7 +736,13 @@ int search_half(mflat_cu_index* ix, const float* queries, int m, int k_out, int3
                "query upload");
         qsrc = ix->q_in.as<float>();
     }
-    const bool list_mode = k_out <= 16;
+    // Small k on a small problem: per-(query, chunk) top lists (one launch
+    // pair, no floor estimate).  Otherwise the
+    // buffer path (floor estimate, then append above the floor), whose 4
+    // epilogue warpgroups keep up with the d = 128 MMA better than the 2 that
+    // per-thread lists leave room for.
+    const bool list_mode =
+        k_out <= 16 && (ix->n <= kAllRowsBuffered || static_cast<double>(m) * ix->n <= 8e8);
     const int kp = k_out <= 4 ? 4 : (k_out <= 8 ? 8 : 16);
     constexpr int kKP1 = 16;
     LargePlan P;
