@@ -494,13 +494,14 @@ struct LargePlan {
     int lists = 0;                 // stage-A lists (chunks)
     int stride_a = 1, sample_a = 0;
     int stride_b = 1, sample_b = 0;
+    int chunks_a = 0, tpc_a = 0;   // stage-A chunking (>= lists, spread over the SMs)
     uint32_t cap = 0;
     int batch = 0;
 };
 
 // want: rank whose sampled score becomes the floor (2k exact path, k recall).
 // lists_per_chunk: lists one list-mode chunk produces (f16 kernel: 2).
-LargePlan plan_large(int64_t n, int k, int m, int kp1, int want, int lists_per_chunk) {
+LargePlan plan_large(int64_t n, int k, int m, int kp1, int want, int lists_per_chunk, int num_sms) {
     LargePlan P;
     const int n_tiles = static_cast<int>((n + kBN - 1) / kBN);
     const int64_t n_round = (n + 255) / 256 * 256;
@@ -537,6 +538,18 @@ LargePlan plan_large(int64_t n, int k, int m, int kp1, int want, int lists_per_c
     const size_t per_q = static_cast<size_t>(P.cap) * 8 + 64;
     P.batch = static_cast<int>(std::max<size_t>(kBM, std::min<size_t>(m, kBufferBudget / per_q)));
     P.batch = std::min(P.batch, m);
+    if (P.prepass) {
+        // Stage A needs >= `lists` chunks for its union; more chunks only enlarge
+        // the union (a sharper floor) and keep every SM busy when few query
+        // tiles share the pass.
+        const int n_qt = (P.batch + kBM - 1) / kBM;
+        const int max_a = std::max(P.lists, kFloorMaxEntries / (kp1 * lists_per_chunk));
+        plan_chunks(n_qt, P.sample_a, num_sms, max_a, P.chunks_a, P.tpc_a);
+        if (P.chunks_a < P.lists) {
+            P.tpc_a = (P.sample_a + P.lists - 1) / P.lists;
+            P.chunks_a = (P.sample_a + P.tpc_a - 1) / P.tpc_a;
+        }
+    }
     return P;
 }
 
@@ -552,8 +565,8 @@ int estimate_floor(mflat_cu_index* ix, const LargePlan& P, const ScreenParams& b
     pa.use_floor = 0;
     pa.tile_stride = P.stride_a;
     pa.n_tiles = P.sample_a;
-    pa.tiles_per_chunk = (P.sample_a + P.lists - 1) / P.lists;
-    pa.n_chunks = (P.sample_a + pa.tiles_per_chunk - 1) / pa.tiles_per_chunk;
+    pa.tiles_per_chunk = P.tpc_a;
+    pa.n_chunks = P.chunks_a;
     CU_TRY(list_pass(pa, kp1), "floor pre-pass launch");
     CU_TRY(launch_prepass_floor(pa.part_score, pa.part_id, pa.n_chunks * lists_per_chunk, base.m,
                                 base.m_pad, kp1, want, base.thr, st),
@@ -592,7 +605,7 @@ cudaError_t launch_pass(mflat_cu_index* ix, const ScreenParams& sp, int kp, cuda
 int search_large(mflat_cu_index* ix, const float* queries, int m, int k_out, int32_t* d_ids,
                  float* d_dist, int on_device, cudaStream_t st) {
     constexpr int kKP1 = 32;
-    const LargePlan P = plan_large(ix->n, k_out, m, kKP1, 2 * k_out, 1);
+    const LargePlan P = plan_large(ix->n, k_out, m, kKP1, 2 * k_out, 1, ix->num_sms);
     const int d_pad = ix->d_pad;
     const int n_tiles = static_cast<int>((ix->n + kBN - 1) / kBN);
     const float* qsrc = queries;
@@ -614,7 +627,7 @@ int search_large(mflat_cu_index* ix, const float* queries, int m, int k_out, int
     CU_TRY(ix->flag_list.ensure(static_cast<size_t>(bm_pad) * sizeof(int)), "flag list");
     CU_TRY(ix->lk_words.ensure(2 * sizeof(int)), "status words");
     if (P.prepass) {
-        const size_t parts = static_cast<size_t>(P.lists) * bm_pad * kKP1;
+        const size_t parts = static_cast<size_t>(P.chunks_a) * bm_pad * kKP1;
         CU_TRY(ix->part_s.ensure(parts * sizeof(float)), "pre-pass lists");
         CU_TRY(ix->part_i.ensure(parts * sizeof(int32_t)), "pre-pass lists");
     } else {
@@ -749,7 +762,7 @@ int search_half(mflat_cu_index* ix, const float* queries, int m, int k_out, int3
     if (list_mode) {
         P.batch = m;
     } else {
-        P = plan_large(ix->n, k_out, m, kKP1, k_out, 2);   // two lists (column halves) per chunk
+        P = plan_large(ix->n, k_out, m, kKP1, k_out, 2, ix->num_sms);   // two lists (column halves) per chunk
     }
     const int bm_pad = (P.batch + kBM - 1) / kBM * kBM;
     CU_TRY(ix->q16.ensure(static_cast<size_t>(bm_pad) * d_pad * 2), "query conversion");
@@ -762,7 +775,7 @@ int search_half(mflat_cu_index* ix, const float* queries, int m, int k_out, int3
         CU_TRY(ix->lk_words.ensure(2 * sizeof(int)), "status words");
         CU_TRY(cudaMemsetAsync(ix->lk_words.p, 0, 2 * sizeof(int), st), "status words");
     }
-    const int max_lists = list_mode ? kMaxChunks / 2 : P.lists;
+    const int max_lists = list_mode ? kMaxChunks / 2 : P.chunks_a;
     const int lk = list_mode ? kp : kKP1;
     const size_t parts = static_cast<size_t>(2 * std::max(max_lists, 1)) * bm_pad * lk;
     CU_TRY(ix->part_s.ensure(parts * sizeof(float)), "candidate lists");

@@ -89,7 +89,7 @@ __device__ __forceinline__ double exact_score(int metric, const float* qh, const
 }
 
 template <int KP>
-__global__ void __launch_bounds__(128) select_exact_kernel(const SelectParams p) {
+__global__ void __launch_bounds__(kSelectMaxThreads) select_exact_kernel(const SelectParams p) {
     const int qi = blockIdx.x;
     if (qi >= p.m) return;
     __shared__ Cand red[33];
@@ -363,7 +363,7 @@ __global__ void __launch_bounds__(128) kmeans_fallback_kernel(const SelectParams
 
 // Recall path (fp16 / bf16 storage): the screen's scores are the answer.
 template <int KP>
-__global__ void __launch_bounds__(128) select_recall_kernel(const SelectParams p, const float* qsq) {
+__global__ void __launch_bounds__(kSelectMaxThreads) select_recall_kernel(const SelectParams p, const float* qsq) {
     const int qi = blockIdx.x;
     if (qi >= p.m) return;
     __shared__ Cand red[33];
@@ -394,9 +394,12 @@ __global__ void __launch_bounds__(128) select_recall_kernel(const SelectParams p
     }
 }
 
+// One thread per candidate list in the tournament merge.
+inline int select_threads(int n_lists) { return n_lists > 128 ? kSelectMaxThreads : 128; }
+
 template <int KP>
 cudaError_t launch_select_kp(const SelectParams& p, cudaStream_t stream) {
-    select_exact_kernel<KP><<<p.m, 128, 0, stream>>>(p);
+    select_exact_kernel<KP><<<p.m, select_threads(p.n_chunks), 0, stream>>>(p);
     return cudaGetLastError();
 }
 
@@ -426,9 +429,9 @@ cudaError_t launch_kmeans_select(const SelectParams& p, int32_t* out, int grid_f
 cudaError_t launch_select_recall(int kp, const SelectParams& p, const float* qsq, cudaStream_t stream) {
     if (p.n_chunks > kMaxChunks || p.n_chunks < 1 || p.k_out > kp) return cudaErrorInvalidValue;
     switch (kp) {
-        case 4: select_recall_kernel<4><<<p.m, 128, 0, stream>>>(p, qsq); break;
-        case 8: select_recall_kernel<8><<<p.m, 128, 0, stream>>>(p, qsq); break;
-        case 16: select_recall_kernel<16><<<p.m, 128, 0, stream>>>(p, qsq); break;
+        case 4: select_recall_kernel<4><<<p.m, select_threads(p.n_chunks), 0, stream>>>(p, qsq); break;
+        case 8: select_recall_kernel<8><<<p.m, select_threads(p.n_chunks), 0, stream>>>(p, qsq); break;
+        case 16: select_recall_kernel<16><<<p.m, select_threads(p.n_chunks), 0, stream>>>(p, qsq); break;
         default: return cudaErrorInvalidValue;
     }
     return cudaGetLastError();

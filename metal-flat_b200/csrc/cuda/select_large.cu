@@ -259,7 +259,7 @@ __global__ void __launch_bounds__(kSelThreads) select_large_kernel(const LargeSe
 // union of its L lists (each the KP1 best rows of one sample chunk).  At least
 // `want` sampled rows score at or above it, so it is <= the global want-th
 // best.  thr[q] = 0 (no floor) when the union holds fewer than `want` rows.
-constexpr int kFloorMax = 4096;
+constexpr int kFloorMax = kFloorMaxEntries;
 
 __global__ void __launch_bounds__(256) prepass_floor_kernel(const float* __restrict__ part_s,
                                                             const int32_t* __restrict__ part_i,
