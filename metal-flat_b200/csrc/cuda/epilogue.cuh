@@ -55,12 +55,24 @@ __device__ __forceinline__ void chunk_scores(const uint32_t (&r)[32], const floa
     }
 }
 
-// Eight float4 of the per-row score bias for 32 columns.  Every lane of the
-// warp reads the same addresses (an L1 broadcast).
+// Eight float4 of the per-row score bias for 32 columns, from global memory.
+// Every lane of the warp reads the same addresses (an L1 broadcast).
 __device__ __forceinline__ void load_bias(float4 (&cb)[8], const float* src) {
     const float4* s4 = reinterpret_cast<const float4*>(src);
 #pragma unroll
     for (int q = 0; q < 8; ++q) cb[q] = __ldg(s4 + q);
+}
+
+// The same from shared memory (a broadcast read; `src` must point into this
+// CTA's shared memory -- the read-only global path cannot address it).
+__device__ __forceinline__ void load_bias_shared(float4 (&cb)[8], const float* src) {
+    const uint32_t a = smem_u32(src);
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+        asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                     : "=f"(cb[q].x), "=f"(cb[q].y), "=f"(cb[q].z), "=f"(cb[q].w)
+                     : "r"(a + q * 16)
+                     : "memory");
 }
 
 // Bit mask of the columns scoring above `gate` (slow paths only).  The eight

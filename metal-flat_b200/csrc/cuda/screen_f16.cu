@@ -30,6 +30,8 @@ constexpr int kBTileBytesH = kBN * 128;           // 32 KB
 constexpr int kMaxStagesH = 6;
 constexpr int kSmemBudgetH = 7 * kBTileBytesH;    // 224 KB for A + ring
 constexpr int kMaxResidentKb = 6;                 // d_pad <= 384 keeps A resident
+constexpr int kBarBytesH = 256;                   // mbarriers, TMEM slot, abort flag
+constexpr int kBiasBytesH = kBN * 4;              // one tile's score bias (fp32)
 
 __host__ __device__ inline bool a_streamed(int kb) { return kb > kMaxResidentKb; }
 __host__ __device__ inline int stage_bytes_h(int kb) {
@@ -44,9 +46,10 @@ __host__ __device__ inline int n_stages_h(int kb) {
 struct SmemH {
     uint8_t* a;         // resident A [kb][16 KB] (resident mode)
     uint8_t* ring;      // [stages][stage bytes]: ([A 16 KB]) [B 32 KB]
-    uint64_t *full, *empty, *a_full, *a_empty, *acc_full, *acc_empty, *drain;
+    uint64_t *full, *empty, *a_full, *a_empty, *acc_full, *acc_empty, *drain, *bias_full;
     uint32_t* tmem_slot;
     int* abort_flag;
+    float* bias;        // [2][kBN]: score bias of the tile in accumulator buffer b
 };
 
 __device__ inline SmemH carve_h(uint8_t* base, int kb, int stages) {
@@ -61,8 +64,10 @@ __device__ inline SmemH carve_h(uint8_t* base, int kb, int stages) {
     S.acc_full = S.a_full + 2;
     S.acc_empty = S.a_full + 4;
     S.drain = S.a_full + 6;
-    S.tmem_slot = reinterpret_cast<uint32_t*>(S.a_full + 7);
+    S.bias_full = S.a_full + 7;
+    S.tmem_slot = reinterpret_cast<uint32_t*>(S.a_full + 9);
     S.abort_flag = reinterpret_cast<int*>(S.tmem_slot + 1);
+    S.bias = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + kBarBytesH);
     return S;
 }
 
@@ -70,11 +75,13 @@ template <int KP, bool kBuf, bool kBF16>
 __global__ void __launch_bounds__(threads_h(kBuf), 1)
 screen_f16_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                   const ScreenParams p) {
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t* base = reinterpret_cast<uint8_t*>(
-        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    // SWIZZLE_128B tiles need 1024-byte aligned shared memory.  The declared
+    // alignment is checked, not assumed: a misaligned base ends the launch
+    // with a configuration error before any copy is issued.
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* base = smem_raw;
     const int kb_count = p.d_pad / kBKH;
-    if (kb_count < 1 || kb_count * kBKH != p.d_pad) {
+    if (kb_count < 1 || kb_count * kBKH != p.d_pad || (smem_u32(smem_raw) & 1023u) != 0u) {
         if (threadIdx.x == 0) atomicExch(p.err, kErrConfig);
         return;
     }
@@ -99,9 +106,11 @@ screen_f16_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
         mbar_init(S.a_empty, 1);
         for (int b = 0; b < 2; ++b) {
             mbar_init(&S.acc_full[b], 1);
-            mbar_init(&S.acc_empty[b], kEpiWG * 128);
+            mbar_init(&S.acc_empty[b], kEpiWG * 4);   // one arrival per epilogue warp
         }
         mbar_init(S.drain, 1);
+        mbar_init(&S.bias_full[0], 1);
+        mbar_init(&S.bias_full[1], 1);
         *S.abort_flag = 0;
         fence_mbar_init();
     }
@@ -169,6 +178,7 @@ screen_f16_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
         if (lane == 0) {
             int stage = 0;
             uint32_t sphase = 0, a_phase = 0, tcount = 0;
+            uint32_t bias_pending = 0, bias_phase = 0;   // bias copies issued (drain on abort)
             bool ok = true, issued_any = false;
             for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
                 const int ch = u / p.n_qtiles;
@@ -184,6 +194,14 @@ screen_f16_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
                     const uint32_t ph = (tcount >> 1) & 1u;
                     if (!mbar_wait(&S.acc_empty[b], ph ^ 1u, abort_flag)) { ok = false; break; }
                     tc_fence_after();
+                    // the epilogue is done with buffer b's tile (two tiles back),
+                    // so its bias slot takes this tile's bias; the copy lands
+                    // while the MMAs run
+                    mbar_arrive_expect_tx(&S.bias_full[b], kBiasBytesH);
+                    bulk_load_g2s(S.bias + b * kBN, p.colbias + static_cast<int64_t>(t) * p.tile_stride * kBN,
+                                  kBiasBytesH, &S.bias_full[b]);
+                    bias_pending |= 1u << b;
+                    bias_phase = (bias_phase & ~(1u << b)) | (ph << b);
                     const uint32_t d_tmem = tmem_base + b * kBN;
                     for (int kb = 0; kb < kb_count; ++kb) {
                         if (!mbar_wait(&S.full[stage], sphase, abort_flag)) { ok = false; break; }
@@ -208,6 +226,11 @@ screen_f16_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
             if (*abort_flag && issued_any) {
                 tc_commit(S.drain);
                 mbar_wait_drain(S.drain, 0u, 200000000ull);
+            }
+            if (*abort_flag) {
+                for (int b = 0; b < 2; ++b)
+                    if (bias_pending & (1u << b))
+                        mbar_wait_drain(&S.bias_full[b], (bias_phase >> b) & 1u, 200000000ull);
             }
         }
     } else {
@@ -241,22 +264,23 @@ screen_f16_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
                 const uint32_t ph = (tcount >> 1) & 1u;
                 const uint32_t fkey = fkey_next;
                 if (!kBuf && live && p.use_floor && t + 1 < t1) fkey_next = __ldcg(p.thr + row);
-                // the next tile's bias prefetch overlaps the accumulator wait
-                if (lane < kCols / 32 && t + 1 < t1)
-                    prefetch_l1(p.colbias + static_cast<int64_t>(t + 1) * p.tile_stride * kBN +
-                                g * kCols + lane * 32);
-                if (!mbar_wait(&S.acc_full[b], ph, abort_flag)) { ok = false; break; }
+                // one lane polls the barriers, the warp follows
+                bool ready = true;
+                if (lane == 0)
+                    ready = mbar_wait(&S.acc_full[b], ph, abort_flag) &&
+                            mbar_wait(&S.bias_full[b], ph, abort_flag);
+                if (!__shfl_sync(0xffffffffu, ready ? 1 : 0, 0)) { ok = false; break; }
                 const float floor_adj =
                     !live ? __int_as_float(0x7f800000)
                           : (p.use_floor ? floor_below(fkey) : -__int_as_float(0x7f800000));
                 const int id_tile = t * p.tile_stride * kBN + g * kCols;
-                const float* cb_tile = p.colbias + id_tile;
+                const float* cb_tile = S.bias + b * kBN + g * kCols;   // shared memory
                 const uint32_t taddr = lane_addr + b * kBN + g * kCols;
                 // inner product on columns wholly inside the database: bias 0
                 const bool raw = p.alpha == 1.0f && static_cast<int64_t>(id_tile) + kCols <= p.n;
                 if constexpr (kEpiWG == 4) {
                     // 4 warps per SMSP: one chunk at a time, latency hidden by
-                    // the other warps (keeps the thread within 112 registers)
+                    // the other warps (keeps the thread within 96 registers)
                     __syncwarp();
                     tc_fence_after();
 #pragma unroll 1
@@ -265,7 +289,7 @@ screen_f16_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
                         float4 cb[8];
                         __syncwarp();
                         tmem_ld_32x32b_x32(taddr + c * 32, r);
-                        if (!raw) load_bias(cb, cb_tile + c * 32);
+                        if (!raw) load_bias_shared(cb, cb_tile + c * 32);
                         tmem_wait_ld_regs(r);
                         if constexpr (kBuf) {
                             if (raw) buffer_chunk_raw(r, floor_adj, br, id_tile + c * 32);
@@ -283,7 +307,7 @@ screen_f16_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
                     tmem_ld_32x32b_x32(taddr, ra);
     #pragma unroll 1
                     for (int c = 0; c < kCols / 32; c += 2) {
-                        if (!raw) load_bias(cb, cb_tile + c * 32);
+                        if (!raw) load_bias_shared(cb, cb_tile + c * 32);
                         tmem_wait_ld_regs(ra);
                         __syncwarp();
                         tmem_ld_32x32b_x32(taddr + (c + 1) * 32, rb);
@@ -294,7 +318,7 @@ screen_f16_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
                             if (raw) scan_chunk_raw<KP>(ra, floor_adj, L, id_tile + c * 32);
                             else scan_chunk<KP>(ra, cb, p.alpha, floor_adj, L, id_tile + c * 32);
                         }
-                        if (!raw) load_bias(cb, cb_tile + (c + 1) * 32);
+                        if (!raw) load_bias_shared(cb, cb_tile + (c + 1) * 32);
                         tmem_wait_ld_regs(rb);
                         if (c + 2 < kCols / 32) {
                             __syncwarp();
@@ -309,9 +333,9 @@ screen_f16_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
                         }
                     }
                 }
-                __syncwarp();
                 tc_fence_before();
-                mbar_arrive(&S.acc_empty[b]);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&S.acc_empty[b]);
             }
             if (!ok) break;
             if (!kBuf && live) {
@@ -363,7 +387,7 @@ cudaError_t launch_h_kp(int kp, const CUtensorMap& a, const CUtensorMap& b, cons
 int screen_f16_smem_bytes(int d_pad) {
     const int kb = d_pad / kBKH;
     const int a = a_streamed(kb) ? 0 : kb * kATileBytesH;
-    return 1024 + a + n_stages_h(kb) * stage_bytes_h(kb) + 256;
+    return a + n_stages_h(kb) * stage_bytes_h(kb) + kBarBytesH + 2 * kBiasBytesH;
 }
 
 cudaError_t launch_screen_f16(int kp, bool bf16, const CUtensorMap& a, const CUtensorMap& b,

@@ -107,7 +107,7 @@ screen_tf32x3_kernel(const __grid_constant__ CUtensorMap tm_a_hi,
         mbar_init(S.a_empty, 1);
         for (int b = 0; b < 2; ++b) {
             mbar_init(&S.acc_full[b], 1);
-            mbar_init(&S.acc_empty[b], kEpiWarps * 32);
+            mbar_init(&S.acc_empty[b], kEpiWarps);   // one arrival per epilogue warp
         }
         mbar_init(S.drain, 1);
         *S.abort_flag = 0;
@@ -272,7 +272,10 @@ screen_tf32x3_kernel(const __grid_constant__ CUtensorMap tm_a_hi,
                 // the next tile's bias prefetch overlaps the accumulator wait
                 if (lane < 8 && t + 1 < t1)
                     prefetch_l1(p.colbias + static_cast<int64_t>(t + 1) * p.tile_stride * kBN + lane * 32);
-                if (!mbar_wait(&S.acc_full[b], ph, abort_flag)) { ok = false; break; }
+                // one lane polls the barrier, the warp follows
+                bool ready = true;
+                if (lane == 0) ready = mbar_wait(&S.acc_full[b], ph, abort_flag);
+                if (!__shfl_sync(0xffffffffu, ready ? 1 : 0, 0)) { ok = false; break; }
                 const float floor_adj =
                     !live ? __int_as_float(0x7f800000)
                           : (p.use_floor ? floor_below(fkey) : -__int_as_float(0x7f800000));
@@ -303,9 +306,9 @@ screen_tf32x3_kernel(const __grid_constant__ CUtensorMap tm_a_hi,
                         buffer_chunk(rb, cbv, p.alpha, floor_adj, br, id_tile + (c + 1) * 32);
                     else scan_chunk<KP>(rb, cbv, p.alpha, floor_adj, L, id_tile + (c + 1) * 32);
                 }
-                __syncwarp();
                 tc_fence_before();
-                mbar_arrive(&S.acc_empty[b]);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&S.acc_empty[b]);
             }
             if (!ok) break;
             if (!kBuf && live) {
