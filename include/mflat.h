@@ -55,7 +55,8 @@ typedef enum {                      /* c/include/mflat.h:42-49, value-stable */
     MFLAT_ERR_ALLOC     = 3,        /* host or device allocation failed */
     MFLAT_ERR_NOT_READY = 4,
     MFLAT_ERR_INTERNAL  = 5,
-    MFLAT_ERR_DEVICE    = 6         /* ADDITIVE: CUDA / NCCL failure or no device */
+    MFLAT_ERR_DEVICE    = 6,        /* ADDITIVE: CUDA / NCCL failure or no device */
+    MFLAT_ERR_IO        = 7         /* ADDITIVE: index file unreadable / unwritable */
 } mflat_status_t;
 
 /* ADDITIVE: storage precision of the database rows on the device. */
@@ -177,6 +178,20 @@ MFLAT_API mflat_status_t mflat_kmeans_assign_device(const float* d_points, int n
 MFLAT_API mflat_status_t mflat_comm_unique_id(uint8_t out_id[MFLAT_COMM_ID_BYTES]);
 MFLAT_API mflat_status_t mflat_flat_set_shard(mflat_flat_index_t*, int rank, int world,
         const uint8_t comm_id[MFLAT_COMM_ID_BYTES], int64_t id_base);
+
+/* Persistence of a flat index (the reference persists only its graph index:
+ * GraphIndex::save / load, src/GraphIndex.mm:424-452, 'MFGR' header; this is
+ * the same style for the flat index).  File: int32 header {0x4d46464c 'MFFL',
+ * version 1, dim, metric, storage, n, 0, 0}, then n x dim stored elements --
+ * fp32, or the fp16 / bf16 bit patterns -- little-endian.  A loaded index is
+ * identical to the saved one (same rows, norms and results).
+ * save: NULL h / path -> NULL_ARG; I/O failure -> MFLAT_ERR_IO.
+ * load: a new handle on `device` (-1 = default) with the file's dim, metric
+ * and storage; NULL path -> NULL_ARG; unreadable or malformed file ->
+ * MFLAT_ERR_IO (and NULL). */
+MFLAT_API mflat_status_t mflat_flat_save(const mflat_flat_index_t*, const char* path);
+MFLAT_API mflat_flat_index_t* mflat_flat_load(const char* path, int device,
+                                              mflat_status_t* out_status);
 
 #ifdef __cplusplus
 }

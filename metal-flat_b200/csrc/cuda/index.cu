@@ -165,6 +165,49 @@ __global__ void ingest_rows_half_kernel(const float* __restrict__ src, int64_t n
     colbias[row0 + i] = metric == kL2 ? -static_cast<float>(s2) : 0.0f;
 }
 
+// 16-bit rows that are already stored values (a reloaded index): copied bit
+// for bit; the norm term is recomputed from them exactly as at first ingest.
+__global__ void ingest_rows_bits_kernel(const uint16_t* __restrict__ src, int64_t n, int dim,
+                                        int d_pad, int metric, bool bf16, int64_t row0,
+                                        uint16_t* __restrict__ db, float* __restrict__ colbias,
+                                        float* __restrict__ dnorm) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const uint16_t* row = src + i * dim;
+    uint16_t* o = db + (row0 + i) * d_pad;
+    double s2 = 0.0;
+    for (int c = 0; c < dim; ++c) {
+        const float x = from_half_bits(row[c], bf16);
+        s2 += static_cast<double>(x) * x;
+        o[c] = row[c];
+    }
+    for (int c = dim; c < d_pad; ++c) o[c] = 0;
+    dnorm[row0 + i] = static_cast<float>(s2);
+    colbias[row0 + i] = metric == kL2 ? -static_cast<float>(s2) : 0.0f;
+}
+
+// Stored rows [row0, row0 + n) in storage precision without padding: fp32
+// rows as hi + lo (exactly the ingested value), 16-bit rows bit for bit.
+__global__ void export_rows_f32_kernel(const float* __restrict__ db_hi, const float* __restrict__ db_lo,
+                                       int64_t row0, int64_t n, int dim, int d_pad,
+                                       float* __restrict__ out) {
+    const int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (e >= n * dim) return;
+    const int64_t r = e / dim;
+    const int c = static_cast<int>(e - r * dim);
+    const int64_t o = (row0 + r) * d_pad + c;
+    out[e] = db_hi[o] + db_lo[o];
+}
+
+__global__ void export_rows_bits_kernel(const uint16_t* __restrict__ db, int64_t row0, int64_t n,
+                                        int dim, int d_pad, uint16_t* __restrict__ out) {
+    const int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (e >= n * dim) return;
+    const int64_t r = e / dim;
+    const int c = static_cast<int>(e - r * dim);
+    out[e] = db[(row0 + r) * d_pad + c];
+}
+
 __global__ void prep_queries_half_kernel(const float* __restrict__ src, int m, int m_pad, int dim,
                                          int d_pad, int metric, bool bf16, uint16_t* __restrict__ q,
                                          float* __restrict__ qsq) {
@@ -203,8 +246,9 @@ __device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
 // One thread per row: optional Cosine normalisation (src/Distance.h:50-60),
 // squared norm with double accumulation (Distance.h:40-47), tf32 split,
 // zero padding to d_pad, score bias and running max row norm.
+// `normalize` = 0 for rows that are already stored values (a reloaded index).
 __global__ void ingest_rows_kernel(const float* __restrict__ src, int64_t n, int dim, int d_pad,
-                                   int metric, int64_t row0, float* __restrict__ db_hi,
+                                   int metric, int normalize, int64_t row0, float* __restrict__ db_hi,
                                    float* __restrict__ db_lo, float* __restrict__ colbias,
                                    float* __restrict__ dnorm, unsigned* xmax_bits) {
     const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -214,7 +258,7 @@ __global__ void ingest_rows_kernel(const float* __restrict__ src, int64_t n, int
     float* ol = db_lo + (row0 + i) * d_pad;
     float inv = 1.0f;
     bool scale = false;
-    if (metric == kCosine) {
+    if (metric == kCosine && normalize) {
         double s = 0.0;
         for (int c = 0; c < dim; ++c) s += static_cast<double>(row[c]) * row[c];
         if (s > 0.0) { inv = static_cast<float>(1.0 / sqrt(s)); scale = true; }
@@ -898,6 +942,57 @@ int search_half(mflat_cu_index* ix, const float* queries, int m, int k_out, int3
 
 using namespace mflat_cu;
 
+namespace mflat_cu {
+namespace {
+
+// Append n rows.  raw = 0: caller vectors (Cosine rows are normalised);
+// raw = 1: host rows that are already stored values, in storage precision
+// (fp32, or 16-bit bit patterns), taken as they are.
+int index_add(mflat_cu_index_t* ix, const void* vectors, int64_t n, int on_device, void* stream,
+              int raw) {
+    if (!ix || (!vectors && n > 0) || n < 0) return fail(ST_BAD_ARG, "bad argument");
+    if (n == 0) return ST_OK;
+    if (ix->n + n > static_cast<int64_t>(INT32_MAX) - kBN)
+        return fail(ST_BAD_ARG, "database would exceed 2^31 rows");
+    DeviceGuard g(ix->device);
+    cudaStream_t caller = static_cast<cudaStream_t>(stream);
+    if (on_device) order_after(ix->stream, caller);
+    CU_TRY(grow(ix, ix->n + n), "database allocation");
+    const size_t elem = raw && ix->storage != 0 ? sizeof(uint16_t) : sizeof(float);
+    const int64_t chunk =
+        on_device ? n : std::max<int64_t>(1, (int64_t(64) << 20) / (int64_t(ix->dim) * 4));
+    for (int64_t off = 0; off < n; off += chunk) {
+        const int64_t cnt = std::min(chunk, n - off);
+        const void* src = static_cast<const uint8_t*>(vectors) + off * ix->dim * elem;
+        if (!on_device) {
+            const size_t bytes = static_cast<size_t>(cnt) * ix->dim * elem;
+            CU_TRY(ix->stage_in.ensure(bytes), "staging");
+            CU_TRY(cudaMemcpyAsync(ix->stage_in.p, src, bytes, cudaMemcpyHostToDevice, ix->stream), "upload");
+            src = ix->stage_in.p;
+        }
+        if (ix->storage != 0 && raw)
+            ingest_rows_bits_kernel<<<blocks_for(cnt, 128), 128, 0, ix->stream>>>(
+                static_cast<const uint16_t*>(src), cnt, ix->dim, ix->d_pad, ix->metric, ix->storage == 2,
+                ix->n + off, static_cast<uint16_t*>(ix->db16), ix->colbias, ix->dnorm);
+        else if (ix->storage != 0)
+            ingest_rows_half_kernel<<<blocks_for(cnt, 128), 128, 0, ix->stream>>>(
+                static_cast<const float*>(src), cnt, ix->dim, ix->d_pad, ix->metric, ix->storage == 2,
+                ix->n + off, static_cast<uint16_t*>(ix->db16), ix->colbias, ix->dnorm);
+        else
+            ingest_rows_kernel<<<blocks_for(cnt, 128), 128, 0, ix->stream>>>(
+                static_cast<const float*>(src), cnt, ix->dim, ix->d_pad, ix->metric, raw ? 0 : 1,
+                ix->n + off, ix->db_hi, ix->db_lo, ix->colbias, ix->dnorm, ix->xmax_bits);
+        CU_TRY(cudaGetLastError(), "ingest launch");
+        if (!on_device) CU_TRY(cudaStreamSynchronize(ix->stream), "ingest");
+    }
+    ix->n += n;
+    if (on_device) order_after(caller, ix->stream);
+    return ST_OK;
+}
+
+}  // namespace
+}  // namespace mflat_cu
+
 // =====================================================================
 extern "C" {
 
@@ -991,40 +1086,41 @@ int mflat_cu_index_device(const mflat_cu_index_t* ix) { return ix ? ix->device :
 
 int mflat_cu_index_add(mflat_cu_index_t* ix, const float* vectors, int64_t n, int on_device,
                        void* stream) {
-    if (!ix || (!vectors && n > 0) || n < 0) return fail(ST_BAD_ARG, "bad argument");
-    if (n == 0) return ST_OK;
-    if (ix->n + n > static_cast<int64_t>(INT32_MAX) - kBN)
-        return fail(ST_BAD_ARG, "database would exceed 2^31 rows");
+    return index_add(ix, vectors, n, on_device, stream, 0);
+}
+
+int mflat_cu_index_add_raw(mflat_cu_index_t* ix, const void* host_rows, int64_t n) {
+    return index_add(ix, host_rows, n, 0, nullptr, 1);
+}
+
+int mflat_cu_index_export_rows(mflat_cu_index_t* ix, int64_t start, int64_t count, void* host_out) {
+    if (!ix || start < 0 || count < 0 || start + count > ix->n || (count > 0 && !host_out))
+        return fail(ST_BAD_ARG, "export range outside the index");
+    if (count == 0) return ST_OK;
     DeviceGuard g(ix->device);
-    cudaStream_t caller = static_cast<cudaStream_t>(stream);
-    if (on_device) order_after(ix->stream, caller);
-    CU_TRY(grow(ix, ix->n + n), "database allocation");
-    const int64_t chunk =
-        on_device ? n : std::max<int64_t>(1, (int64_t(64) << 20) / (int64_t(ix->dim) * 4));
-    for (int64_t off = 0; off < n; off += chunk) {
-        const int64_t cnt = std::min(chunk, n - off);
-        const float* src = vectors + off * ix->dim;
-        if (!on_device) {
-            const size_t bytes = static_cast<size_t>(cnt) * ix->dim * sizeof(float);
-            CU_TRY(ix->stage_in.ensure(bytes), "staging");
-            CU_TRY(cudaMemcpyAsync(ix->stage_in.p, src, bytes, cudaMemcpyHostToDevice, ix->stream), "upload");
-            src = ix->stage_in.as<float>();
-        }
+    const size_t elem = ix->storage != 0 ? sizeof(uint16_t) : sizeof(float);
+    const int64_t chunk = std::max<int64_t>(1, (int64_t(64) << 20) / (int64_t(ix->dim) * 4));
+    for (int64_t off = 0; off < count; off += chunk) {
+        const int64_t cnt = std::min(chunk, count - off);
+        const int64_t elems = cnt * ix->dim;
+        CU_TRY(ix->stage_in.ensure(static_cast<size_t>(elems) * elem), "staging");
         if (ix->storage != 0)
-            ingest_rows_half_kernel<<<blocks_for(cnt, 128), 128, 0, ix->stream>>>(
-                src, cnt, ix->dim, ix->d_pad, ix->metric, ix->storage == 2, ix->n + off,
-                static_cast<uint16_t*>(ix->db16), ix->colbias, ix->dnorm);
+            export_rows_bits_kernel<<<blocks_for(elems, 256), 256, 0, ix->stream>>>(
+                static_cast<const uint16_t*>(ix->db16), start + off, cnt, ix->dim, ix->d_pad,
+                ix->stage_in.as<uint16_t>());
         else
-            ingest_rows_kernel<<<blocks_for(cnt, 128), 128, 0, ix->stream>>>(
-                src, cnt, ix->dim, ix->d_pad, ix->metric, ix->n + off, ix->db_hi, ix->db_lo,
-                ix->colbias, ix->dnorm, ix->xmax_bits);
-        CU_TRY(cudaGetLastError(), "ingest launch");
-        if (!on_device) CU_TRY(cudaStreamSynchronize(ix->stream), "ingest");
+            export_rows_f32_kernel<<<blocks_for(elems, 256), 256, 0, ix->stream>>>(
+                ix->db_hi, ix->db_lo, start + off, cnt, ix->dim, ix->d_pad, ix->stage_in.as<float>());
+        CU_TRY(cudaGetLastError(), "export launch");
+        CU_TRY(cudaMemcpyAsync(static_cast<uint8_t*>(host_out) + off * ix->dim * elem, ix->stage_in.p,
+                               static_cast<size_t>(elems) * elem, cudaMemcpyDeviceToHost, ix->stream),
+               "download");
+        CU_TRY(cudaStreamSynchronize(ix->stream), "export");
     }
-    ix->n += n;
-    if (on_device) order_after(caller, ix->stream);
     return ST_OK;
 }
+
+int mflat_cu_index_storage(const mflat_cu_index_t* ix) { return ix ? ix->storage : -1; }
 
 int mflat_cu_index_reset(mflat_cu_index_t* ix) {
     if (!ix) return fail(ST_BAD_ARG, "bad argument");

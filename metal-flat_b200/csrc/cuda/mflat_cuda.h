@@ -43,6 +43,15 @@ MFLAT_CU_API int mflat_cu_index_device(const mflat_cu_index_t* ix);
 MFLAT_CU_API int mflat_cu_index_add(mflat_cu_index_t* ix, const float* vectors, int64_t n,
                                     int on_device, void* stream);
 MFLAT_CU_API int mflat_cu_index_reset(mflat_cu_index_t* ix);
+/* Persistence.  export_rows copies stored rows [start, start + count) to host
+ * memory in storage precision without padding (fp32: the ingested values;
+ * fp16 / bf16: the stored bit patterns, 2 bytes per element).  add_raw appends
+ * host rows in that same form as they are (no Cosine normalisation), so an
+ * exported index reloads to the identical device state. */
+MFLAT_CU_API int mflat_cu_index_export_rows(mflat_cu_index_t* ix, int64_t start, int64_t count,
+                                            void* host_out);
+MFLAT_CU_API int mflat_cu_index_add_raw(mflat_cu_index_t* ix, const void* host_rows, int64_t n);
+MFLAT_CU_API int mflat_cu_index_storage(const mflat_cu_index_t* ix);
 /* Writes m rows of k_out (ids, distances), nearest-first, -1 / +-inf padded. */
 MFLAT_CU_API int mflat_cu_index_search(mflat_cu_index_t* ix, const float* queries, int m,
                                        int k_out, int32_t* out_ids, float* out_dist,

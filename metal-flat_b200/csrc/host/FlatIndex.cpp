@@ -9,9 +9,11 @@
 // search path.
 #include <algorithm>
 #include <cmath>
+#include <cstdio>
 #include <new>
 #include <stdexcept>
 #include <string>
+#include <vector>
 
 #include "../cuda/mflat_cuda.h"
 #include "Log_internal.h"
@@ -157,6 +159,143 @@ SearchTiming FlatIndex::lastTiming() const {
 
 void FlatIndex::setShard(int rank, int world, const uint8_t* comm_id, int64_t id_base) {
     raise_status(mflat_cu_index_set_shard(mImpl->need(), rank, world, comm_id, id_base), "shard");
+}
+
+namespace {
+
+constexpr int32_t kFlatMagic = 0x4d46464c;   // 'MFFL'
+constexpr int32_t kFlatVersion = 1;
+constexpr size_t kIoChunkBytes = size_t(64) << 20;
+
+struct FlatFileHeader {
+    int32_t magic, version, dim, metric, storage, n, reserved0, reserved1;
+};
+
+size_t elem_bytes(Storage s) { return s == Storage::FP32 ? sizeof(float) : sizeof(uint16_t); }
+
+// Reads and checks the header; false (with a log line) on any mismatch.
+bool read_header(std::FILE* f, const char* path, FlatFileHeader& h) {
+    if (std::fread(&h, sizeof h, 1, f) != 1 || h.magic != kFlatMagic) {
+        MFLAT_LOG_ERROR("load %s: not a flat index file", path);
+        return false;
+    }
+    if (h.version != kFlatVersion || h.dim <= 0 || h.n < 0 || h.metric < 0 || h.metric > 2 ||
+        h.storage < 0 || h.storage > 2) {
+        MFLAT_LOG_ERROR("load %s: unsupported header (version %d, dim %d, n %d)", path, h.version,
+                        h.dim, h.n);
+        return false;
+    }
+    return true;
+}
+
+}  // namespace
+
+bool FlatIndex::save(const char* path) const {
+    if (!path) return false;
+    mflat_cu_index_t* dev = mImpl->need();
+    std::FILE* f = std::fopen(path, "wb");
+    if (!f) {
+        MFLAT_LOG_ERROR("save %s: cannot open for writing", path);
+        return false;
+    }
+    const int64_t n = mflat_cu_index_size(dev);
+    const FlatFileHeader h{kFlatMagic, kFlatVersion, mImpl->dim, static_cast<int32_t>(mImpl->metric),
+                           static_cast<int32_t>(mImpl->storage), static_cast<int32_t>(n), 0, 0};
+    bool ok = std::fwrite(&h, sizeof h, 1, f) == 1;
+    const size_t row = static_cast<size_t>(mImpl->dim) * elem_bytes(mImpl->storage);
+    const int64_t chunk = std::max<int64_t>(1, static_cast<int64_t>(kIoChunkBytes / row));
+    std::vector<uint8_t> buf;
+    for (int64_t off = 0; ok && off < n; off += chunk) {
+        const int64_t cnt = std::min(chunk, n - off);
+        buf.resize(static_cast<size_t>(cnt) * row);
+        const int st = mflat_cu_index_export_rows(dev, off, cnt, buf.data());
+        if (st != 0) {
+            std::fclose(f);
+            raise_status(st, "save");
+        }
+        ok = std::fwrite(buf.data(), 1, buf.size(), f) == buf.size();
+    }
+    ok = (std::fclose(f) == 0) && ok;
+    if (!ok) MFLAT_LOG_ERROR("save %s: write failed", path);
+    return ok;
+}
+
+bool FlatIndex::load(const char* path) {
+    if (!path) return false;
+    mflat_cu_index_t* dev = mImpl->need();
+    std::FILE* f = std::fopen(path, "rb");
+    if (!f) {
+        MFLAT_LOG_ERROR("load %s: cannot open", path);
+        return false;
+    }
+    FlatFileHeader h{};
+    if (!read_header(f, path, h)) {
+        std::fclose(f);
+        return false;
+    }
+    if (h.dim != mImpl->dim || h.metric != static_cast<int32_t>(mImpl->metric) ||
+        h.storage != static_cast<int32_t>(mImpl->storage)) {
+        MFLAT_LOG_ERROR("load %s: file holds dim %d metric %d storage %d, index is dim %d metric %d "
+                        "storage %d", path, h.dim, h.metric, h.storage, mImpl->dim,
+                        static_cast<int>(mImpl->metric), static_cast<int>(mImpl->storage));
+        std::fclose(f);
+        return false;
+    }
+    raise_status(mflat_cu_index_reset(dev), "load");
+    const size_t row = static_cast<size_t>(h.dim) * elem_bytes(mImpl->storage);
+    const int64_t chunk = std::max<int64_t>(1, static_cast<int64_t>(kIoChunkBytes / row));
+    std::vector<uint8_t> buf;
+    for (int64_t off = 0; off < h.n; off += chunk) {
+        const int64_t cnt = std::min<int64_t>(chunk, h.n - off);
+        buf.resize(static_cast<size_t>(cnt) * row);
+        if (std::fread(buf.data(), 1, buf.size(), f) != buf.size()) {
+            MFLAT_LOG_ERROR("load %s: file ends after %lld of %d rows", path,
+                            static_cast<long long>(off), h.n);
+            std::fclose(f);
+            raise_status(mflat_cu_index_reset(dev), "load");
+            return false;
+        }
+        const int st = mflat_cu_index_add_raw(dev, buf.data(), cnt);
+        if (st != 0) {
+            std::fclose(f);
+            raise_status(st, "load");
+        }
+    }
+    std::fclose(f);
+    return true;
+}
+
+bool readFlatFileInfo(const char* path, int& dim, Metric& metric, Storage& storage, int& n) {
+    if (!path) return false;
+    std::FILE* f = std::fopen(path, "rb");
+    if (!f) return false;
+    FlatFileHeader h{};
+    const bool ok = read_header(f, path, h);
+    std::fclose(f);
+    if (!ok) return false;
+    dim = h.dim;
+    metric = static_cast<Metric>(h.metric);
+    storage = static_cast<Storage>(h.storage);
+    n = h.n;
+    return true;
+}
+
+std::unique_ptr<FlatIndex> FlatIndex::open(const char* path, int device) {
+    if (!path) return nullptr;
+    std::FILE* f = std::fopen(path, "rb");
+    if (!f) {
+        MFLAT_LOG_ERROR("load %s: cannot open", path);
+        return nullptr;
+    }
+    FlatFileHeader h{};
+    const bool ok = read_header(f, path, h);
+    std::fclose(f);
+    if (!ok) return nullptr;
+    auto idx = std::make_unique<FlatIndex>(h.dim, static_cast<Metric>(h.metric),
+                                           static_cast<Storage>(h.storage), device);
+    if (!idx->ready()) throw DeviceError("no usable CUDA device for the loaded index");
+    if (!idx->load(path)) return nullptr;
+    return idx;
 }
 
 void kmeansAssign(const float* points, int n, const float* centroids, int ncentroids, int dim,

@@ -91,7 +91,7 @@ mflat_status_t from_cu(int st) {
 
 struct mflat_flat_index {
     FlatIndex idx;
-    std::mutex mu;
+    mutable std::mutex mu;
     mflat_flat_index(int d, Metric m, mflat::Storage s, int dev) : idx(d, m, s, dev) {}
 };
 
@@ -123,6 +123,7 @@ MFLAT_API const char* mflat_status_str(mflat_status_t s) {
         case MFLAT_ERR_NOT_READY: return "index not built";
         case MFLAT_ERR_INTERNAL: return "internal error";
         case MFLAT_ERR_DEVICE: return "device error";
+        case MFLAT_ERR_IO: return "index file error";
     }
     return "unknown";
 }
@@ -286,6 +287,40 @@ MFLAT_API mflat_status_t mflat_flat_set_shard(mflat_flat_index_t* h, int rank, i
         h->idx.setShard(rank, world, comm_id, id_base);
         return MFLAT_OK;
     });
+}
+
+MFLAT_API mflat_status_t mflat_flat_save(const mflat_flat_index_t* h, const char* path) {
+    if (!h || !path) return MFLAT_ERR_NULL_ARG;
+    return guarded([&] {
+        std::lock_guard<std::mutex> lk(h->mu);
+        return h->idx.save(path) ? MFLAT_OK : MFLAT_ERR_IO;
+    });
+}
+
+MFLAT_API mflat_flat_index_t* mflat_flat_load(const char* path, int device, mflat_status_t* st) {
+    if (!path) {
+        if (st) *st = MFLAT_ERR_NULL_ARG;
+        return nullptr;
+    }
+    int dim = 0, n = 0;
+    Metric metric = Metric::L2;
+    mflat::Storage storage = mflat::Storage::FP32;
+    if (!mflat::readFlatFileInfo(path, dim, metric, storage, n)) {
+        if (st) *st = MFLAT_ERR_IO;
+        return nullptr;
+    }
+    mflat_flat_index_t* h = nullptr;
+    const mflat_status_t rc = guarded([&] {
+        h = new mflat_flat_index(dim, metric, storage, device);
+        if (!h->idx.ready()) return MFLAT_ERR_DEVICE;
+        return h->idx.load(path) ? MFLAT_OK : MFLAT_ERR_IO;
+    });
+    if (rc != MFLAT_OK) {
+        delete h;
+        h = nullptr;
+    }
+    if (st) *st = rc;
+    return h;
 }
 
 }  // extern "C"

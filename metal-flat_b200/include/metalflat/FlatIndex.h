@@ -83,10 +83,26 @@ public:
     // search() becomes a collective over `world` ranks returning global ids.
     void setShard(int rank, int world, const uint8_t* comm_id, int64_t id_base);
 
+    // Persistence (in the style of the reference's GraphIndex::save / load,
+    // src/GraphIndex.mm:424-452).  File: int32 header {'MFFL', version 1, dim,
+    // metric, storage, n, 0, 0}, then n x dim stored elements (fp32, or the
+    // fp16 / bf16 bit patterns).  save() returns false on an I/O failure.
+    // load() replaces this index's rows; it returns false (index unchanged)
+    // when the file is unreadable or its dim / metric / storage differ.
+    bool save(const char* path) const;
+    bool load(const char* path);
+    // A new index on `device` (-1 = default) with the file's dim, metric and
+    // storage; nullptr when the file cannot be read.
+    static std::unique_ptr<FlatIndex> open(const char* path, int device = -1);
+
 private:
     struct Impl;
     std::unique_ptr<Impl> mImpl;
 };
+
+// Header of a file written by FlatIndex::save; false when the file cannot be
+// read or is not a flat index file.
+bool readFlatFileInfo(const char* path, int& dim, Metric& metric, Storage& storage, int& n);
 
 // k-means assignment step: out[i] = argmin_c sqL2_f32(points[i], centroids[c])
 // with the reference's fp32 sequential sqL2 and lowest-index tie rule.

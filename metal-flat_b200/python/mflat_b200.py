@@ -20,7 +20,7 @@ CUDA_LIB_PATH = os.path.join(LIB_DIR, "libmflat_cuda.so")
 METRICS = {"l2": 0, "ip": 1, "inner_product": 1, "cosine": 2}
 STORAGES = {"fp32": 0, "fp16": 1, "bf16": 2}
 STATUS = {0: "ok", 1: "null argument", 2: "bad argument", 3: "allocation failed",
-          4: "index not built", 5: "internal error", 6: "device error"}
+          4: "index not built", 5: "internal error", 6: "device error", 7: "index file error"}
 
 EXPORTS = [
     "mflat_version", "mflat_status_str", "mflat_max_k",
@@ -31,6 +31,7 @@ EXPORTS = [
     "mflat_flat_add_device", "mflat_flat_search_device", "mflat_flat_set_timing",
     "mflat_flat_last_timing", "mflat_kmeans_assign", "mflat_kmeans_assign_device",
     "mflat_comm_unique_id", "mflat_flat_set_shard", "mflat_flat_search_noalloc",
+    "mflat_flat_save", "mflat_flat_load",
 ]
 
 
@@ -89,6 +90,8 @@ def lib() -> ctypes.CDLL:
         "mflat_kmeans_assign_device": ([vp, ci, vp, ci, ci, vp, ci, vp], ci),
         "mflat_comm_unique_id": ([ctypes.c_char_p], ci),
         "mflat_flat_set_shard": ([vp, ci, ci, ctypes.c_char_p, ctypes.c_int64], ci),
+        "mflat_flat_save": ([vp, ctypes.c_char_p], ci),
+        "mflat_flat_load": ([ctypes.c_char_p, ci, ctypes.POINTER(ci)], vp),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)
@@ -149,6 +152,22 @@ class FlatIndex:
         self._lib = L
         self.metric = m
 
+    @classmethod
+    def load(cls, path: str, device: int = -1) -> "FlatIndex":
+        """A new index holding the rows of a file written by save()."""
+        L = lib()
+        st = ctypes.c_int(0)
+        h = L.mflat_flat_load(os.fsencode(path), int(device), ctypes.byref(st))
+        if not h:
+            raise MflatError(st.value, f"load {path}")
+        self = cls.__new__(cls)
+        self._h, self._lib = h, L
+        self.metric = None
+        return self
+
+    def save(self, path: str) -> None:
+        _check(self._lib.mflat_flat_save(self._h, os.fsencode(path)), f"save {path}")
+
     def close(self) -> None:
         if getattr(self, "_h", None):
             self._lib.mflat_flat_free(self._h)
@@ -172,6 +191,10 @@ class FlatIndex:
     @property
     def device(self) -> int:
         return self._lib.mflat_flat_device(self._h)
+
+    @property
+    def storage(self) -> int:
+        return self._lib.mflat_flat_storage(self._h)
 
     def add(self, vectors) -> None:
         v = _f32(vectors)

@@ -133,3 +133,31 @@ def test_kmeans_argument_checks(built_lib):
     assert L.mflat_kmeans_assign(fp, -1, fp, 1, 4, op, -1) == 2
     assert L.mflat_kmeans_assign(fp, 2, fp, 0, 4, op, -1) == 2
     assert L.mflat_kmeans_assign(fp, 0, fp, 1, 4, op, -1) == 0   # nothing to assign
+
+
+def test_persistence_argument_checks_without_device(built_lib, tmp_path):
+    """save / load reject NULLs and unreadable or malformed files before any
+    device work (the file header is checked first)."""
+    L = built_lib
+    st = ctypes.c_int(-1)
+    assert L.mflat_flat_save(None, b"/tmp/x.mffl") == 1
+    assert L.mflat_flat_load(None, -1, ctypes.byref(st)) is None and st.value == 1
+    missing = str(tmp_path / "missing.mffl").encode()
+    assert L.mflat_flat_load(missing, -1, ctypes.byref(st)) is None and st.value == 7
+    bad = tmp_path / "bad.mffl"
+    bad.write_bytes(b"not an index file at all, 32+ bytes long.......")
+    assert L.mflat_flat_load(str(bad).encode(), -1, ctypes.byref(st)) is None and st.value == 7
+    # right magic, unsupported version
+    hdr = np.array([0x4d46464c, 9, 4, 0, 0, 0, 0, 0], np.int32)
+    ver = tmp_path / "ver.mffl"
+    ver.write_bytes(hdr.tobytes())
+    assert L.mflat_flat_load(str(ver).encode(), -1, ctypes.byref(st)) is None and st.value == 7
+    # a valid header without a device: the handle cannot be made ready
+    ok = tmp_path / "ok.mffl"
+    ok.write_bytes(np.array([0x4d46464c, 1, 4, 0, 0, 0, 0, 0], np.int32).tobytes())
+    h = L.mflat_flat_load(str(ok).encode(), -1, ctypes.byref(st))
+    if has_gpu():
+        assert h and st.value == 0
+        L.mflat_flat_free(h)
+    else:
+        assert h is None and st.value == 6
