@@ -179,6 +179,29 @@ MFLAT_API mflat_status_t mflat_comm_unique_id(uint8_t out_id[MFLAT_COMM_ID_BYTES
 MFLAT_API mflat_status_t mflat_flat_set_shard(mflat_flat_index_t*, int rank, int world,
         const uint8_t comm_id[MFLAT_COMM_ID_BYTES], int64_t id_base);
 
+/* IVF coarse layer: k-means training, CSR inverted-list scaffold, cell probing.
+ * The reference has this only as an internal C++ class (src/CoarseQuantizer.h:
+ * 27-75, used by its IVF indexes); these entries expose the same operations
+ * to FFI callers.  train: seed 12345, 256 training points per centroid,
+ * `iters` iterations, all on the device (data: host, n x dim, already
+ * metric-normalised); nlist is clamped to n.  csr: cell_start[nlist + 1]
+ * offsets and reordered_ids[n] (point ids grouped by cell, ascending within a
+ * cell); NULL outputs are skipped.  probe: nearest-first cell ids, m x nprobe,
+ * nprobe <= MFLAT_MAX_K.  Calls on one handle are serialised. */
+typedef struct mflat_coarse mflat_coarse_t;
+MFLAT_API mflat_coarse_t* mflat_coarse_create(int dim, int device, mflat_status_t* out_status);
+MFLAT_API void mflat_coarse_free(mflat_coarse_t*);
+MFLAT_API mflat_status_t mflat_coarse_train(mflat_coarse_t*, const float* data, int n, int nlist,
+        int iters);
+MFLAT_API int mflat_coarse_nlist(const mflat_coarse_t*);
+MFLAT_API int mflat_coarse_size(const mflat_coarse_t*);
+MFLAT_API int mflat_coarse_dim(const mflat_coarse_t*);
+MFLAT_API mflat_status_t mflat_coarse_centroids(const mflat_coarse_t*, float* out_centroids);
+MFLAT_API mflat_status_t mflat_coarse_csr(const mflat_coarse_t*, int32_t* out_cell_start,
+        int32_t* out_reordered_ids);
+MFLAT_API mflat_status_t mflat_coarse_probe(mflat_coarse_t*, const float* queries, int m,
+        int nprobe, int32_t* out_cells);
+
 /* Persistence of a flat index (the reference persists only its graph index:
  * GraphIndex::save / load, src/GraphIndex.mm:424-452, 'MFGR' header; this is
  * the same style for the flat index).  File: int32 header {0x4d46464c 'MFFL',

@@ -70,6 +70,31 @@ MFLAT_CU_API int mflat_cu_kmeans_assign(const float* points, int64_t n, const fl
                                         int ncentroids, int dim, int32_t* out_assign,
                                         int device, int on_device, void* stream);
 
+/* k-means training session (CoarseQuantizer::train).  create uploads the
+ * points (or borrows device points) and gathers the training subset given by
+ * train_rows (train_n < n) -- the host draws it, with the seeds and the
+ * empty-cell reseeds, from its own mt19937.  iterate = assignment of the
+ * training points + centroid means of the non-empty cells (double sums in
+ * ascending point order), cell counts to host_counts[nlist]; empty cells keep
+ * their centroid until reseed.  finish = assignment of all points + CSR:
+ * cell_start[nlist + 1] (prefix sums) and reordered[n] (point ids grouped by
+ * cell, ascending within a cell); each output pointer may be NULL.  The CSR
+ * also stays on the device (the *_device accessors) until destroy. */
+typedef struct mflat_cu_kmeans mflat_cu_kmeans_t;
+MFLAT_CU_API int mflat_cu_kmeans_create(int device, int dim, const float* points, int64_t n,
+                                        int on_device, const int32_t* train_rows, int64_t train_n,
+                                        int nlist, mflat_cu_kmeans_t** out);
+MFLAT_CU_API void mflat_cu_kmeans_destroy(mflat_cu_kmeans_t* k);
+MFLAT_CU_API int mflat_cu_kmeans_set_centroids(mflat_cu_kmeans_t* k, const float* host_centroids);
+MFLAT_CU_API int mflat_cu_kmeans_get_centroids(mflat_cu_kmeans_t* k, float* host_out);
+MFLAT_CU_API int mflat_cu_kmeans_iterate(mflat_cu_kmeans_t* k, int32_t* host_counts);
+MFLAT_CU_API int mflat_cu_kmeans_reseed(mflat_cu_kmeans_t* k, const int32_t* host_cells,
+                                        const int32_t* host_train_rows, int count);
+MFLAT_CU_API int mflat_cu_kmeans_finish(mflat_cu_kmeans_t* k, int32_t* host_assign,
+                                        int32_t* host_cell_start, int32_t* host_reordered);
+MFLAT_CU_API const int32_t* mflat_cu_kmeans_cell_start_device(const mflat_cu_kmeans_t* k);
+MFLAT_CU_API const int32_t* mflat_cu_kmeans_reordered_device(const mflat_cu_kmeans_t* k);
+
 /* Row sharding across ranks (NCCL). */
 MFLAT_CU_API int mflat_cu_comm_unique_id(uint8_t* out_id /* 128 bytes */);
 MFLAT_CU_API int mflat_cu_index_set_shard(mflat_cu_index_t* ix, int rank, int world,

@@ -12,9 +12,11 @@
 #include <mutex>
 #include <new>
 #include <stdexcept>
+#include <vector>
 
 #include "../../../include/mflat.h"
 #include "../cuda/mflat_cuda.h"
+#include "metalflat/CoarseQuantizer.h"
 #include "metalflat/FlatIndex.h"
 #include "metalflat/Log.h"
 
@@ -93,6 +95,12 @@ struct mflat_flat_index {
     FlatIndex idx;
     mutable std::mutex mu;
     mflat_flat_index(int d, Metric m, mflat::Storage s, int dev) : idx(d, m, s, dev) {}
+};
+
+struct mflat_coarse {
+    mflat::CoarseQuantizer cq;
+    mutable std::mutex mu;
+    mflat_coarse(int d, int dev) : cq(d, dev) {}
 };
 
 extern "C" {
@@ -285,6 +293,72 @@ MFLAT_API mflat_status_t mflat_flat_set_shard(mflat_flat_index_t* h, int rank, i
     return guarded([&] {
         std::lock_guard<std::mutex> lk(h->mu);
         h->idx.setShard(rank, world, comm_id, id_base);
+        return MFLAT_OK;
+    });
+}
+
+MFLAT_API mflat_coarse_t* mflat_coarse_create(int dim, int device, mflat_status_t* st) {
+    if (dim <= 0) {
+        if (st) *st = MFLAT_ERR_BAD_ARG;
+        return nullptr;
+    }
+    mflat_coarse_t* h = nullptr;
+    const mflat_status_t rc = guarded([&] {
+        h = new mflat_coarse(dim, device);
+        return MFLAT_OK;
+    });
+    if (st) *st = rc;
+    return rc == MFLAT_OK ? h : nullptr;
+}
+
+MFLAT_API void mflat_coarse_free(mflat_coarse_t* h) { delete h; }
+
+MFLAT_API mflat_status_t mflat_coarse_train(mflat_coarse_t* h, const float* data, int n, int nlist,
+                                            int iters) {
+    if (!h || !data) return MFLAT_ERR_NULL_ARG;
+    if (n <= 0 || nlist <= 0 || iters < 0) return MFLAT_ERR_BAD_ARG;
+    return guarded([&] {
+        std::lock_guard<std::mutex> lk(h->mu);
+        h->cq.train(data, n, nlist, iters);
+        return MFLAT_OK;
+    });
+}
+
+MFLAT_API int mflat_coarse_nlist(const mflat_coarse_t* h) { return h ? h->cq.nlist() : 0; }
+MFLAT_API int mflat_coarse_size(const mflat_coarse_t* h) { return h ? h->cq.size() : 0; }
+MFLAT_API int mflat_coarse_dim(const mflat_coarse_t* h) { return h ? h->cq.dim() : 0; }
+
+MFLAT_API mflat_status_t mflat_coarse_centroids(const mflat_coarse_t* h, float* out) {
+    if (!h || !out) return MFLAT_ERR_NULL_ARG;
+    std::lock_guard<std::mutex> lk(h->mu);
+    if (h->cq.nlist() == 0) return MFLAT_ERR_NOT_READY;
+    const auto& c = h->cq.centroids();
+    std::memcpy(out, c.data(), c.size() * sizeof(float));
+    return MFLAT_OK;
+}
+
+MFLAT_API mflat_status_t mflat_coarse_csr(const mflat_coarse_t* h, int32_t* cell_start,
+                                          int32_t* reordered) {
+    if (!h) return MFLAT_ERR_NULL_ARG;
+    std::lock_guard<std::mutex> lk(h->mu);
+    if (h->cq.nlist() == 0) return MFLAT_ERR_NOT_READY;
+    const auto& cs = h->cq.cellStart();
+    const auto& ro = h->cq.reorderedIds();
+    if (cell_start) std::memcpy(cell_start, cs.data(), cs.size() * sizeof(int32_t));
+    if (reordered) std::memcpy(reordered, ro.data(), ro.size() * sizeof(int32_t));
+    return MFLAT_OK;
+}
+
+MFLAT_API mflat_status_t mflat_coarse_probe(mflat_coarse_t* h, const float* queries, int m,
+                                            int nprobe, int32_t* out_cells) {
+    if (!h || !queries || !out_cells) return MFLAT_ERR_NULL_ARG;
+    if (m < 0 || nprobe < 1 || nprobe > MFLAT_MAX_K) return MFLAT_ERR_BAD_ARG;
+    return guarded([&] {
+        std::lock_guard<std::mutex> lk(h->mu);
+        if (h->cq.nlist() == 0) return MFLAT_ERR_NOT_READY;
+        std::vector<int32_t> probed;
+        h->cq.probeCells(queries, m, nprobe, probed);
+        std::memcpy(out_cells, probed.data(), probed.size() * sizeof(int32_t));
         return MFLAT_OK;
     });
 }

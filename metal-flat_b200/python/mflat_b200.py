@@ -32,6 +32,9 @@ EXPORTS = [
     "mflat_flat_last_timing", "mflat_kmeans_assign", "mflat_kmeans_assign_device",
     "mflat_comm_unique_id", "mflat_flat_set_shard", "mflat_flat_search_noalloc",
     "mflat_flat_save", "mflat_flat_load",
+    "mflat_coarse_create", "mflat_coarse_free", "mflat_coarse_train", "mflat_coarse_nlist",
+    "mflat_coarse_size", "mflat_coarse_dim", "mflat_coarse_centroids", "mflat_coarse_csr",
+    "mflat_coarse_probe",
 ]
 
 
@@ -92,6 +95,15 @@ def lib() -> ctypes.CDLL:
         "mflat_flat_set_shard": ([vp, ci, ci, ctypes.c_char_p, ctypes.c_int64], ci),
         "mflat_flat_save": ([vp, ctypes.c_char_p], ci),
         "mflat_flat_load": ([ctypes.c_char_p, ci, ctypes.POINTER(ci)], vp),
+        "mflat_coarse_create": ([ci, ci, ctypes.POINTER(ci)], vp),
+        "mflat_coarse_free": ([vp], None),
+        "mflat_coarse_train": ([vp, f32p, ci, ci, ci], ci),
+        "mflat_coarse_nlist": ([vp], ci),
+        "mflat_coarse_size": ([vp], ci),
+        "mflat_coarse_dim": ([vp], ci),
+        "mflat_coarse_centroids": ([vp, f32p], ci),
+        "mflat_coarse_csr": ([vp, i32p, i32p], ci),
+        "mflat_coarse_probe": ([vp, f32p, ci, ci, i32p], ci),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)
@@ -252,3 +264,59 @@ class FlatIndex:
     def set_shard(self, rank: int, world: int, comm_id: bytes | None, id_base: int) -> None:
         _check(self._lib.mflat_flat_set_shard(self._h, rank, world, comm_id, int(id_base)),
                "set_shard")
+
+
+class CoarseQuantizer:
+    """IVF coarse layer (k-means train, CSR scaffold, cell probing) through the C ABI."""
+
+    def __init__(self, dim: int, device: int = -1):
+        L = lib()
+        st = ctypes.c_int(0)
+        self._h = L.mflat_coarse_create(int(dim), int(device), ctypes.byref(st))
+        if not self._h:
+            raise MflatError(st.value, "coarse create")
+        self._lib = L
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            self._lib.mflat_coarse_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        self.close()
+
+    @property
+    def nlist(self) -> int:
+        return self._lib.mflat_coarse_nlist(self._h)
+
+    @property
+    def size(self) -> int:
+        return self._lib.mflat_coarse_size(self._h)
+
+    @property
+    def dim(self) -> int:
+        return self._lib.mflat_coarse_dim(self._h)
+
+    def train(self, data, nlist: int, iters: int = 12) -> None:
+        d = _f32(data)
+        _check(self._lib.mflat_coarse_train(self._h, _ptr(d, ctypes.c_float), d.shape[0], int(nlist),
+                                            int(iters)), "coarse train")
+
+    def centroids(self) -> np.ndarray:
+        out = np.empty((self.nlist, self.dim), np.float32)
+        _check(self._lib.mflat_coarse_centroids(self._h, _ptr(out, ctypes.c_float)), "coarse centroids")
+        return out
+
+    def csr(self):
+        cs = np.empty(self.nlist + 1, np.int32)
+        ro = np.empty(self.size, np.int32)
+        _check(self._lib.mflat_coarse_csr(self._h, _ptr(cs, ctypes.c_int32), _ptr(ro, ctypes.c_int32)),
+               "coarse csr")
+        return cs, ro
+
+    def probe(self, queries, nprobe: int) -> np.ndarray:
+        q = _f32(queries)
+        out = np.empty((q.shape[0], nprobe), np.int32)
+        _check(self._lib.mflat_coarse_probe(self._h, _ptr(q, ctypes.c_float), q.shape[0], int(nprobe),
+                                            _ptr(out, ctypes.c_int32)), "coarse probe")
+        return out

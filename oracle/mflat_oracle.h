@@ -62,6 +62,18 @@ int mfo_flat_search_cpusearch(const float* db, int64_t n, int dim, int metric,
 void mfo_kmeans_assign_f32(const float* points, int64_t n, const float* cents,
                            int ncent, int dim, int32_t* out);
 
+/* k-means training of CoarseQuantizer::train (src/Internal.h:257-359,
+ * src/CoarseQuantizer.mm:104-143): seeds, 256-points-per-centroid subset,
+ * `iters` (assign, double means, reseed) iterations, final assignment and CSR.
+ * out_cents[nlist*dim], out_assign[n], out_cell_start[nlist+1],
+ * out_reordered[n] (the last three may be NULL).  Returns nlist (clamped to
+ * n) or -1 on bad arguments.  mflat_oracle_kmeans.cpp. */
+int mfo_kmeans_train(const float* data, int64_t n, int dim, int nlist_req, int iters,
+                     int max_points_per_centroid, float* out_cents, int32_t* out_assign,
+                     int32_t* out_cell_start, int32_t* out_reordered);
+/* The training's seed permutation of 0..n-1 (mt19937(seed), Fisher-Yates). */
+void mfo_kmeans_seed_permutation(int64_t n, uint32_t seed, int32_t* perm);
+
 /* Merge P per-shard result lists (each m x k, nearest-first, ids already
  * global) into one m x k list with the same order and tie rule. */
 void mfo_merge_shards(const int32_t* ids, const float* dist, int nshard,

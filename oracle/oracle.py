@@ -47,6 +47,9 @@ def lib() -> ctypes.CDLL:
             fn.restype = ci
         _lib.mfo_kmeans_assign_f32.argtypes = [f32p, i64, f32p, ci, ci, i32p]
         _lib.mfo_merge_shards.argtypes = [i32p, f32p, ci, i64, ci, ci, i32p, f32p]
+        _lib.mfo_kmeans_train.argtypes = [f32p, i64, ci, ci, ci, ci, f32p, i32p, i32p, i32p]
+        _lib.mfo_kmeans_train.restype = ci
+        _lib.mfo_kmeans_seed_permutation.argtypes = [i64, ctypes.c_uint32, i32p]
     return _lib
 
 
@@ -103,6 +106,28 @@ def kmeans_assign_f32(points, cents) -> np.ndarray:
     out = np.empty(points.shape[0], np.int32)
     lib().mfo_kmeans_assign_f32(points, points.shape[0], cents, cents.shape[0],
                                 points.shape[1], out)
+    return out
+
+
+def kmeans_train(data, nlist: int, iters: int = 12, max_points_per_centroid: int = 256):
+    """CoarseQuantizer::train restated (see mflat_oracle_kmeans.cpp):
+    returns (centroids, assign, cell_start, reordered_ids)."""
+    data = _c(data)
+    n, dim = data.shape
+    nl = min(nlist, n)
+    cents = np.empty((nl, dim), np.float32)
+    assign = np.empty(n, np.int32)
+    start = np.empty(nl + 1, np.int32)
+    reord = np.empty(n, np.int32)
+    got = lib().mfo_kmeans_train(data, n, dim, nlist, iters, max_points_per_centroid, cents, assign,
+                                 start, reord)
+    assert got == nl
+    return cents, assign, start, reord
+
+
+def kmeans_seed_permutation(n: int, seed: int = 12345) -> np.ndarray:
+    out = np.empty(n, np.int32)
+    lib().mfo_kmeans_seed_permutation(n, seed, out)
     return out
 
 

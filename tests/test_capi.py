@@ -161,3 +161,24 @@ def test_persistence_argument_checks_without_device(built_lib, tmp_path):
         L.mflat_flat_free(h)
     else:
         assert h is None and st.value == 6
+
+
+def test_coarse_argument_checks_without_device(built_lib):
+    L = built_lib
+    st = ctypes.c_int(-1)
+    assert L.mflat_coarse_create(0, -1, ctypes.byref(st)) is None and st.value == 2
+    h = L.mflat_coarse_create(8, -1, ctypes.byref(st))
+    assert h and st.value == 0
+    f = np.zeros(16, np.float32)
+    fp = f.ctypes.data_as(ctypes.POINTER(ctypes.c_float))
+    ip = np.zeros(16, np.int32).ctypes.data_as(ctypes.POINTER(ctypes.c_int32))
+    assert L.mflat_coarse_train(None, fp, 2, 1, 1) == 1
+    assert L.mflat_coarse_train(h, None, 2, 1, 1) == 1
+    assert L.mflat_coarse_train(h, fp, 0, 1, 1) == 2
+    assert L.mflat_coarse_train(h, fp, 2, 0, 1) == 2
+    assert L.mflat_coarse_nlist(h) == 0 and L.mflat_coarse_size(h) == 0 and L.mflat_coarse_dim(h) == 8
+    assert L.mflat_coarse_centroids(h, fp) == 4          # not trained yet
+    assert L.mflat_coarse_csr(h, ip, ip) == 4
+    assert L.mflat_coarse_probe(h, fp, 1, 1, ip) == 4
+    assert L.mflat_coarse_probe(h, fp, 1, 0, ip) == 2
+    L.mflat_coarse_free(h)

@@ -90,3 +90,19 @@ def test_merge_shards_equals_single_shard():
         mi, md = O.merge_shards(np.stack(pi), np.stack(pd), metric)
         assert np.array_equal(mi, ref_i)
         assert np.array_equal(md, ref_d)
+
+
+def test_kmeans_oracle_self_consistent():
+    """The training restatement: the seed permutation is a permutation, the
+    CSR groups every point under its final cell, and the centroids are the
+    double means of the training subset's cells."""
+    p = O.kmeans_seed_permutation(1000)
+    assert np.array_equal(np.sort(p), np.arange(1000))
+    rng = np.random.default_rng(3)
+    x = rng.standard_normal((4000, 6)).astype(np.float32)
+    c, a, s, r = O.kmeans_train(x, 12, 4, 256)
+    assert s[0] == 0 and s[-1] == 4000 and np.all(np.diff(s) >= 0)
+    for cell in range(12):
+        ids = r[s[cell]:s[cell + 1]]
+        assert np.all(a[ids] == cell) and np.all(np.diff(ids) > 0)
+    assert np.array_equal(a, O.kmeans_assign_f32(x, c))
