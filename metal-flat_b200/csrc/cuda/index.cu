@@ -493,7 +493,7 @@ int run_screen(mflat_cu_index* ix, const float* queries, int m, int kp, int on_d
 
     if (ix->timing) cudaEventRecord(ix->ev[1], st);
     cudaError_t le;
-    if (ix->force_simt || d_pad > kMaxDPadResident) {
+    if (ix->force_simt) {
         le = launch_screen_simt(kp, sp, st);
     } else {
         CUtensorMap ta_hi, ta_lo, tb_hi, tb_lo;
@@ -632,7 +632,7 @@ int estimate_floor(mflat_cu_index* ix, const LargePlan& P, const ScreenParams& b
 }
 
 cudaError_t launch_pass(mflat_cu_index* ix, const ScreenParams& sp, int kp, cudaStream_t st) {
-    if (ix->force_simt || sp.d_pad > kMaxDPadResident) return launch_screen_simt(kp, sp, st);
+    if (ix->force_simt) return launch_screen_simt(kp, sp, st);
     CUtensorMap ta_hi, ta_lo, tb_hi, tb_lo;
     if (!make_map_f32(&ta_hi, sp.q_hi, sp.d_pad, sp.m_pad, kBM) ||
         !make_map_f32(&ta_lo, sp.q_lo, sp.d_pad, sp.m_pad, kBM) ||

@@ -19,10 +19,12 @@
 //   warps 0-3  epilogue: thread t owns query row t of the tile = TMEM lane t;
 //              reads 32 fp32 columns at a time with tcgen05.ld, forms the
 //              score s = alpha*dot + colbias[row] and keeps a register top-KP.
-//   warp 4     TMA producer: the query tile (A, hi and lo planes, all
-//              k-blocks) stays resident in shared memory for the unit; the
-//              database tile is streamed one (k-block, plane) of 32 KB per
-//              ring stage.
+//   warp 4     TMA producer: for d_pad <= 128 the query tile (A, hi and lo
+//              planes, all k-blocks) stays resident in shared memory for the
+//              unit and the database tile is streamed one (k-block, plane) of
+//              32 KB per ring stage; for larger d_pad each stage carries that
+//              k-block's query plane too (16 + 32 KB), and a k-block's hi and
+//              lo stages are consumed together.
 //   warp 5     TMEM allocator + MMA issuer (one thread), M=128 N=256 K=8,
 //              double-buffered accumulators (2 x 256 TMEM columns).
 #include "epilogue.cuh"
@@ -42,9 +44,18 @@ constexpr int kMaxStages = 6;
 constexpr int kSmemBudget = 7 * kStageBytes;      // A + ring <= 224 KB
 constexpr uint32_t kIdescTF32 = make_idesc(2u, kBM, kBN);
 
+// Query tile resident up to d_pad = 128 (4 k-blocks, 128 KB for both planes);
+// above, streamed with the database tile.
+__host__ __device__ inline bool a_streamed(int kb) { return kb * kBK > kMaxDPadResident; }
+__host__ __device__ inline int stage_bytes_for(int kb) {
+    return a_streamed(kb) ? kATileBytes + kStageBytes : kStageBytes;
+}
 __host__ __device__ inline int n_stages_for(int kb) {
-    const int s = (kSmemBudget - kb * 2 * kATileBytes) / kStageBytes;
-    return s > kMaxStages ? kMaxStages : s;
+    const int a = a_streamed(kb) ? 0 : kb * 2 * kATileBytes;
+    int s = (kSmemBudget - a) / stage_bytes_for(kb);
+    if (s > kMaxStages) s = kMaxStages;
+    if (a_streamed(kb)) s &= ~1;   // a k-block's hi and lo stages are used as a pair
+    return s;
 }
 
 struct SmemLayout {
@@ -64,8 +75,8 @@ struct SmemLayout {
 __device__ inline SmemLayout carve(uint8_t* base, int kb, int stages) {
     SmemLayout L;
     L.a = base;
-    L.b = base + kb * 2 * kATileBytes;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(L.b + stages * kStageBytes);
+    L.b = base + (a_streamed(kb) ? 0 : kb * 2 * kATileBytes);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(L.b + stages * stage_bytes_for(kb));
     L.full = bars;
     L.empty = bars + kMaxStages;
     L.a_full = bars + 2 * kMaxStages;
@@ -88,10 +99,12 @@ screen_tf32x3_kernel(const __grid_constant__ CUtensorMap tm_a_hi,
     uint8_t* base = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
     const int kb_count = p.d_pad / kBK;
-    if (kb_count < 1 || kb_count * kBK != p.d_pad || p.d_pad > kMaxDPadResident) {
+    if (kb_count < 1 || kb_count * kBK != p.d_pad) {
         if (threadIdx.x == 0) atomicExch(p.err, kErrConfig);
         return;
     }
+    const bool stream_a = a_streamed(kb_count);
+    const int sbytes = stage_bytes_for(kb_count);
     const int stages = n_stages_for(kb_count);
     SmemLayout S = carve(base, kb_count, stages);
 
@@ -144,23 +157,30 @@ screen_tf32x3_kernel(const __grid_constant__ CUtensorMap tm_a_hi,
                 const int ch = u / p.n_qtiles;
                 const int t0 = ch * p.tiles_per_chunk;
                 const int t1 = min(t0 + p.tiles_per_chunk, p.n_tiles);
-                if (!mbar_wait(S.a_empty, a_phase ^ 1u, abort_flag)) { ok = false; break; }
-                mbar_arrive_expect_tx(S.a_full, static_cast<uint32_t>(kb_count * 2 * kATileBytes));
-                for (int kb = 0; kb < kb_count; ++kb) {
-                    tma_load_2d(&tm_a_hi, S.a_full, S.a + kb * kATileBytes, kb * kBK, qt * kBM);
-                    tma_load_2d(&tm_a_lo, S.a_full, S.a + (kb_count + kb) * kATileBytes, kb * kBK,
-                                qt * kBM);
+                if (!stream_a) {
+                    if (!mbar_wait(S.a_empty, a_phase ^ 1u, abort_flag)) { ok = false; break; }
+                    mbar_arrive_expect_tx(S.a_full, static_cast<uint32_t>(kb_count * 2 * kATileBytes));
+                    for (int kb = 0; kb < kb_count; ++kb) {
+                        tma_load_2d(&tm_a_hi, S.a_full, S.a + kb * kATileBytes, kb * kBK, qt * kBM);
+                        tma_load_2d(&tm_a_lo, S.a_full, S.a + (kb_count + kb) * kATileBytes, kb * kBK,
+                                    qt * kBM);
+                    }
+                    a_issued = true;
+                    a_issue_phase = a_phase;
+                    a_phase ^= 1u;
                 }
-                a_issued = true;
-                a_issue_phase = a_phase;
-                a_phase ^= 1u;
                 for (int t = t0; t < t1 && ok; ++t) {
                     for (int kb = 0; kb < kb_count && ok; ++kb) {
                         for (int plane = 0; plane < 2; ++plane) {
                             if (!mbar_wait(&S.empty[stage], sphase ^ 1u, abort_flag)) { ok = false; break; }
-                            mbar_arrive_expect_tx(&S.full[stage], kStageBytes);
-                            tma_load_2d(plane ? &tm_b_lo : &tm_b_hi, &S.full[stage],
-                                        S.b + stage * kStageBytes, kb * kBK,
+                            uint8_t* dst = S.b + stage * sbytes;
+                            mbar_arrive_expect_tx(&S.full[stage], static_cast<uint32_t>(sbytes));
+                            if (stream_a) {
+                                tma_load_2d(plane ? &tm_a_lo : &tm_a_hi, &S.full[stage], dst, kb * kBK,
+                                            qt * kBM);
+                                dst += kATileBytes;
+                            }
+                            tma_load_2d(plane ? &tm_b_lo : &tm_b_hi, &S.full[stage], dst, kb * kBK,
                                         t * p.tile_stride * kBN);
                             issued_mask |= 1u << stage;
                             issued_phase = (issued_phase & ~(1u << stage)) | (sphase << stage);
@@ -188,9 +208,11 @@ screen_tf32x3_kernel(const __grid_constant__ CUtensorMap tm_a_hi,
                 const int ch = u / p.n_qtiles;
                 const int t0 = ch * p.tiles_per_chunk;
                 const int t1 = min(t0 + p.tiles_per_chunk, p.n_tiles);
-                if (!mbar_wait(S.a_full, a_phase, abort_flag)) { ok = false; break; }
-                a_phase ^= 1u;
-                tc_fence_after();
+                if (!stream_a) {
+                    if (!mbar_wait(S.a_full, a_phase, abort_flag)) { ok = false; break; }
+                    a_phase ^= 1u;
+                    tc_fence_after();
+                }
                 const uint32_t a_addr = smem_u32(S.a);
                 for (int t = t0; t < t1 && ok; ++t, ++tcount) {
                     const uint32_t b = tcount & 1u;
@@ -198,7 +220,36 @@ screen_tf32x3_kernel(const __grid_constant__ CUtensorMap tm_a_hi,
                     if (!mbar_wait(&S.acc_empty[b], ph ^ 1u, abort_flag)) { ok = false; break; }
                     tc_fence_after();
                     const uint32_t d_tmem = tmem_base + b * kBN;
-                    for (int kb = 0; kb < kb_count && ok; ++kb) {
+                    for (int kb = 0; kb < kb_count && ok && stream_a; ++kb) {
+                        // the k-block's hi stage [A_hi | B_hi] and lo stage [A_lo | B_lo]
+                        const int s_hi = stage;
+                        const uint32_t ph_hi = sphase;
+                        if (++stage == stages) { stage = 0; sphase ^= 1u; }
+                        const int s_lo = stage;
+                        const uint32_t ph_lo = sphase;
+                        if (++stage == stages) { stage = 0; sphase ^= 1u; }
+                        if (!mbar_wait(&S.full[s_hi], ph_hi, abort_flag) ||
+                            !mbar_wait(&S.full[s_lo], ph_lo, abort_flag)) { ok = false; break; }
+                        tc_fence_after();
+                        const uint32_t base_hi = smem_u32(S.b + s_hi * sbytes);
+                        const uint32_t base_lo = smem_u32(S.b + s_lo * sbytes);
+                        const uint64_t a_hi = smem_desc_k_sw128(base_hi);
+                        const uint64_t b_hi = smem_desc_k_sw128(base_hi + kATileBytes);
+                        const uint64_t a_lo = smem_desc_k_sw128(base_lo);
+                        const uint64_t b_lo = smem_desc_k_sw128(base_lo + kATileBytes);
+#pragma unroll
+                        for (int ks = 0; ks < kBK / 8; ++ks) {
+                            const uint64_t o = static_cast<uint64_t>(ks * 2);   // 32 B >> 4
+                            tc_mma_tf32(d_tmem, a_hi + o, b_hi + o, kIdescTF32,
+                                        (kb | ks) != 0 ? 1u : 0u);
+                            tc_mma_tf32(d_tmem, a_lo + o, b_hi + o, kIdescTF32, 1u);
+                            tc_mma_tf32(d_tmem, a_hi + o, b_lo + o, kIdescTF32, 1u);
+                        }
+                        issued_any = true;
+                        tc_commit(&S.empty[s_hi]);
+                        tc_commit(&S.empty[s_lo]);
+                    }
+                    for (int kb = 0; kb < kb_count && ok && !stream_a; ++kb) {
                         const uint64_t a_hi = smem_desc_k_sw128(a_addr + kb * kATileBytes);
                         const uint64_t a_lo =
                             smem_desc_k_sw128(a_addr + (kb_count + kb) * kATileBytes);
@@ -230,7 +281,7 @@ screen_tf32x3_kernel(const __grid_constant__ CUtensorMap tm_a_hi,
                     }
                     if (ok) tc_commit(&S.acc_full[b]);
                 }
-                if (ok) tc_commit(S.a_empty);
+                if (ok && !stream_a) tc_commit(S.a_empty);
             }
             if (*abort_flag && issued_any) {
                 tc_commit(S.drain);
@@ -350,13 +401,14 @@ cudaError_t launch_kp(const CUtensorMap& a_hi, const CUtensorMap& a_lo, const CU
 
 int screen_tf32x3_smem_bytes(int d_pad) {
     const int kb = d_pad / kBK;
-    return 1024 + kb * 2 * kATileBytes + n_stages_for(kb) * kStageBytes + 256;
+    const int a = a_streamed(kb) ? 0 : kb * 2 * kATileBytes;
+    return 1024 + a + n_stages_for(kb) * stage_bytes_for(kb) + 256;
 }
 
 cudaError_t launch_screen_tf32x3(int kp, const CUtensorMap& a_hi, const CUtensorMap& a_lo,
                                  const CUtensorMap& b_hi, const CUtensorMap& b_lo,
                                  const ScreenParams& p, int grid, cudaStream_t stream) {
-    if (p.d_pad % kBK != 0 || p.d_pad > kMaxDPadResident || p.d_pad < kBK) return cudaErrorInvalidValue;
+    if (p.d_pad % kBK != 0 || p.d_pad < kBK) return cudaErrorInvalidValue;
     switch (kp) {
         case 0: return launch_kp<4, true>(a_hi, a_lo, b_hi, b_lo, p, grid, stream);
         case 4: return launch_kp<4>(a_hi, a_lo, b_hi, b_lo, p, grid, stream);
