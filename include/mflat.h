@@ -201,6 +201,15 @@ MFLAT_API mflat_status_t mflat_coarse_csr(const mflat_coarse_t*, int32_t* out_ce
         int32_t* out_reordered_ids);
 MFLAT_API mflat_status_t mflat_coarse_probe(mflat_coarse_t*, const float* queries, int m,
         int nprobe, int32_t* out_cells);
+/* Sharded training over several GPUs, one process (or thread) per GPU: this
+ * handle holds global rows [row_offsets[rank], row_offsets[rank + 1]) and
+ * train() receives only those (n = that count); every rank calls train with
+ * the same nlist and iters.  The ranks all-gather per-cell double sums and
+ * counts over NCCL each iteration and add them in rank order: every rank gets
+ * the same centroids and the same global CSR (reordered ids are global).
+ * world = 1 turns sharding off.  row_offsets has world + 1 entries. */
+MFLAT_API mflat_status_t mflat_coarse_set_shard(mflat_coarse_t*, int rank, int world,
+        const uint8_t comm_id[MFLAT_COMM_ID_BYTES], const int64_t* row_offsets);
 
 /* Persistence of a flat index (the reference persists only its graph index:
  * GraphIndex::save / load, src/GraphIndex.mm:424-452, 'MFGR' header; this is

@@ -212,6 +212,56 @@ extern "C" int mflat_cu_index_set_shard(mflat_cu_index_t* ix, int rank, int worl
 // Used by the search path (index.cu) after enqueueing a sharded search with
 // host outputs.
 namespace mflat_cu {
+
+int comm_create(void** out, int rank, int world, const uint8_t* comm_id) {
+    *out = nullptr;
+    if (world < 2 || rank < 0 || rank >= world || !comm_id) return fail(ST_BAD_ARG, "bad communicator");
+    if (!nccl().ok) return fail(ST_DEVICE, "NCCL (libnccl.so.2) not available");
+    ncclUniqueId id;
+    std::memcpy(id.internal, comm_id, 128);
+    ncclComm_t comm = nullptr;
+    const ncclResult_t r = nccl().CommInitRank(&comm, world, id, rank);
+    if (r != ncclSuccess) return nccl_fail("ncclCommInitRank", r);
+    *out = comm;
+    return ST_OK;
+}
+
+void comm_destroy(void* comm) {
+    if (comm) nccl().CommDestroy(static_cast<ncclComm_t>(comm));
+}
+
+int comm_allgather_bytes(void* comm, const void* send, void* recv, size_t bytes, cudaStream_t st) {
+    const ncclResult_t r =
+        nccl().AllGather(send, recv, bytes, ncclChar, static_cast<ncclComm_t>(comm), st);
+    if (r != ncclSuccess) return nccl_fail("all-gather", r);
+    return ST_OK;
+}
+
+// Synchronise `st` while watching the communicator (as wait_collective); on a
+// peer failure or after MFLAT_NCCL_TIMEOUT_S the communicator is aborted and
+// *comm cleared.
+int comm_wait(void** comm, cudaStream_t st) {
+    const char* env = std::getenv("MFLAT_NCCL_TIMEOUT_S");
+    const double limit = env ? std::atof(env) : 300.0;
+    const auto t0 = std::chrono::steady_clock::now();
+    for (;;) {
+        const cudaError_t q = cudaStreamQuery(st);
+        if (q == cudaSuccess) return ST_OK;
+        if (q != cudaErrorNotReady) return fail(ST_DEVICE, "collective", q);
+        ncclResult_t ar = ncclSuccess;
+        nccl().CommGetAsyncError(static_cast<ncclComm_t>(*comm), &ar);
+        const double el = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+        if ((ar != ncclSuccess && ar != ncclInProgress) || el > limit) {
+            nccl().CommAbort(static_cast<ncclComm_t>(*comm));
+            *comm = nullptr;
+            return ar != ncclSuccess && ar != ncclInProgress
+                       ? nccl_fail("collective failed", ar)
+                       : fail(ST_DEVICE, "collective timed out; communicator aborted");
+        }
+        std::this_thread::sleep_for(std::chrono::microseconds(50));
+    }
+}
+
 int wait_stream_checked(mflat_cu_index* ix, cudaStream_t st) {
     if (ix->comm && ix->world > 1) return wait_collective(ix, st);
     CU_TRY(cudaStreamSynchronize(st), "search");

@@ -94,6 +94,11 @@ int run_screen(mflat_cu_index* ix, const float* queries, int m, int kp, int on_d
                cudaStream_t st, ScreenRun& out, int max_chunks = kMaxChunks);
 int check_device_error(mflat_cu_index* ix);
 void comm_release(mflat_cu_index* ix);
+// Plain communicator helpers (k-means training over sharded points).
+int comm_create(void** out, int rank, int world, const uint8_t* comm_id);
+void comm_destroy(void* comm);
+int comm_allgather_bytes(void* comm, const void* send, void* recv, size_t bytes, cudaStream_t st);
+int comm_wait(void** comm, cudaStream_t st);
 int shard_merge(mflat_cu_index* ix, int m, int k_out, int32_t* ids, float* dist, cudaStream_t st);
 // Synchronise `st`; with a communicator attached, watch it for peer failure.
 int wait_stream_checked(mflat_cu_index* ix, cudaStream_t st);

@@ -17,11 +17,20 @@
 // prefix sum of the cell histogram, reorderedIds = point ids grouped by cell,
 // ascending within a cell (the stable slot permutation).
 //
+// Sharded training (an addition; the reference trains on one device): each
+// rank holds a contiguous block of the points.  Per iteration every rank
+// forms per-cell double sums of its own training points (ascending training
+// order), the ranks all-gather those sums and the cell counts over NCCL, and
+// every rank adds the ranks' sums in rank order before dividing -- the same
+// centroids on every rank, deterministic for a given sharding.  Rows named by
+// global id (seeds, reseeds) are fetched from their owning rank the same way.
+//
 // Grouping uses CUB's device radix sort and scan (header library of the CUDA
 // toolkit); everything else is kernels of this file.
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstring>
 #include <cub/device/device_radix_sort.cuh>
 #include <cub/device/device_scan.cuh>
 #include <vector>
@@ -35,15 +44,19 @@ using namespace mflat_cu;
 struct mflat_cu_kmeans {
     int device = 0;
     int dim = 0;
-    int64_t n = 0, train_n = 0;
+    int64_t n = 0, train_n = 0;        // this rank's points / training points
     int nlist = 0;
+    int rank = 0, world = 1;
+    std::vector<int64_t> offsets;      // [world + 1]: global row range of every rank
+    void* comm = nullptr;
     cudaStream_t stream = nullptr;
     const float* data = nullptr;       // n x dim (owned when copied from the host)
     float* data_owned = nullptr;
     const float* train = nullptr;      // train_n x dim (== data when not subsampled)
     float* train_owned = nullptr;
     float* cents = nullptr;            // nlist x dim
-    DevBuf assign, keys_sorted, ids, ids_sorted, counts, offsets, temp, picks;
+    DevBuf assign, keys_sorted, ids, ids_sorted, counts, offsets_dev, temp, picks;
+    DevBuf sums, gsums, gcounts, rows, fetch, gfetch, gids, csr_start, csr_ids;
 };
 
 namespace {
@@ -57,9 +70,9 @@ __global__ void gather_rows_kernel(const float* __restrict__ src, const int32_t*
     dst[e] = src[static_cast<int64_t>(rows[i]) * dim + c];
 }
 
-__global__ void iota_kernel(int32_t* p, int64_t n) {
+__global__ void iota_kernel(int32_t* p, int64_t n, int32_t base) {
     const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (i < n) p[i] = static_cast<int32_t>(i);
+    if (i < n) p[i] = static_cast<int32_t>(i) + base;
 }
 
 __global__ void histogram_kernel(const int32_t* __restrict__ assign, int64_t n, int32_t* counts) {
@@ -67,36 +80,60 @@ __global__ void histogram_kernel(const int32_t* __restrict__ assign, int64_t n, 
     if (i < n) atomicAdd(counts + assign[i], 1);
 }
 
-// One warp per cell: cents[c] = mean of the cell's points (double sums in
-// ascending point order, then rounded to float); empty cells are left alone.
-__global__ void cell_mean_kernel(const float* __restrict__ pts, const int32_t* __restrict__ ids_sorted,
-                                 const int32_t* __restrict__ offsets, int nlist, int dim,
-                                 float* __restrict__ cents) {
+// One warp per cell: sums[c] = double sum of the cell's points in ascending
+// point order (0 for an empty cell).  ids_sorted holds local row indices.
+__global__ void cell_sum_kernel(const float* __restrict__ pts, const int32_t* __restrict__ ids_sorted,
+                                const int32_t* __restrict__ offsets, int nlist, int dim,
+                                double* __restrict__ sums) {
     const int c = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (c >= nlist) return;
     const int32_t j0 = offsets[c], j1 = offsets[c + 1];
-    if (j1 == j0) return;
-    const double cnt = static_cast<double>(j1 - j0);
-    for (int d0 = 0; d0 < dim; d0 += 32) {
-        const int d = d0 + lane;
+    for (int d = lane; d < dim; d += 32) {
         double acc = 0.0;
-        if (d < dim)
-            for (int32_t j = j0; j < j1; ++j)
-                acc += static_cast<double>(pts[static_cast<int64_t>(ids_sorted[j]) * dim + d]);
-        if (d < dim) cents[static_cast<int64_t>(c) * dim + d] = static_cast<float>(acc / cnt);
+        for (int32_t j = j0; j < j1; ++j)
+            acc += static_cast<double>(pts[static_cast<int64_t>(ids_sorted[j]) * dim + d]);
+        sums[static_cast<int64_t>(c) * dim + d] = acc;
     }
 }
 
-// cents[cells[i]] = train[rows[i]] for the reseeded (empty) cells.
-__global__ void reseed_kernel(const float* __restrict__ train, const int32_t* __restrict__ picks,
-                              int count, int dim, float* __restrict__ cents) {
-    const int e = blockIdx.x * blockDim.x + threadIdx.x;
-    if (e >= count * dim) return;
-    const int i = e / dim;
-    const int d = e - i * dim;
-    cents[static_cast<int64_t>(picks[2 * i]) * dim + d] =
-        train[static_cast<int64_t>(picks[2 * i + 1]) * dim + d];
+// Centroids of the non-empty cells from the ranks' sums, added in rank order;
+// total counts out.  world = 1 takes the one rank's sums as they are.
+__global__ void reduce_means_kernel(const double* __restrict__ gsums, const int32_t* __restrict__ gcounts,
+                                    int world, int nlist, int dim, float* __restrict__ cents,
+                                    int32_t* __restrict__ counts_total) {
+    const int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const int64_t per = static_cast<int64_t>(nlist) * dim;
+    if (e >= per) return;
+    const int c = static_cast<int>(e / dim);
+    int64_t cnt = 0;
+    for (int r = 0; r < world; ++r) cnt += gcounts[static_cast<int64_t>(r) * nlist + c];
+    if (e % dim == 0) counts_total[c] = static_cast<int32_t>(cnt);
+    if (cnt == 0) return;
+    double acc = gsums[e];
+    for (int r = 1; r < world; ++r) acc += gsums[r * per + e];
+    cents[e] = static_cast<float>(acc / static_cast<double>(cnt));
+}
+
+// out[i] = global row rows[i] when this rank owns it, else zeros.
+__global__ void pick_rows_kernel(const float* __restrict__ data, int64_t n_local, int64_t base,
+                                 const int64_t* __restrict__ rows, int count, int dim,
+                                 float* __restrict__ out) {
+    const int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (e >= static_cast<int64_t>(count) * dim) return;
+    const int64_t i = e / dim;
+    const int d = static_cast<int>(e - i * dim);
+    const int64_t r = rows[i] - base;
+    out[e] = (r >= 0 && r < n_local) ? data[r * dim + d] : 0.0f;
+}
+
+__global__ void set_rows_kernel(const int32_t* __restrict__ cells, const float* __restrict__ rows,
+                                int count, int dim, float* __restrict__ cents) {
+    const int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (e >= static_cast<int64_t>(count) * dim) return;
+    const int64_t i = e / dim;
+    const int d = static_cast<int>(e - i * dim);
+    cents[static_cast<int64_t>(cells[i]) * dim + d] = rows[e];
 }
 
 int key_bits(int nlist) {
@@ -105,40 +142,60 @@ int key_bits(int nlist) {
     return b;
 }
 
-// Group `m` assignments by cell: counts, offsets (nlist + 1), ids_sorted.
-int group_by_cell(mflat_cu_kmeans* k, int64_t m) {
+int sync(mflat_cu_kmeans* k, const char* what) {
+    if (k->world > 1) {
+        if (!k->comm) return fail(ST_DEVICE, "kmeans: communicator lost");
+        return comm_wait(&k->comm, k->stream);
+    }
+    CU_TRY(cudaStreamSynchronize(k->stream), what);
+    return ST_OK;
+}
+
+int allgather(mflat_cu_kmeans* k, const void* send, void* recv, size_t bytes) {
+    if (!k->comm) return fail(ST_DEVICE, "kmeans: communicator lost");
+    return comm_allgather_bytes(k->comm, send, recv, bytes, k->stream);
+}
+
+// Group `m` local assignments by cell: counts, offsets_dev (nlist + 1) and
+// ids_sorted (local row index + id_base, grouped by cell, ascending).
+int group_by_cell(mflat_cu_kmeans* k, int64_t m, int32_t id_base) {
     cudaStream_t st = k->stream;
     const int nl = k->nlist;
     CU_TRY(cudaMemsetAsync(k->counts.p, 0, static_cast<size_t>(nl) * sizeof(int32_t), st), "counts");
-    histogram_kernel<<<blocks_for(m, 256), 256, 0, st>>>(k->assign.as<int32_t>(), m,
-                                                          k->counts.as<int32_t>());
-    CU_TRY(cudaGetLastError(), "histogram launch");
-    iota_kernel<<<blocks_for(m, 256), 256, 0, st>>>(k->ids.as<int32_t>(), m);
-    CU_TRY(cudaGetLastError(), "iota launch");
-    size_t sort_bytes = 0, scan_bytes = 0;
-    CU_TRY(cub::DeviceRadixSort::SortPairs(nullptr, sort_bytes, k->assign.as<int32_t>(),
-                                           k->keys_sorted.as<int32_t>(), k->ids.as<int32_t>(),
-                                           k->ids_sorted.as<int32_t>(), static_cast<int>(m), 0,
-                                           key_bits(nl), st),
-           "sort size");
-    CU_TRY(cub::DeviceScan::ExclusiveSum(nullptr, scan_bytes, k->counts.as<int32_t>(),
-                                         k->offsets.as<int32_t>(), nl + 1, st),
-           "scan size");
-    CU_TRY(k->temp.ensure(std::max(sort_bytes, scan_bytes)), "sort scratch");
-    CU_TRY(cub::DeviceRadixSort::SortPairs(k->temp.p, sort_bytes, k->assign.as<int32_t>(),
-                                           k->keys_sorted.as<int32_t>(), k->ids.as<int32_t>(),
-                                           k->ids_sorted.as<int32_t>(), static_cast<int>(m), 0,
-                                           key_bits(nl), st),
-           "sort");
+    if (m > 0) {
+        histogram_kernel<<<blocks_for(m, 256), 256, 0, st>>>(k->assign.as<int32_t>(), m,
+                                                              k->counts.as<int32_t>());
+        CU_TRY(cudaGetLastError(), "histogram launch");
+        iota_kernel<<<blocks_for(m, 256), 256, 0, st>>>(k->ids.as<int32_t>(), m, id_base);
+        CU_TRY(cudaGetLastError(), "iota launch");
+        size_t sort_bytes = 0;
+        CU_TRY(cub::DeviceRadixSort::SortPairs(nullptr, sort_bytes, k->assign.as<int32_t>(),
+                                               k->keys_sorted.as<int32_t>(), k->ids.as<int32_t>(),
+                                               k->ids_sorted.as<int32_t>(), static_cast<int>(m), 0,
+                                               key_bits(nl), st),
+               "sort size");
+        CU_TRY(k->temp.ensure(sort_bytes), "sort scratch");
+        CU_TRY(cub::DeviceRadixSort::SortPairs(k->temp.p, sort_bytes, k->assign.as<int32_t>(),
+                                               k->keys_sorted.as<int32_t>(), k->ids.as<int32_t>(),
+                                               k->ids_sorted.as<int32_t>(), static_cast<int>(m), 0,
+                                               key_bits(nl), st),
+               "sort");
+    }
     // counts has nlist + 1 entries with a zero last one, so the scan's last
     // output is the total
+    size_t scan_bytes = 0;
+    CU_TRY(cub::DeviceScan::ExclusiveSum(nullptr, scan_bytes, k->counts.as<int32_t>(),
+                                         k->offsets_dev.as<int32_t>(), nl + 1, st),
+           "scan size");
+    CU_TRY(k->temp.ensure(scan_bytes), "scan scratch");
     CU_TRY(cub::DeviceScan::ExclusiveSum(k->temp.p, scan_bytes, k->counts.as<int32_t>(),
-                                         k->offsets.as<int32_t>(), nl + 1, st),
+                                         k->offsets_dev.as<int32_t>(), nl + 1, st),
            "scan");
     return ST_OK;
 }
 
 int assign_points(mflat_cu_kmeans* k, const float* pts, int64_t m) {
+    if (m == 0) return ST_OK;
     return mflat_cu_kmeans_assign(pts, m, k->cents, k->nlist, k->dim, k->assign.as<int32_t>(),
                                   k->device, 1, k->stream);
 }
@@ -148,10 +205,12 @@ int assign_points(mflat_cu_kmeans* k, const float* pts, int64_t m) {
 extern "C" {
 
 int mflat_cu_kmeans_create(int device, int dim, const float* data, int64_t n, int on_device,
-                           const int32_t* train_rows, int64_t train_n, int nlist,
+                           const int32_t* train_rows, int64_t train_n, int nlist, int rank,
+                           int world, const uint8_t* comm_id, const int64_t* row_offsets,
                            mflat_cu_kmeans_t** out) {
-    if (!out || !data || dim < 1 || n < 1 || nlist < 1 || nlist > n || train_n < 1 || train_n > n ||
-        (train_n < n && !train_rows))
+    if (!out || (!data && n > 0) || dim < 1 || n < 0 || nlist < 1 || train_n < 0 || train_n > n ||
+        (train_n > 0 && train_n < n && !train_rows) || world < 1 || rank < 0 || rank >= world ||
+        (world > 1 && (!comm_id || !row_offsets)))
         return fail(ST_BAD_ARG, "kmeans: bad argument");
     if (n > INT32_MAX - kBM) return fail(ST_BAD_ARG, "kmeans: too many points");
     *out = nullptr;
@@ -166,14 +225,31 @@ int mflat_cu_kmeans_create(int device, int dim, const float* data, int64_t n, in
     k->n = n;
     k->train_n = train_n;
     k->nlist = nlist;
+    k->rank = rank;
+    k->world = world;
+    k->offsets.assign(world + 1, 0);
+    if (world > 1) {
+        for (int r = 0; r <= world; ++r) k->offsets[r] = row_offsets[r];
+        if (k->offsets[rank + 1] - k->offsets[rank] != n) {
+            delete k;
+            return fail(ST_BAD_ARG, "kmeans: row offsets disagree with this rank's point count");
+        }
+    } else {
+        k->offsets[1] = n;
+    }
     auto bail = [&](int rc) {
         mflat_cu_kmeans_destroy(k);
         return rc;
     };
+    if (k->offsets[world] < nlist) return bail(fail(ST_BAD_ARG, "kmeans: fewer points than cells"));
     if (cudaStreamCreateWithFlags(&k->stream, cudaStreamNonBlocking) != cudaSuccess)
         return bail(fail(ST_DEVICE, "kmeans: stream"));
+    if (world > 1) {
+        const int rc = comm_create(&k->comm, rank, world, comm_id);
+        if (rc != ST_OK) return bail(rc);
+    }
     const size_t row = static_cast<size_t>(dim) * sizeof(float);
-    if (on_device) {
+    if (on_device || n == 0) {
         k->data = data;
     } else {
         if (cudaMalloc(&k->data_owned, static_cast<size_t>(n) * row) != cudaSuccess)
@@ -184,26 +260,35 @@ int mflat_cu_kmeans_create(int device, int dim, const float* data, int64_t n, in
         k->data = k->data_owned;
     }
     if (train_n < n) {
-        // the training rows' indices go through the reseed buffer
-        if (k->picks.ensure(static_cast<size_t>(train_n) * sizeof(int32_t)) != cudaSuccess ||
-            cudaMalloc(&k->train_owned, static_cast<size_t>(train_n) * row) != cudaSuccess)
-            return bail(fail(ST_ALLOC, "kmeans: training buffer"));
-        cudaMemcpyAsync(k->picks.p, train_rows, static_cast<size_t>(train_n) * sizeof(int32_t),
-                        cudaMemcpyHostToDevice, k->stream);
-        gather_rows_kernel<<<blocks_for(train_n * dim, 256), 256, 0, k->stream>>>(
-            k->data, k->picks.as<int32_t>(), train_n, dim, k->train_owned);
-        if (cudaGetLastError() != cudaSuccess || cudaStreamSynchronize(k->stream) != cudaSuccess)
-            return bail(fail(ST_DEVICE, "kmeans: gather"));
+        if (train_n > 0) {
+            if (k->picks.ensure(static_cast<size_t>(train_n) * sizeof(int32_t)) != cudaSuccess ||
+                cudaMalloc(&k->train_owned, static_cast<size_t>(train_n) * row) != cudaSuccess)
+                return bail(fail(ST_ALLOC, "kmeans: training buffer"));
+            cudaMemcpyAsync(k->picks.p, train_rows, static_cast<size_t>(train_n) * sizeof(int32_t),
+                            cudaMemcpyHostToDevice, k->stream);
+            gather_rows_kernel<<<blocks_for(train_n * dim, 256), 256, 0, k->stream>>>(
+                k->data, k->picks.as<int32_t>(), train_n, dim, k->train_owned);
+            if (cudaGetLastError() != cudaSuccess || cudaStreamSynchronize(k->stream) != cudaSuccess)
+                return bail(fail(ST_DEVICE, "kmeans: gather"));
+        }
         k->train = k->train_owned;
     } else {
         k->train = k->data;
     }
-    const size_t m = static_cast<size_t>(n);
-    if (cudaMalloc(&k->cents, static_cast<size_t>(nlist) * row) != cudaSuccess ||
+    // grouped ids are all-gathered at the end, padded to the largest shard:
+    // size the id buffers for that up front (a later grow would drop them)
+    int64_t max_n = 1;
+    for (int r = 0; r < world; ++r) max_n = std::max(max_n, k->offsets[r + 1] - k->offsets[r]);
+    const size_t m = static_cast<size_t>(max_n);
+    const size_t per = static_cast<size_t>(nlist) * dim;
+    if (cudaMalloc(&k->cents, per * sizeof(float)) != cudaSuccess ||
         k->assign.ensure(m * 4) != cudaSuccess || k->keys_sorted.ensure(m * 4) != cudaSuccess ||
         k->ids.ensure(m * 4) != cudaSuccess || k->ids_sorted.ensure(m * 4) != cudaSuccess ||
         k->counts.ensure((static_cast<size_t>(nlist) + 1) * 4) != cudaSuccess ||
-        k->offsets.ensure((static_cast<size_t>(nlist) + 1) * 4) != cudaSuccess)
+        k->offsets_dev.ensure((static_cast<size_t>(nlist) + 1) * 4) != cudaSuccess ||
+        k->sums.ensure(per * sizeof(double)) != cudaSuccess ||
+        (world > 1 && (k->gsums.ensure(per * world * sizeof(double)) != cudaSuccess ||
+                       k->gcounts.ensure(static_cast<size_t>(nlist) * world * 4) != cudaSuccess)))
         return bail(fail(ST_ALLOC, "kmeans: work buffers"));
     if (cudaMemsetAsync(k->counts.p, 0, (static_cast<size_t>(nlist) + 1) * 4, k->stream) != cudaSuccess ||
         cudaStreamSynchronize(k->stream) != cudaSuccess)
@@ -216,11 +301,13 @@ void mflat_cu_kmeans_destroy(mflat_cu_kmeans_t* k) {
     if (!k) return;
     DeviceGuard g(k->device);
     if (k->stream) cudaStreamSynchronize(k->stream);
+    comm_destroy(k->comm);
     cudaFree(k->data_owned);
     cudaFree(k->train_owned);
     cudaFree(k->cents);
-    for (DevBuf* b : {&k->assign, &k->keys_sorted, &k->ids, &k->ids_sorted, &k->counts, &k->offsets,
-                      &k->temp, &k->picks})
+    for (DevBuf* b : {&k->assign, &k->keys_sorted, &k->ids, &k->ids_sorted, &k->counts, &k->offsets_dev,
+                      &k->temp, &k->picks, &k->sums, &k->gsums, &k->gcounts, &k->rows, &k->fetch,
+                      &k->gfetch, &k->gids, &k->csr_start, &k->csr_ids})
         b->release();
     if (k->stream) cudaStreamDestroy(k->stream);
     delete k;
@@ -247,48 +334,98 @@ int mflat_cu_kmeans_get_centroids(mflat_cu_kmeans_t* k, float* host_out) {
     return ST_OK;
 }
 
+int mflat_cu_kmeans_fetch_rows(mflat_cu_kmeans_t* k, const int64_t* host_rows, int count,
+                               float* host_out) {
+    if (!k || count < 0 || (count > 0 && (!host_rows || !host_out)))
+        return fail(ST_BAD_ARG, "kmeans: bad argument");
+    const int64_t total = k->offsets[k->world];
+    for (int i = 0; i < count; ++i)
+        if (host_rows[i] < 0 || host_rows[i] >= total) return fail(ST_BAD_ARG, "kmeans: row out of range");
+    if (count == 0) return ST_OK;
+    DeviceGuard g(k->device);
+    const size_t bytes = static_cast<size_t>(count) * k->dim * sizeof(float);
+    CU_TRY(k->rows.ensure(static_cast<size_t>(count) * sizeof(int64_t)), "row ids");
+    CU_TRY(k->fetch.ensure(bytes), "fetch buffer");
+    CU_TRY(cudaMemcpyAsync(k->rows.p, host_rows, static_cast<size_t>(count) * sizeof(int64_t),
+                           cudaMemcpyHostToDevice, k->stream),
+           "row ids");
+    pick_rows_kernel<<<blocks_for(static_cast<int64_t>(count) * k->dim, 256), 256, 0, k->stream>>>(
+        k->data, k->n, k->offsets[k->rank], k->rows.as<int64_t>(), count, k->dim, k->fetch.as<float>());
+    CU_TRY(cudaGetLastError(), "fetch launch");
+    if (k->world == 1) {
+        CU_TRY(cudaMemcpyAsync(host_out, k->fetch.p, bytes, cudaMemcpyDeviceToHost, k->stream), "fetch");
+        return sync(k, "fetch");
+    }
+    CU_TRY(k->gfetch.ensure(bytes * k->world), "fetch gather buffer");
+    int rc = allgather(k, k->fetch.p, k->gfetch.p, bytes);
+    if (rc != ST_OK) return rc;
+    std::vector<float> all(static_cast<size_t>(count) * k->dim * k->world);
+    CU_TRY(cudaMemcpyAsync(all.data(), k->gfetch.p, bytes * k->world, cudaMemcpyDeviceToHost, k->stream),
+           "fetch");
+    rc = sync(k, "fetch");
+    if (rc != ST_OK) return rc;
+    const size_t row = static_cast<size_t>(k->dim);
+    for (int i = 0; i < count; ++i) {
+        int owner = 0;
+        while (host_rows[i] >= k->offsets[owner + 1]) ++owner;
+        std::memcpy(host_out + i * row, &all[(static_cast<size_t>(owner) * count + i) * row],
+                    row * sizeof(float));
+    }
+    return ST_OK;
+}
+
+int mflat_cu_kmeans_set_rows(mflat_cu_kmeans_t* k, const int32_t* host_cells, const float* host_rows,
+                             int count) {
+    if (!k || count < 0 || (count > 0 && (!host_cells || !host_rows)))
+        return fail(ST_BAD_ARG, "kmeans: bad argument");
+    for (int i = 0; i < count; ++i)
+        if (host_cells[i] < 0 || host_cells[i] >= k->nlist) return fail(ST_BAD_ARG, "kmeans: cell out of range");
+    if (count == 0) return ST_OK;
+    DeviceGuard g(k->device);
+    const size_t bytes = static_cast<size_t>(count) * k->dim * sizeof(float);
+    CU_TRY(k->picks.ensure(static_cast<size_t>(count) * sizeof(int32_t)), "cell ids");
+    CU_TRY(k->fetch.ensure(bytes), "row buffer");
+    CU_TRY(cudaMemcpyAsync(k->picks.p, host_cells, static_cast<size_t>(count) * sizeof(int32_t),
+                           cudaMemcpyHostToDevice, k->stream),
+           "cell ids");
+    CU_TRY(cudaMemcpyAsync(k->fetch.p, host_rows, bytes, cudaMemcpyHostToDevice, k->stream), "rows");
+    set_rows_kernel<<<blocks_for(static_cast<int64_t>(count) * k->dim, 256), 256, 0, k->stream>>>(
+        k->picks.as<int32_t>(), k->fetch.as<float>(), count, k->dim, k->cents);
+    CU_TRY(cudaGetLastError(), "set rows launch");
+    CU_TRY(cudaStreamSynchronize(k->stream), "set rows");
+    return ST_OK;
+}
+
 int mflat_cu_kmeans_iterate(mflat_cu_kmeans_t* k, int32_t* host_counts) {
     if (!k || !host_counts) return fail(ST_BAD_ARG, "kmeans: bad argument");
     DeviceGuard g(k->device);
     int rc = assign_points(k, k->train, k->train_n);
     if (rc != ST_OK) return rc;
-    rc = group_by_cell(k, k->train_n);
+    rc = group_by_cell(k, k->train_n, 0);
     if (rc != ST_OK) return rc;
     const int warps_per_block = 8;
-    cell_mean_kernel<<<(k->nlist + warps_per_block - 1) / warps_per_block, warps_per_block * 32, 0,
-                       k->stream>>>(k->train, k->ids_sorted.as<int32_t>(), k->offsets.as<int32_t>(),
-                                    k->nlist, k->dim, k->cents);
+    cell_sum_kernel<<<(k->nlist + warps_per_block - 1) / warps_per_block, warps_per_block * 32, 0,
+                      k->stream>>>(k->train, k->ids_sorted.as<int32_t>(), k->offsets_dev.as<int32_t>(),
+                                   k->nlist, k->dim, k->sums.as<double>());
+    CU_TRY(cudaGetLastError(), "cell sum launch");
+    const size_t per = static_cast<size_t>(k->nlist) * k->dim;
+    const double* gs = k->sums.as<double>();
+    const int32_t* gc = k->counts.as<int32_t>();
+    if (k->world > 1) {
+        rc = allgather(k, k->sums.p, k->gsums.p, per * sizeof(double));
+        if (rc == ST_OK) rc = allgather(k, k->counts.p, k->gcounts.p, static_cast<size_t>(k->nlist) * 4);
+        if (rc != ST_OK) return rc;
+        gs = k->gsums.as<double>();
+        gc = k->gcounts.as<int32_t>();
+    }
+    // the total counts land in offsets_dev (free until the next grouping)
+    reduce_means_kernel<<<blocks_for(static_cast<int64_t>(per), 256), 256, 0, k->stream>>>(
+        gs, gc, k->world, k->nlist, k->dim, k->cents, k->offsets_dev.as<int32_t>());
     CU_TRY(cudaGetLastError(), "centroid update launch");
-    CU_TRY(cudaMemcpyAsync(host_counts, k->counts.p, static_cast<size_t>(k->nlist) * sizeof(int32_t),
+    CU_TRY(cudaMemcpyAsync(host_counts, k->offsets_dev.p, static_cast<size_t>(k->nlist) * sizeof(int32_t),
                            cudaMemcpyDeviceToHost, k->stream),
            "counts download");
-    CU_TRY(cudaStreamSynchronize(k->stream), "k-means iteration");
-    return ST_OK;
-}
-
-int mflat_cu_kmeans_reseed(mflat_cu_kmeans_t* k, const int32_t* host_cells,
-                           const int32_t* host_train_rows, int count) {
-    if (!k || count < 0 || (count > 0 && (!host_cells || !host_train_rows)))
-        return fail(ST_BAD_ARG, "kmeans: bad argument");
-    if (count == 0) return ST_OK;
-    std::vector<int32_t> picks(2 * static_cast<size_t>(count));
-    for (int i = 0; i < count; ++i) {
-        if (host_cells[i] < 0 || host_cells[i] >= k->nlist || host_train_rows[i] < 0 ||
-            host_train_rows[i] >= k->train_n)
-            return fail(ST_BAD_ARG, "kmeans: reseed index out of range");
-        picks[2 * i] = host_cells[i];
-        picks[2 * i + 1] = host_train_rows[i];
-    }
-    DeviceGuard g(k->device);
-    CU_TRY(k->picks.ensure(picks.size() * sizeof(int32_t)), "reseed buffer");
-    CU_TRY(cudaMemcpyAsync(k->picks.p, picks.data(), picks.size() * sizeof(int32_t),
-                           cudaMemcpyHostToDevice, k->stream),
-           "reseed upload");
-    reseed_kernel<<<blocks_for(static_cast<int64_t>(count) * k->dim, 256), 256, 0, k->stream>>>(
-        k->train, k->picks.as<int32_t>(), count, k->dim, k->cents);
-    CU_TRY(cudaGetLastError(), "reseed launch");
-    CU_TRY(cudaStreamSynchronize(k->stream), "reseed");
-    return ST_OK;
+    return sync(k, "k-means iteration");
 }
 
 int mflat_cu_kmeans_finish(mflat_cu_kmeans_t* k, int32_t* host_assign, int32_t* host_cell_start,
@@ -297,31 +434,74 @@ int mflat_cu_kmeans_finish(mflat_cu_kmeans_t* k, int32_t* host_assign, int32_t* 
     DeviceGuard g(k->device);
     int rc = assign_points(k, k->data, k->n);
     if (rc != ST_OK) return rc;
-    rc = group_by_cell(k, k->n);
+    const int32_t base = static_cast<int32_t>(k->offsets[k->rank]);
+    rc = group_by_cell(k, k->n, base);
     if (rc != ST_OK) return rc;
-    if (host_assign)
+    if (host_assign && k->n > 0)
         CU_TRY(cudaMemcpyAsync(host_assign, k->assign.p, static_cast<size_t>(k->n) * sizeof(int32_t),
                                cudaMemcpyDeviceToHost, k->stream),
                "assignment download");
-    if (host_cell_start)
-        CU_TRY(cudaMemcpyAsync(host_cell_start, k->offsets.p,
-                               (static_cast<size_t>(k->nlist) + 1) * sizeof(int32_t),
-                               cudaMemcpyDeviceToHost, k->stream),
-               "cell start download");
-    if (host_reordered)
-        CU_TRY(cudaMemcpyAsync(host_reordered, k->ids_sorted.p, static_cast<size_t>(k->n) * sizeof(int32_t),
-                               cudaMemcpyDeviceToHost, k->stream),
-               "permutation download");
-    CU_TRY(cudaStreamSynchronize(k->stream), "k-means finish");
+    const int nl = k->nlist;
+    const int64_t total = k->offsets[k->world];
+    if (k->world == 1) {
+        if (host_cell_start)
+            CU_TRY(cudaMemcpyAsync(host_cell_start, k->offsets_dev.p, (static_cast<size_t>(nl) + 1) * 4,
+                                   cudaMemcpyDeviceToHost, k->stream),
+                   "cell start download");
+        if (host_reordered)
+            CU_TRY(cudaMemcpyAsync(host_reordered, k->ids_sorted.p, static_cast<size_t>(k->n) * 4,
+                                   cudaMemcpyDeviceToHost, k->stream),
+                   "permutation download");
+        return sync(k, "k-means finish");
+    }
+    // every rank's counts and grouped ids (padded to the largest shard)
+    int64_t max_n = 1;
+    for (int r = 0; r < k->world; ++r) max_n = std::max(max_n, k->offsets[r + 1] - k->offsets[r]);
+    CU_TRY(k->gids.ensure(static_cast<size_t>(max_n) * 4 * k->world), "id gather buffer");
+    rc = allgather(k, k->counts.p, k->gcounts.p, static_cast<size_t>(nl) * 4);
+    if (rc == ST_OK) rc = allgather(k, k->ids_sorted.p, k->gids.p, static_cast<size_t>(max_n) * 4);
+    if (rc != ST_OK) return rc;
+    std::vector<int32_t> cnt(static_cast<size_t>(nl) * k->world), ids(static_cast<size_t>(max_n) * k->world);
+    CU_TRY(cudaMemcpyAsync(cnt.data(), k->gcounts.p, cnt.size() * 4, cudaMemcpyDeviceToHost, k->stream),
+           "count download");
+    CU_TRY(cudaMemcpyAsync(ids.data(), k->gids.p, ids.size() * 4, cudaMemcpyDeviceToHost, k->stream),
+           "id download");
+    rc = sync(k, "k-means finish");
+    if (rc != ST_OK) return rc;
+    // global CSR: cells in order, within a cell the ranks in order (= ascending id)
+    std::vector<int32_t> start(static_cast<size_t>(nl) + 1, 0), reord(static_cast<size_t>(total));
+    std::vector<int64_t> cursor(k->world, 0);
+    for (int c = 0; c < nl; ++c) {
+        int64_t pos = start[c];
+        for (int r = 0; r < k->world; ++r) {
+            const int32_t m = cnt[static_cast<size_t>(r) * nl + c];
+            const int32_t* src = &ids[static_cast<size_t>(r) * max_n + cursor[r]];
+            std::memcpy(&reord[pos], src, static_cast<size_t>(m) * 4);
+            cursor[r] += m;
+            pos += m;
+        }
+        start[c + 1] = static_cast<int32_t>(pos);
+    }
+    CU_TRY(k->csr_start.ensure(start.size() * 4), "CSR buffer");
+    CU_TRY(k->csr_ids.ensure(std::max<size_t>(reord.size(), 1) * 4), "CSR buffer");
+    CU_TRY(cudaMemcpyAsync(k->csr_start.p, start.data(), start.size() * 4, cudaMemcpyHostToDevice, k->stream),
+           "CSR upload");
+    CU_TRY(cudaMemcpyAsync(k->csr_ids.p, reord.data(), reord.size() * 4, cudaMemcpyHostToDevice, k->stream),
+           "CSR upload");
+    CU_TRY(cudaStreamSynchronize(k->stream), "CSR upload");
+    if (host_cell_start) std::memcpy(host_cell_start, start.data(), start.size() * 4);
+    if (host_reordered) std::memcpy(host_reordered, reord.data(), reord.size() * 4);
     return ST_OK;
 }
 
 const int32_t* mflat_cu_kmeans_cell_start_device(const mflat_cu_kmeans_t* k) {
-    return k ? static_cast<const int32_t*>(k->offsets.p) : nullptr;
+    if (!k) return nullptr;
+    return static_cast<const int32_t*>(k->world > 1 ? k->csr_start.p : k->offsets_dev.p);
 }
 
 const int32_t* mflat_cu_kmeans_reordered_device(const mflat_cu_kmeans_t* k) {
-    return k ? static_cast<const int32_t*>(k->ids_sorted.p) : nullptr;
+    if (!k) return nullptr;
+    return static_cast<const int32_t*>(k->world > 1 ? k->csr_ids.p : k->ids_sorted.p);
 }
 
 }  // extern "C"

@@ -70,26 +70,38 @@ MFLAT_CU_API int mflat_cu_kmeans_assign(const float* points, int64_t n, const fl
                                         int ncentroids, int dim, int32_t* out_assign,
                                         int device, int on_device, void* stream);
 
-/* k-means training session (CoarseQuantizer::train).  create uploads the
- * points (or borrows device points) and gathers the training subset given by
- * train_rows (train_n < n) -- the host draws it, with the seeds and the
- * empty-cell reseeds, from its own mt19937.  iterate = assignment of the
- * training points + centroid means of the non-empty cells (double sums in
- * ascending point order), cell counts to host_counts[nlist]; empty cells keep
- * their centroid until reseed.  finish = assignment of all points + CSR:
- * cell_start[nlist + 1] (prefix sums) and reordered[n] (point ids grouped by
- * cell, ascending within a cell); each output pointer may be NULL.  The CSR
- * also stays on the device (the *_device accessors) until destroy. */
+/* k-means training session (CoarseQuantizer::train).  create uploads this
+ * rank's points (or borrows device points) and gathers its training rows
+ * (train_rows: local row indices, NULL when train_n == n = all rows in
+ * order); the host draws the seeds, the training subset and the empty-cell
+ * reseeds from its own mt19937.  Sharded training: world > 1 ranks, each with
+ * a contiguous block of rows, row_offsets[world + 1] giving every rank's
+ * global range, comm_id from mflat_cu_comm_unique_id; the calls marked
+ * (collective) must then be made by every rank in the same order.
+ *   fetch_rows (collective): global rows -> host, from their owning ranks.
+ *   set_rows: centroid cells[i] = rows[i] (host data).
+ *   iterate (collective): assignment of the training points + centroid means
+ *     of the non-empty cells (per-rank double sums in ascending training
+ *     order, added across ranks in rank order); the cells' total counts go to
+ *     host_counts[nlist]; empty cells keep their centroid.
+ *   finish (collective): assignment of every point + global CSR:
+ *     cell_start[nlist + 1], reordered[total] (global point ids grouped by
+ *     cell, ascending within a cell); host_assign gets this rank's
+ *     assignments.  Output pointers may be NULL.  The CSR also stays on the
+ *     device (the *_device accessors) until destroy. */
 typedef struct mflat_cu_kmeans mflat_cu_kmeans_t;
 MFLAT_CU_API int mflat_cu_kmeans_create(int device, int dim, const float* points, int64_t n,
                                         int on_device, const int32_t* train_rows, int64_t train_n,
-                                        int nlist, mflat_cu_kmeans_t** out);
+                                        int nlist, int rank, int world, const uint8_t* comm_id,
+                                        const int64_t* row_offsets, mflat_cu_kmeans_t** out);
 MFLAT_CU_API void mflat_cu_kmeans_destroy(mflat_cu_kmeans_t* k);
 MFLAT_CU_API int mflat_cu_kmeans_set_centroids(mflat_cu_kmeans_t* k, const float* host_centroids);
 MFLAT_CU_API int mflat_cu_kmeans_get_centroids(mflat_cu_kmeans_t* k, float* host_out);
+MFLAT_CU_API int mflat_cu_kmeans_fetch_rows(mflat_cu_kmeans_t* k, const int64_t* host_rows,
+                                            int count, float* host_out);
+MFLAT_CU_API int mflat_cu_kmeans_set_rows(mflat_cu_kmeans_t* k, const int32_t* host_cells,
+                                          const float* host_rows, int count);
 MFLAT_CU_API int mflat_cu_kmeans_iterate(mflat_cu_kmeans_t* k, int32_t* host_counts);
-MFLAT_CU_API int mflat_cu_kmeans_reseed(mflat_cu_kmeans_t* k, const int32_t* host_cells,
-                                        const int32_t* host_train_rows, int count);
 MFLAT_CU_API int mflat_cu_kmeans_finish(mflat_cu_kmeans_t* k, int32_t* host_assign,
                                         int32_t* host_cell_start, int32_t* host_reordered);
 MFLAT_CU_API const int32_t* mflat_cu_kmeans_cell_start_device(const mflat_cu_kmeans_t* k);

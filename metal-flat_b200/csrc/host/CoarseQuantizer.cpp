@@ -17,6 +17,7 @@
 // the mt19937 stream, so seeds and reseeds draw exactly as the reference's
 // host code does.
 #include <algorithm>
+#include <climits>
 #include <cstring>
 #include <random>
 #include <stdexcept>
@@ -60,6 +61,7 @@ void seed_shuffle(std::vector<int>& perm, std::mt19937& g) {
 }
 
 constexpr int kMaxPointsPerCentroid = 256;   // faiss convention (CoarseQuantizer.mm:118-121)
+constexpr int MFLAT_COMM_ID_BYTES_CU = 128;   // NCCL unique id (mflat_cu_comm_unique_id)
 
 }  // namespace
 
@@ -73,6 +75,9 @@ void kmeansSeedPermutation(int n, uint32_t seed, std::vector<int>& perm) {
 struct CoarseQuantizer::Impl {
     int dim = 0;
     int device = -1;
+    int rank = 0, world = 1;                // sharded training (setShard)
+    std::vector<uint8_t> commId;
+    std::vector<int64_t> rowOffsets;        // [world + 1]
     int nlist = 0;
     int dbCount = 0;
     std::vector<float> centroids;
@@ -92,61 +97,114 @@ CoarseQuantizer::CoarseQuantizer(int dim, int device) : mImpl(std::make_unique<I
 
 CoarseQuantizer::~CoarseQuantizer() = default;
 
+void CoarseQuantizer::setShard(int rank, int world, const uint8_t* comm_id, const int64_t* row_offsets) {
+    if (world < 1 || rank < 0 || rank >= world)
+        throw std::invalid_argument("CoarseQuantizer::setShard: bad rank / world");
+    if (world == 1) {
+        mImpl->rank = 0;
+        mImpl->world = 1;
+        mImpl->commId.clear();
+        mImpl->rowOffsets.clear();
+        return;
+    }
+    if (!comm_id || !row_offsets) throw std::invalid_argument("CoarseQuantizer::setShard: null argument");
+    for (int r = 0; r < world; ++r)
+        if (row_offsets[r] < 0 || row_offsets[r + 1] < row_offsets[r])
+            throw std::invalid_argument("CoarseQuantizer::setShard: row offsets must be non-decreasing");
+    mImpl->rank = rank;
+    mImpl->world = world;
+    mImpl->commId.assign(comm_id, comm_id + MFLAT_COMM_ID_BYTES_CU);
+    mImpl->rowOffsets.assign(row_offsets, row_offsets + world + 1);
+}
+
 void CoarseQuantizer::train(const float* data, int n, int nlistReq, int iters, KmeansBackend) {
-    if (!data || n <= 0) throw std::invalid_argument("CoarseQuantizer::train: no points");
+    const bool sharded = mImpl->world > 1;
+    if ((!data && n > 0) || n < 0 || (!sharded && n == 0))
+        throw std::invalid_argument("CoarseQuantizer::train: no points");
     if (nlistReq <= 0) throw std::invalid_argument("CoarseQuantizer::train: nlist must be positive");
     if (iters < 0) throw std::invalid_argument("CoarseQuantizer::train: negative iteration count");
+    const int64_t base = sharded ? mImpl->rowOffsets[mImpl->rank] : 0;
+    const int64_t total = sharded ? mImpl->rowOffsets[mImpl->world] : n;
+    if (sharded && mImpl->rowOffsets[mImpl->rank + 1] - base != n)
+        throw std::invalid_argument("CoarseQuantizer::train: n differs from this rank's row range");
+    if (total <= 0 || total > INT32_MAX - 256) throw std::invalid_argument("CoarseQuantizer::train: bad size");
     const int dim = mImpl->dim;
-    const int nlist = std::min(nlistReq, n);
+    const int nlist = static_cast<int>(std::min<int64_t>(nlistReq, total));
     const size_t row = static_cast<size_t>(dim);
+    const int nt = static_cast<int>(total);
 
-    // seeds: shuffled ids, centroid c = row perm[c % n]
+    // seeds: shuffled global ids, centroid c = row perm[c % total]
     std::mt19937 rng(12345);
-    std::vector<int> perm(n);
-    for (int i = 0; i < n; ++i) perm[i] = i;
+    std::vector<int> perm(nt);
+    for (int i = 0; i < nt; ++i) perm[i] = i;
     seed_shuffle(perm, rng);
-    std::vector<float> cents(static_cast<size_t>(nlist) * row);
-    for (int c = 0; c < nlist; ++c)
-        std::memcpy(&cents[c * row], data + static_cast<size_t>(perm[c % n]) * row, row * sizeof(float));
 
-    // training subset: the first 256 * nlist shuffled ids, when fewer than n
-    int64_t trainN = n;
-    if (static_cast<int64_t>(kMaxPointsPerCentroid) * nlist < n)
+    // training subset: the first 256 * nlist shuffled ids, when fewer than all;
+    // this rank trains on the ones it holds, in shuffled order
+    int64_t trainN = total;
+    if (static_cast<int64_t>(kMaxPointsPerCentroid) * nlist < total)
         trainN = static_cast<int64_t>(kMaxPointsPerCentroid) * nlist;
+    const bool subsampled = trainN < total;
+    std::vector<int32_t> localTrain;
+    if (subsampled) {
+        for (int64_t i = 0; i < trainN; ++i) {
+            const int64_t g = perm[i];
+            if (g >= base && g < base + n) localTrain.push_back(static_cast<int32_t>(g - base));
+        }
+    }
 
     mflat_cu_kmeans_destroy(mImpl->session);
     mImpl->session = nullptr;
     mImpl->coarse.reset();
     mflat_cu_kmeans_t* k = nullptr;
-    check(mflat_cu_kmeans_create(mImpl->device, dim, data, n, 0, trainN < n ? perm.data() : nullptr,
-                                 trainN, nlist, &k),
+    check(mflat_cu_kmeans_create(mImpl->device, dim, data, n, 0, subsampled ? localTrain.data() : nullptr,
+                                 subsampled ? static_cast<int64_t>(localTrain.size()) : n, nlist,
+                                 mImpl->rank, mImpl->world, sharded ? mImpl->commId.data() : nullptr,
+                                 sharded ? mImpl->rowOffsets.data() : nullptr, &k),
           "kmeans create");
     mImpl->session = k;
+
+    std::vector<float> cents(static_cast<size_t>(nlist) * row);
+    if (sharded) {
+        std::vector<int64_t> seedRows(nlist);
+        for (int c = 0; c < nlist; ++c) seedRows[c] = perm[c % nt];
+        check(mflat_cu_kmeans_fetch_rows(k, seedRows.data(), nlist, cents.data()), "kmeans seeds");
+    } else {
+        for (int c = 0; c < nlist; ++c)
+            std::memcpy(&cents[c * row], data + static_cast<size_t>(perm[c % nt]) * row, row * sizeof(float));
+    }
     check(mflat_cu_kmeans_set_centroids(k, cents.data()), "kmeans seeds");
 
-    std::vector<int32_t> counts(nlist), cells, rows;
+    std::vector<int32_t> counts(nlist), cells;
+    std::vector<int64_t> rows;
+    std::vector<float> rowData;
     for (int it = 0; it < iters; ++it) {
         check(mflat_cu_kmeans_iterate(k, counts.data()), "kmeans iteration");
         cells.clear();
         rows.clear();
         for (int c = 0; c < nlist; ++c) {
             if (counts[c] == 0) {
+                const int64_t r = static_cast<int64_t>(rng() % static_cast<unsigned>(trainN));
                 cells.push_back(c);
-                rows.push_back(static_cast<int32_t>(rng() % static_cast<unsigned>(trainN)));
+                rows.push_back(subsampled ? perm[r] : r);   // training row r, as a global row id
             }
         }
-        check(mflat_cu_kmeans_reseed(k, cells.data(), rows.data(), static_cast<int>(cells.size())),
-              "kmeans reseed");
+        if (!cells.empty()) {
+            rowData.resize(cells.size() * row);
+            const int cnt = static_cast<int>(cells.size());
+            check(mflat_cu_kmeans_fetch_rows(k, rows.data(), cnt, rowData.data()), "kmeans reseed");
+            check(mflat_cu_kmeans_set_rows(k, cells.data(), rowData.data(), cnt), "kmeans reseed");
+        }
     }
     check(mflat_cu_kmeans_get_centroids(k, cents.data()), "kmeans centroids");
 
     mImpl->cellStart.assign(static_cast<size_t>(nlist) + 1, 0);
-    mImpl->reorderedIds.assign(n, 0);
+    mImpl->reorderedIds.assign(static_cast<size_t>(total), 0);
     check(mflat_cu_kmeans_finish(k, nullptr, mImpl->cellStart.data(), mImpl->reorderedIds.data()),
           "kmeans final assignment");
     mImpl->centroids = std::move(cents);
     mImpl->nlist = nlist;
-    mImpl->dbCount = n;
+    mImpl->dbCount = nt;
 
     mImpl->coarse = std::make_unique<FlatIndex>(dim, Metric::L2, Storage::FP32, mImpl->device);
     mImpl->coarse->add(mImpl->centroids.data(), nlist);

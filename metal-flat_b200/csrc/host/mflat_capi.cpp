@@ -315,8 +315,8 @@ MFLAT_API void mflat_coarse_free(mflat_coarse_t* h) { delete h; }
 
 MFLAT_API mflat_status_t mflat_coarse_train(mflat_coarse_t* h, const float* data, int n, int nlist,
                                             int iters) {
-    if (!h || !data) return MFLAT_ERR_NULL_ARG;
-    if (n <= 0 || nlist <= 0 || iters < 0) return MFLAT_ERR_BAD_ARG;
+    if (!h || (!data && n > 0)) return MFLAT_ERR_NULL_ARG;
+    if (n < 0 || nlist <= 0 || iters < 0) return MFLAT_ERR_BAD_ARG;
     return guarded([&] {
         std::lock_guard<std::mutex> lk(h->mu);
         h->cq.train(data, n, nlist, iters);
@@ -359,6 +359,19 @@ MFLAT_API mflat_status_t mflat_coarse_probe(mflat_coarse_t* h, const float* quer
         std::vector<int32_t> probed;
         h->cq.probeCells(queries, m, nprobe, probed);
         std::memcpy(out_cells, probed.data(), probed.size() * sizeof(int32_t));
+        return MFLAT_OK;
+    });
+}
+
+MFLAT_API mflat_status_t mflat_coarse_set_shard(mflat_coarse_t* h, int rank, int world,
+                                                const uint8_t comm_id[MFLAT_COMM_ID_BYTES],
+                                                const int64_t* row_offsets) {
+    if (!h) return MFLAT_ERR_NULL_ARG;
+    if (world < 1 || rank < 0 || rank >= world) return MFLAT_ERR_BAD_ARG;
+    if (world > 1 && (!comm_id || !row_offsets)) return MFLAT_ERR_NULL_ARG;
+    return guarded([&] {
+        std::lock_guard<std::mutex> lk(h->mu);
+        h->cq.setShard(rank, world, comm_id, row_offsets);
         return MFLAT_OK;
     });
 }

@@ -45,7 +45,7 @@ public:
 
     int dim() const;
     int nlist() const;
-    int size() const;                                   // n
+    int size() const;                                   // n (all ranks' rows when sharded)
     const std::vector<float>& centroids() const;        // nlist x dim
     const std::vector<int>& cellStart() const;          // nlist + 1 (CSR offsets)
     const std::vector<int>& reorderedIds() const;       // n: slot -> original id
@@ -56,6 +56,15 @@ public:
     // probed (resized to m * nprobe) = nearest-first cell ids of each query,
     // from the coarse FlatIndex (exact L2 over the centroids, lowest id on ties).
     void probeCells(const float* queries, int m, int nprobe, std::vector<int32_t>& probed) const;
+
+    // Sharded training (additive; the reference trains on one device): this
+    // process holds global rows [row_offsets[rank], row_offsets[rank + 1]) and
+    // passes only those to train(); every rank calls train() with the same
+    // nlist and iters.  Per iteration the ranks all-gather per-cell double sums
+    // and counts over NCCL (comm_id: 128 bytes from mflat_comm_unique_id) and
+    // add them in rank order, so all ranks end with the same centroids and the
+    // same global CSR.  world = 1 turns sharding off.
+    void setShard(int rank, int world, const uint8_t* comm_id, const int64_t* row_offsets);
 
     bool gpuReady() const;                 // coarse FlatIndex ready
     const int32_t* cellBuffer() const;     // device: cellStart (nlist + 1)

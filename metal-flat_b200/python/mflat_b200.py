@@ -34,7 +34,7 @@ EXPORTS = [
     "mflat_flat_save", "mflat_flat_load",
     "mflat_coarse_create", "mflat_coarse_free", "mflat_coarse_train", "mflat_coarse_nlist",
     "mflat_coarse_size", "mflat_coarse_dim", "mflat_coarse_centroids", "mflat_coarse_csr",
-    "mflat_coarse_probe",
+    "mflat_coarse_probe", "mflat_coarse_set_shard",
 ]
 
 
@@ -104,6 +104,7 @@ def lib() -> ctypes.CDLL:
         "mflat_coarse_centroids": ([vp, f32p], ci),
         "mflat_coarse_csr": ([vp, i32p, i32p], ci),
         "mflat_coarse_probe": ([vp, f32p, ci, ci, i32p], ci),
+        "mflat_coarse_set_shard": ([vp, ci, ci, ctypes.c_char_p, ctypes.POINTER(ctypes.c_int64)], ci),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)
@@ -297,9 +298,16 @@ class CoarseQuantizer:
     def dim(self) -> int:
         return self._lib.mflat_coarse_dim(self._h)
 
+    def set_shard(self, rank: int, world: int, comm_id: bytes | None, row_offsets) -> None:
+        """This handle holds global rows [row_offsets[rank], row_offsets[rank + 1])."""
+        off = np.ascontiguousarray(row_offsets, dtype=np.int64)
+        _check(self._lib.mflat_coarse_set_shard(self._h, int(rank), int(world), comm_id,
+                                                _ptr(off, ctypes.c_int64)), "coarse set_shard")
+
     def train(self, data, nlist: int, iters: int = 12) -> None:
         d = _f32(data)
-        _check(self._lib.mflat_coarse_train(self._h, _ptr(d, ctypes.c_float), d.shape[0], int(nlist),
+        n = d.shape[0] if d.ndim == 2 else 0
+        _check(self._lib.mflat_coarse_train(self._h, _ptr(d, ctypes.c_float), n, int(nlist),
                                             int(iters)), "coarse train")
 
     def centroids(self) -> np.ndarray:

@@ -71,6 +71,12 @@ void mfo_kmeans_assign_f32(const float* points, int64_t n, const float* cents,
 int mfo_kmeans_train(const float* data, int64_t n, int dim, int nlist_req, int iters,
                      int max_points_per_centroid, float* out_cents, int32_t* out_assign,
                      int32_t* out_cell_start, int32_t* out_reordered);
+/* The same over `world` row shards (rank r holds global rows
+ * [offsets[r], offsets[r+1])): per-cell sums per rank, then ranks added in order. */
+int mfo_kmeans_train_sharded(const float* data, int64_t n, int dim, int nlist_req, int iters,
+                             int max_points_per_centroid, int world, const int64_t* offsets,
+                             float* out_cents, int32_t* out_assign, int32_t* out_cell_start,
+                             int32_t* out_reordered);
 /* The training's seed permutation of 0..n-1 (mt19937(seed), Fisher-Yates). */
 void mfo_kmeans_seed_permutation(int64_t n, uint32_t seed, int32_t* perm);
 

@@ -16,7 +16,8 @@
 //   * means: per cell, double sum over its points in ascending point order
 //     (the single-thread order; the reference's thread-chunked sum can differ
 //     in the last double bits with the host's thread count), then
-//     float(sum / count);
+//     float(sum / count); sharded training (an addition of this build) sums
+//     per rank over the rank's rows, then adds the ranks' sums in rank order;
 //   * empty cells, in cell order: centroid = training row rng() % trainN;
 //   * CSR: cellStart = prefix sums of the final all-points histogram,
 //     reorderedIds = ids grouped by cell, ascending (CoarseQuantizer.mm:134-143).
@@ -52,10 +53,11 @@ extern "C" void mfo_kmeans_seed_permutation(int64_t n, uint32_t seed, int32_t* p
     }
 }
 
-extern "C" int mfo_kmeans_train(const float* data, int64_t n, int dim, int nlist_req, int iters,
-                                int max_points_per_centroid, float* out_cents, int32_t* out_assign,
-                                int32_t* out_cell_start, int32_t* out_reordered) {
-    if (n < 1 || dim < 1 || nlist_req < 1) return -1;
+extern "C" int mfo_kmeans_train_sharded(const float* data, int64_t n, int dim, int nlist_req, int iters,
+                                        int max_points_per_centroid, int world, const int64_t* offsets,
+                                        float* out_cents, int32_t* out_assign,
+                                        int32_t* out_cell_start, int32_t* out_reordered) {
+    if (n < 1 || dim < 1 || nlist_req < 1 || world < 1) return -1;
     const int nlist = static_cast<int>(std::min<int64_t>(nlist_req, n));
     const size_t row = static_cast<size_t>(dim);
     std::mt19937 rng(12345);
@@ -80,8 +82,16 @@ extern "C" int mfo_kmeans_train(const float* data, int64_t n, int dim, int nlist
         train = train_vec.data();
     }
 
+    // owning rank of every training row (sharded sums: per rank, then ranks in order)
+    std::vector<int> owner(train_n, 0);
+    for (int64_t i = 0; i < train_n; ++i) {
+        const int64_t g = train_n < n ? perm[i] : i;
+        int r = 0;
+        while (world > 1 && g >= offsets[r + 1]) ++r;
+        owner[i] = r;
+    }
     std::vector<int32_t> assign(train_n);
-    std::vector<double> sums(static_cast<size_t>(nlist) * row);
+    std::vector<double> sums(static_cast<size_t>(world) * nlist * row);
     std::vector<int64_t> counts(nlist);
     for (int it = 0; it < iters; ++it) {
         mfo_kmeans_assign_f32(train, train_n, cents.data(), nlist, dim, assign.data());
@@ -89,16 +99,18 @@ extern "C" int mfo_kmeans_train(const float* data, int64_t n, int dim, int nlist
         std::fill(counts.begin(), counts.end(), 0);
         for (int64_t i = 0; i < train_n; ++i) {
             const int c = assign[i];
-            double* s = &sums[c * row];
+            double* s = &sums[(static_cast<size_t>(owner[i]) * nlist + c) * row];
             const float* v = train + i * row;
             for (int d = 0; d < dim; ++d) s[d] += v[d];
             ++counts[c];
         }
         for (int c = 0; c < nlist; ++c)
             if (counts[c] > 0)
-                for (int d = 0; d < dim; ++d)
-                    cents[c * row + d] =
-                        static_cast<float>(sums[c * row + d] / static_cast<double>(counts[c]));
+                for (int d = 0; d < dim; ++d) {
+                    double acc = sums[c * row + d];
+                    for (int r = 1; r < world; ++r) acc += sums[(static_cast<size_t>(r) * nlist + c) * row + d];
+                    cents[c * row + d] = static_cast<float>(acc / static_cast<double>(counts[c]));
+                }
         for (int c = 0; c < nlist; ++c) {
             if (counts[c] == 0) {
                 const int64_t r = static_cast<int64_t>(rng() % static_cast<unsigned>(train_n));
@@ -120,4 +132,12 @@ extern "C" int mfo_kmeans_train(const float* data, int64_t n, int dim, int nlist
         for (int64_t i = 0; i < n; ++i) out_reordered[cursor[final_assign[i]]++] = static_cast<int32_t>(i);
     }
     return nlist;
+}
+
+extern "C" int mfo_kmeans_train(const float* data, int64_t n, int dim, int nlist_req, int iters,
+                                int max_points_per_centroid, float* out_cents, int32_t* out_assign,
+                                int32_t* out_cell_start, int32_t* out_reordered) {
+    const int64_t offsets[2] = {0, n};
+    return mfo_kmeans_train_sharded(data, n, dim, nlist_req, iters, max_points_per_centroid, 1, offsets,
+                                    out_cents, out_assign, out_cell_start, out_reordered);
 }

@@ -50,6 +50,10 @@ def lib() -> ctypes.CDLL:
         _lib.mfo_kmeans_train.argtypes = [f32p, i64, ci, ci, ci, ci, f32p, i32p, i32p, i32p]
         _lib.mfo_kmeans_train.restype = ci
         _lib.mfo_kmeans_seed_permutation.argtypes = [i64, ctypes.c_uint32, i32p]
+        _lib.mfo_kmeans_train_sharded.argtypes = [f32p, i64, ci, ci, ci, ci, ci,
+                                                  np.ctypeslib.ndpointer(np.int64, flags="C_CONTIGUOUS"),
+                                                  f32p, i32p, i32p, i32p]
+        _lib.mfo_kmeans_train_sharded.restype = ci
     return _lib
 
 
@@ -121,6 +125,22 @@ def kmeans_train(data, nlist: int, iters: int = 12, max_points_per_centroid: int
     reord = np.empty(n, np.int32)
     got = lib().mfo_kmeans_train(data, n, dim, nlist, iters, max_points_per_centroid, cents, assign,
                                  start, reord)
+    assert got == nl
+    return cents, assign, start, reord
+
+
+def kmeans_train_sharded(data, nlist: int, iters: int, offsets, max_points_per_centroid: int = 256):
+    """kmeans_train over row shards [offsets[r], offsets[r+1]) (per-rank sums added in rank order)."""
+    data = _c(data)
+    n, dim = data.shape
+    off = np.ascontiguousarray(offsets, dtype=np.int64)
+    nl = min(nlist, n)
+    cents = np.empty((nl, dim), np.float32)
+    assign = np.empty(n, np.int32)
+    start = np.empty(nl + 1, np.int32)
+    reord = np.empty(n, np.int32)
+    got = lib().mfo_kmeans_train_sharded(data, n, dim, nlist, iters, max_points_per_centroid,
+                                         len(off) - 1, off, cents, assign, start, reord)
     assert got == nl
     return cents, assign, start, reord
 

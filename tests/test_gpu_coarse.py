@@ -66,3 +66,40 @@ def test_probe_clustered_cells():
     ref_i, ref_d = O.flat_search_f64(cents, q, 5, O.L2)
     dist = ((q[:, None, :].astype(np.float64) - cents[got].astype(np.float64)) ** 2).sum(-1)
     assert O.exact_ids_match(got, dist.astype(np.float32), ref_i, ref_d, rel=1e-6) == 0
+
+
+def _gpus():
+    try:
+        import torch
+        return torch.cuda.device_count()
+    except Exception:                                  # noqa: BLE001
+        return 0
+
+
+@pytest.mark.skipif(_gpus() < 2, reason="needs at least two GPUs")
+def test_sharded_training_matches_oracle():
+    import os
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    world = min(_gpus(), 8)
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", MFLAT_NCCL_TIMEOUT_S="120")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={world}",
+           "--master-addr", "127.0.0.1", "--master-port", "29541",
+           os.path.join(root, "tests", "coarse_shard_worker.py")]
+    r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=600)
+    print(r.stdout[-3000:], r.stderr[-3000:])
+    assert r.returncode == 0
+
+
+def test_single_rank_shard_setting_is_plain_training():
+    """set_shard(0, 1, ...) is the unsharded path."""
+    rng = np.random.default_rng(12)
+    data = rng.standard_normal((4000, 20)).astype(np.float32)
+    cq = M.CoarseQuantizer(20)
+    cq.set_shard(0, 1, None, np.array([0, 4000], np.int64))
+    cq.train(data, 16, 3)
+    c_ref, _, s_ref, r_ref = O.kmeans_train(data, 16, 3, 256)
+    assert np.array_equal(cq.centroids().view(np.uint32), c_ref.view(np.uint32))
+    s, r = cq.csr()
+    assert np.array_equal(s, s_ref) and np.array_equal(r, r_ref)
