@@ -530,7 +530,14 @@ int run_screen(mflat_cu_index* ix, const float* queries, int m, int kp, int on_d
 namespace {
 
 constexpr int64_t kAllRowsBuffered = 32768;        // below this, no pre-pass
-constexpr size_t kBufferBudget = size_t(6) << 30;  // bytes of candidate buffers
+
+// Bytes the candidate buffers of one query batch may take: a quarter of the
+// device's free memory, at most 16 GB.
+size_t buffer_budget() {
+    size_t free_b = 0, total_b = 0;
+    if (cudaMemGetInfo(&free_b, &total_b) != cudaSuccess) return size_t(4) << 30;
+    return std::max<size_t>(size_t(1) << 30, std::min<size_t>(size_t(16) << 30, free_b / 4));
+}
 
 struct LargePlan {
     bool prepass = false;          // floor estimate before the main pass
@@ -539,6 +546,7 @@ struct LargePlan {
     int stride_a = 1, sample_a = 0;
     int stride_b = 1, sample_b = 0;
     int chunks_a = 0, tpc_a = 0;   // stage-A chunking (>= lists, spread over the SMs)
+    int r_stat = 0;                // rank of the statistical floor in the stage-B sample (0: none)
     uint32_t cap = 0;
     int batch = 0;
 };
@@ -571,6 +579,14 @@ LargePlan plan_large(int64_t n, int k, int m, int kp1, int want, int lists_per_c
                 P.stride_a = 256;
                 P.sample_a = (n_tiles + 255) / 256;
             }
+            if (P.two_stage) {
+                // about want / stride_b of the sampled rows are in the global
+                // top-want; six standard deviations above that (see
+                // buffer_floor_kernel) the floor admits ~r_stat * stride_b rows
+                const double mean = static_cast<double>(want) / P.stride_b;
+                const int r = static_cast<int>(std::ceil(mean + 6.0 * std::sqrt(mean))) + 1;
+                P.r_stat = r < want ? r : 0;
+            }
             // the floor is about the (want * stride_b)-th best row overall; the
             // stage-B buffer holds about want * stride_a / stride_b rows
             const int64_t expect = static_cast<int64_t>(want) * P.stride_b;
@@ -580,7 +596,7 @@ LargePlan plan_large(int64_t n, int k, int m, int kp1, int want, int lists_per_c
         }
     }
     const size_t per_q = static_cast<size_t>(P.cap) * 8 + 64;
-    P.batch = static_cast<int>(std::max<size_t>(kBM, std::min<size_t>(m, kBufferBudget / per_q)));
+    P.batch = static_cast<int>(std::max<size_t>(kBM, std::min<size_t>(m, buffer_budget() / per_q)));
     P.batch = std::min(P.batch, m);
     if (P.prepass) {
         // Stage A needs >= `lists` chunks for its union; more chunks only enlarge
@@ -599,12 +615,13 @@ LargePlan plan_large(int64_t n, int k, int m, int kp1, int want, int lists_per_c
 
 // Floor estimate for one query batch (see plan_large): stage A list-mode
 // pass + union select, then (two-stage plans) stage B buffer-mode pass + the
-// want-th best of each buffer.  list_pass / buffer_pass launch the storage's
+// want-th best of each buffer (valid floor, in base.thr) and its r_stat-th
+// best (statistical floor, in thr_stat).  list_pass / buffer_pass launch the storage's
 // screen kernel; `base` carries the batch's queries and buffers.
 template <class ListPass, class BufferPass>
 int estimate_floor(mflat_cu_index* ix, const LargePlan& P, const ScreenParams& base, int want,
                    int kp1, int lists_per_chunk, ListPass list_pass, BufferPass buffer_pass,
-                   cudaStream_t st) {
+                   uint32_t* thr_stat, cudaStream_t st) {
     ScreenParams pa = base;
     pa.use_floor = 0;
     pa.tile_stride = P.stride_a;
@@ -626,7 +643,8 @@ int estimate_floor(mflat_cu_index* ix, const LargePlan& P, const ScreenParams& b
     pb.tiles_per_chunk = tpc;
     CU_TRY(cudaMemsetAsync(base.buf_cnt, 0, static_cast<size_t>(base.m_pad) * sizeof(uint32_t), st), "counts");
     CU_TRY(buffer_pass(pb), "floor buffer pass launch");
-    CU_TRY(launch_buffer_floor(base.buf_cnt, base.buf_s, base.cap, want, base.m, base.thr, st),
+    CU_TRY(launch_buffer_floor(base.buf_cnt, base.buf_s, base.cap, want, P.r_stat, base.m, base.thr,
+                               thr_stat, st),
            "floor select launch");
     return ST_OK;
 }
@@ -669,7 +687,8 @@ int search_large(mflat_cu_index* ix, const float* queries, int m, int k_out, int
     CU_TRY(ix->buf_s.ensure(static_cast<size_t>(bm_pad) * P.cap * sizeof(float)), "candidate buffer");
     CU_TRY(ix->buf_i.ensure(static_cast<size_t>(bm_pad) * P.cap * sizeof(int32_t)), "candidate buffer");
     CU_TRY(ix->flag_list.ensure(static_cast<size_t>(bm_pad) * sizeof(int)), "flag list");
-    CU_TRY(ix->lk_words.ensure(2 * sizeof(int)), "status words");
+    CU_TRY(ix->lk_words.ensure(4 * sizeof(int)), "status words");
+    CU_TRY(ix->thr_stat.ensure(static_cast<size_t>(bm_pad) * sizeof(uint32_t)), "floors");
     if (P.prepass) {
         const size_t parts = static_cast<size_t>(P.chunks_a) * bm_pad * kKP1;
         CU_TRY(ix->part_s.ensure(parts * sizeof(float)), "pre-pass lists");
@@ -678,8 +697,10 @@ int search_large(mflat_cu_index* ix, const float* queries, int m, int k_out, int
         CU_TRY(ix->part_s.ensure(sizeof(float)), "pre-pass lists");
         CU_TRY(ix->part_i.ensure(sizeof(int32_t)), "pre-pass lists");
     }
-    int* words = ix->lk_words.as<int>();      // [0] overflow, [1] proof failures
-    CU_TRY(cudaMemsetAsync(words, 0, 2 * sizeof(int), st), "status words");
+    // per batch: [0] overflows, [1] unproven queries, [2] statistical-floor misses
+    int* words = ix->lk_words.as<int>();
+    const bool use_stat = P.prepass && P.two_stage && P.r_stat > 0;
+    int overflows = 0, unproven = 0, redone = 0;
     if (ix->timing) cudaEventRecord(ix->ev[0], st);
 
     for (int b0 = 0; b0 < m; b0 += P.batch) {
@@ -692,6 +713,7 @@ int search_large(mflat_cu_index* ix, const float* queries, int m, int k_out, int
         CU_TRY(cudaMemsetAsync(ix->thr.p, 0, static_cast<size_t>(mb_pad) * sizeof(uint32_t), st), "floors");
         CU_TRY(cudaMemsetAsync(ix->buf_cnt.p, 0, static_cast<size_t>(mb_pad) * sizeof(uint32_t), st), "counts");
         CU_TRY(cudaMemsetAsync(ix->flag_count, 0, sizeof(int), st), "flag count");
+        CU_TRY(cudaMemsetAsync(words, 0, 4 * sizeof(int), st), "status words");
 
         ScreenParams sp{};
         sp.m = mb;
@@ -717,10 +739,9 @@ int search_large(mflat_cu_index* ix, const float* queries, int m, int k_out, int
             const int rc = estimate_floor(
                 ix, P, sp, 2 * k_out, kKP1, 1,
                 [&](const ScreenParams& q, int kp) { return launch_pass(ix, q, kp, st); },
-                [&](const ScreenParams& q) { return launch_pass(ix, q, 0, st); }, st);
+                [&](const ScreenParams& q) { return launch_pass(ix, q, 0, st); },
+                ix->thr_stat.as<uint32_t>(), st);
             if (rc != ST_OK) return rc;
-            CU_TRY(cudaMemsetAsync(ix->buf_cnt.p, 0, static_cast<size_t>(mb_pad) * sizeof(uint32_t), st),
-                   "counts");
         }
         sp.use_floor = 1;
         sp.tile_stride = 1;
@@ -729,13 +750,6 @@ int search_large(mflat_cu_index* ix, const float* queries, int m, int k_out, int
         plan_chunks(sp.n_qtiles, n_tiles, ix->num_sms, kMaxChunks, n_chunks, tpc);
         sp.n_chunks = n_chunks;
         sp.tiles_per_chunk = tpc;
-        sp.buf_cnt = ix->buf_cnt.as<uint32_t>();
-        sp.buf_s = ix->buf_s.as<float>();
-        sp.buf_i = ix->buf_i.as<int32_t>();
-        sp.cap = P.cap;
-        if (ix->timing && b0 == 0) cudaEventRecord(ix->ev[1], st);
-        CU_TRY(launch_pass(ix, sp, 0, st), "buffer screen launch");
-        if (ix->timing && b0 == 0) cudaEventRecord(ix->ev[2], st);
 
         LargeSelectParams ls{};
         ls.m = mb;
@@ -748,7 +762,6 @@ int search_large(mflat_cu_index* ix, const float* queries, int m, int k_out, int
         ls.buf_s = sp.buf_s;
         ls.buf_i = sp.buf_i;
         ls.cap = P.cap;
-        ls.thr = sp.thr;
         ls.exact = 1;
         ls.q_hi = sp.q_hi;
         ls.q_lo = sp.q_lo;
@@ -763,15 +776,43 @@ int search_large(mflat_cu_index* ix, const float* queries, int m, int k_out, int
         ls.flag_count = words + 1;
         ls.flag_list = ix->flag_list.as<int>();
         ls.overflow = words;
-        CU_TRY(launch_select_large(ls, st), "large select launch");
+
+        // The statistical floor first; when it failed for any query of the
+        // batch (too few rows reached it, an overflow or an unproven window),
+        // the batch is redone with the valid floor.
+        for (int attempt = 0; attempt < 2; ++attempt) {
+            const bool stat = use_stat && attempt == 0;
+            sp.thr = stat ? ix->thr_stat.as<uint32_t>() : ix->thr.as<uint32_t>();
+            ls.thr = sp.thr;
+            CU_TRY(cudaMemsetAsync(ix->buf_cnt.p, 0, static_cast<size_t>(mb_pad) * sizeof(uint32_t), st),
+                   "counts");
+            if (ix->timing && b0 == 0 && attempt == 0) cudaEventRecord(ix->ev[1], st);
+            CU_TRY(launch_pass(ix, sp, 0, st), "buffer screen launch");
+            if (ix->timing && b0 == 0 && attempt == 0) cudaEventRecord(ix->ev[2], st);
+            if (stat)
+                CU_TRY(launch_floor_check(sp.buf_cnt, ix->thr_stat.as<uint32_t>(), ix->thr.as<uint32_t>(),
+                                          2 * k_out, mb, words + 2, st),
+                       "floor check launch");
+            CU_TRY(launch_select_large(ls, st), "large select launch");
+            CU_TRY(cudaMemcpyAsync(&ix->host_words[4], words, 3 * sizeof(int), cudaMemcpyDeviceToHost, st),
+                   "status");
+            CU_TRY(cudaStreamSynchronize(st), "large-k search");
+            if (!stat || (ix->host_words[4] == 0 && ix->host_words[5] == 0 && ix->host_words[6] == 0))
+                break;
+            ++redone;
+            CU_TRY(cudaMemsetAsync(words, 0, 4 * sizeof(int), st), "status words");
+        }
+        overflows += ix->host_words[4];
+        unproven += ix->host_words[5];
     }
-    if (ix->timing) cudaEventRecord(ix->ev[3], st);
+    if (ix->timing) {
+        cudaEventRecord(ix->ev[3], st);
+        cudaEventSynchronize(ix->ev[3]);
+    }
     // Overflows and unproven queries are rare; surface them as errors.
-    CU_TRY(cudaMemcpyAsync(&ix->host_words[2], words, 2 * sizeof(int), cudaMemcpyDeviceToHost, st), "status");
-    CU_TRY(cudaStreamSynchronize(st), "large-k search");
-    if (ix->host_words[2] > 0) return fail(ST_INTERNAL, "candidate buffer overflow (too many rows tie with the k-th best)");
-    if (ix->host_words[3] > 0) return fail(ST_INTERNAL, "exactness could not be proven for some queries (near-ties)");
-    ix->last.screen_launches = 1;
+    if (overflows > 0) return fail(ST_INTERNAL, "candidate buffer overflow (too many rows tie with the k-th best)");
+    if (unproven > 0) return fail(ST_INTERNAL, "exactness could not be proven for some queries (near-ties)");
+    ix->last.screen_launches = 1 + redone;
     ix->last.launches = (P.prepass ? (P.two_stage ? 7 : 5) : 3) * ((m + P.batch - 1) / P.batch);
     return ST_OK;
 }
@@ -816,9 +857,13 @@ int search_half(mflat_cu_index* ix, const float* queries, int m, int k_out, int3
         CU_TRY(ix->buf_cnt.ensure(static_cast<size_t>(bm_pad) * sizeof(uint32_t)), "buffer counts");
         CU_TRY(ix->buf_s.ensure(static_cast<size_t>(bm_pad) * P.cap * sizeof(float)), "candidate buffer");
         CU_TRY(ix->buf_i.ensure(static_cast<size_t>(bm_pad) * P.cap * sizeof(int32_t)), "candidate buffer");
-        CU_TRY(ix->lk_words.ensure(2 * sizeof(int)), "status words");
-        CU_TRY(cudaMemsetAsync(ix->lk_words.p, 0, 2 * sizeof(int), st), "status words");
+        CU_TRY(ix->lk_words.ensure(4 * sizeof(int)), "status words");
+        CU_TRY(ix->thr_stat.ensure(static_cast<size_t>(bm_pad) * sizeof(uint32_t)), "floors");
     }
+    // per batch: [0] overflows, [2] statistical-floor misses
+    int* words = list_mode ? nullptr : ix->lk_words.as<int>();
+    const bool use_stat = !list_mode && P.prepass && P.two_stage && P.r_stat > 0;
+    int overflows = 0, redone = 0;
     const int max_lists = list_mode ? kMaxChunks / 2 : P.chunks_a;
     const int lk = list_mode ? kp : kKP1;
     const size_t parts = static_cast<size_t>(2 * std::max(max_lists, 1)) * bm_pad * lk;
@@ -884,13 +929,15 @@ int search_half(mflat_cu_index* ix, const float* queries, int m, int k_out, int3
         sp.buf_s = ix->buf_s.as<float>();
         sp.buf_i = ix->buf_i.as<int32_t>();
         sp.cap = P.cap;
+        CU_TRY(cudaMemsetAsync(words, 0, 4 * sizeof(int), st), "status words");
         if (P.prepass) {
+            CU_TRY(cudaMemsetAsync(ix->buf_cnt.p, 0, static_cast<size_t>(mb_pad) * sizeof(uint32_t), st),
+                   "counts");
             const int rc = estimate_floor(
                 ix, P, sp, k_out, kKP1, 2, [&](const ScreenParams& q, int kpp) { return launch(q, kpp); },
-                [&](const ScreenParams& q) { return launch(q, 0); }, st);
+                [&](const ScreenParams& q) { return launch(q, 0); }, ix->thr_stat.as<uint32_t>(), st);
             if (rc != ST_OK) return rc;
         }
-        CU_TRY(cudaMemsetAsync(ix->buf_cnt.p, 0, static_cast<size_t>(mb_pad) * sizeof(uint32_t), st), "counts");
         sp.use_floor = 1;
         sp.tile_stride = 1;
         sp.n_tiles = n_tiles;
@@ -898,13 +945,6 @@ int search_half(mflat_cu_index* ix, const float* queries, int m, int k_out, int3
         plan_chunks(sp.n_qtiles, n_tiles, ix->num_sms, kMaxChunks, n_chunks, tpc);
         sp.n_chunks = n_chunks;
         sp.tiles_per_chunk = tpc;
-        sp.buf_cnt = ix->buf_cnt.as<uint32_t>();
-        sp.buf_s = ix->buf_s.as<float>();
-        sp.buf_i = ix->buf_i.as<int32_t>();
-        sp.cap = P.cap;
-        if (ix->timing && b0 == 0) cudaEventRecord(ix->ev[1], st);
-        CU_TRY(launch(sp, 0), "buffer screen launch");
-        if (ix->timing && b0 == 0) cudaEventRecord(ix->ev[2], st);
         LargeSelectParams ls{};
         ls.m = mb;
         ls.m_pad = mb_pad;
@@ -914,27 +954,46 @@ int search_half(mflat_cu_index* ix, const float* queries, int m, int k_out, int3
         ls.buf_s = sp.buf_s;
         ls.buf_i = sp.buf_i;
         ls.cap = P.cap;
-        ls.thr = sp.thr;
         ls.exact = 0;
         ls.qsq = ix->qsq.as<float>();
         ls.id_base = ix->world > 1 ? ix->id_base : 0;
         ls.out_ids = d_ids + static_cast<int64_t>(b0) * k_out;
         ls.out_dist = d_dist + static_cast<int64_t>(b0) * k_out;
-        ls.flag_count = ix->lk_words.as<int>() + 1;
+        ls.flag_count = words + 1;
         ls.flag_list = nullptr;
-        ls.overflow = ix->lk_words.as<int>();
-        CU_TRY(launch_select_large(ls, st), "large select launch");
+        ls.overflow = words;
+        // statistical floor first, the valid floor when it failed (see search_large)
+        for (int attempt = 0; attempt < 2; ++attempt) {
+            const bool stat = use_stat && attempt == 0;
+            sp.thr = stat ? ix->thr_stat.as<uint32_t>() : ix->thr.as<uint32_t>();
+            ls.thr = sp.thr;
+            CU_TRY(cudaMemsetAsync(ix->buf_cnt.p, 0, static_cast<size_t>(mb_pad) * sizeof(uint32_t), st),
+                   "counts");
+            if (ix->timing && b0 == 0 && attempt == 0) cudaEventRecord(ix->ev[1], st);
+            CU_TRY(launch(sp, 0), "buffer screen launch");
+            if (ix->timing && b0 == 0 && attempt == 0) cudaEventRecord(ix->ev[2], st);
+            if (stat)
+                CU_TRY(launch_floor_check(sp.buf_cnt, ix->thr_stat.as<uint32_t>(), ix->thr.as<uint32_t>(),
+                                          k_out, mb, words + 2, st),
+                       "floor check launch");
+            CU_TRY(launch_select_large(ls, st), "large select launch");
+            CU_TRY(cudaMemcpyAsync(&ix->host_words[4], words, 3 * sizeof(int), cudaMemcpyDeviceToHost, st),
+                   "status");
+            CU_TRY(cudaStreamSynchronize(st), "large-k search");
+            if (!stat || (ix->host_words[4] == 0 && ix->host_words[6] == 0)) break;
+            ++redone;
+            CU_TRY(cudaMemsetAsync(words, 0, 4 * sizeof(int), st), "status words");
+        }
+        overflows += ix->host_words[4];
     }
-    if (ix->timing) cudaEventRecord(ix->ev[3], st);
-    ix->last.screen_launches = 1;
+    if (ix->timing) {
+        cudaEventRecord(ix->ev[3], st);
+        cudaEventSynchronize(ix->ev[3]);
+    }
+    ix->last.screen_launches = 1 + redone;
     ix->last.launches = list_mode ? 3 : (P.prepass ? (P.two_stage ? 7 : 5) : 3);
-    if (!list_mode) {
-        CU_TRY(cudaMemcpyAsync(&ix->host_words[2], ix->lk_words.p, 2 * sizeof(int), cudaMemcpyDeviceToHost, st),
-               "status");
-        CU_TRY(cudaStreamSynchronize(st), "large-k search");
-        if (ix->host_words[2] > 0)
-            return fail(ST_INTERNAL, "candidate buffer overflow (too many rows tie with the k-th best)");
-    }
+    if (overflows > 0)
+        return fail(ST_INTERNAL, "candidate buffer overflow (too many rows tie with the k-th best)");
     return ST_OK;
 }
 
@@ -1039,14 +1098,14 @@ int mflat_cu_index_create(int device, int dim, int metric, int storage, mflat_cu
         (e = cudaMalloc(&ix->xmax_bits, sizeof(unsigned))) != cudaSuccess ||
         (e = cudaMalloc(&ix->err, sizeof(int))) != cudaSuccess ||
         (e = cudaMalloc(&ix->flag_count, sizeof(int))) != cudaSuccess ||
-        (e = cudaHostAlloc(&ix->host_words, 4 * sizeof(int), cudaHostAllocDefault)) != cudaSuccess) {
+        (e = cudaHostAlloc(&ix->host_words, 8 * sizeof(int), cudaHostAllocDefault)) != cudaSuccess) {
         mflat_cu_index_destroy(ix);
         return fail(e == cudaErrorMemoryAllocation ? ST_ALLOC : ST_DEVICE, "index setup", e);
     }
     for (auto& ev : ix->ev) cudaEventCreate(&ev);
     cudaMemsetAsync(ix->xmax_bits, 0, sizeof(unsigned), ix->stream);
     cudaMemsetAsync(ix->err, 0, sizeof(int), ix->stream);
-    std::memset(ix->host_words, 0, 4 * sizeof(int));
+    std::memset(ix->host_words, 0, 8 * sizeof(int));
     if ((e = cudaStreamSynchronize(ix->stream)) != cudaSuccess) {
         mflat_cu_index_destroy(ix);
         return fail(ST_DEVICE, "index setup", e);
@@ -1071,7 +1130,7 @@ void mflat_cu_index_destroy(mflat_cu_index_t* ix) {
     if (ix->host_words) cudaFreeHost(ix->host_words);
     for (DevBuf* b : {&ix->stage_in, &ix->q_in, &ix->q_hi, &ix->q_lo, &ix->qnorm, &ix->part_s,
                       &ix->part_i, &ix->flag_list, &ix->out_ids, &ix->out_dist, &ix->gather_ids,
-                      &ix->gather_dist, &ix->merge_tmp_ids, &ix->merge_tmp_dist, &ix->thr, &ix->fb_s,
+                      &ix->gather_dist, &ix->merge_tmp_ids, &ix->merge_tmp_dist, &ix->thr, &ix->thr_stat, &ix->fb_s,
                       &ix->fb_i, &ix->buf_cnt, &ix->buf_s, &ix->buf_i, &ix->lk_words,
                       &ix->q16, &ix->qsq})
         b->release();

@@ -72,7 +72,7 @@ struct mflat_cu_index {
     int* flag_count = nullptr;    // queries routed to the exact full scan
     int* host_words = nullptr;    // pinned: [0] err, [1] flag_count
     mflat_cu::DevBuf stage_in, q_in, q_hi, q_lo, qnorm, part_s, part_i, flag_list, out_ids, out_dist;
-    mflat_cu::DevBuf thr, fb_s, fb_i;
+    mflat_cu::DevBuf thr, thr_stat, fb_s, fb_i;
     mflat_cu::DevBuf buf_cnt, buf_s, buf_i, lk_words;   // large-k candidate buffers
     mflat_cu::DevBuf q16, qsq;                          // 16-bit queries, ||q||^2
     bool timing = false;

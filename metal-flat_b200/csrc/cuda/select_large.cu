@@ -301,26 +301,64 @@ __global__ void __launch_bounds__(256) prepass_floor_kernel(const float* __restr
 // floor) is met by `want` rows, hence <= the global want-th best.  That holds
 // for any subset, so an overflowed buffer (the first `cap` appends) still
 // gives a valid floor.  Leaves thr unchanged when fewer than `want` were kept.
+//
+// thr_stat (when r_stat > 0) gets the r_stat-th best kept score, r_stat <
+// want: a statistical floor.  With the sample a 1/s slice of the rows, the
+// number of sampled rows among the global top-`want` is about want/s, and
+// r_stat sits several standard deviations above that, so the floor is almost
+// always below the global want-th best while admitting ~r_stat * s rows
+// instead of ~want * s.  It is only a guess: floor_check_kernel verifies it
+// after the full pass (at least `want` rows must reach it) and the caller
+// redoes the pass with the valid floor when it fails.
 __global__ void __launch_bounds__(512) buffer_floor_kernel(const uint32_t* __restrict__ cnt,
                                                            const float* __restrict__ buf_s, uint32_t cap,
-                                                           int want, int m, uint32_t* thr) {
+                                                           int want, int r_stat, int m, uint32_t* thr,
+                                                           uint32_t* thr_stat) {
     const int q = blockIdx.x;
     if (q >= m) return;
     __shared__ uint32_t hist[256];
     __shared__ uint32_t sh_prefix;
     __shared__ int sh_remaining;
     const uint32_t n = min(cnt[q], cap);
-    if (n < static_cast<uint32_t>(want)) return;
-    radix_select(buf_s + static_cast<int64_t>(q) * cap, static_cast<int>(n), want, hist, &sh_prefix,
-                 &sh_remaining);
-    if (threadIdx.x == 0 && sh_prefix > thr[q]) thr[q] = sh_prefix;
+    const float* s = buf_s + static_cast<int64_t>(q) * cap;
+    uint32_t valid = thr[q];
+    if (n >= static_cast<uint32_t>(want)) {
+        radix_select(s, static_cast<int>(n), want, hist, &sh_prefix, &sh_remaining);
+        valid = max(valid, sh_prefix);
+        __syncthreads();
+    }
+    uint32_t stat = valid;
+    if (r_stat > 0 && n >= static_cast<uint32_t>(r_stat)) {
+        radix_select(s, static_cast<int>(n), r_stat, hist, &sh_prefix, &sh_remaining);
+        stat = max(stat, sh_prefix);
+    }
+    if (threadIdx.x == 0) {
+        thr[q] = valid;
+        if (thr_stat) thr_stat[q] = stat;
+    }
+}
+
+// A query whose full pass used a statistical floor above its valid one must
+// have kept at least `want` rows; count the ones that did not.
+__global__ void floor_check_kernel(const uint32_t* __restrict__ cnt, const uint32_t* __restrict__ used,
+                                   const uint32_t* __restrict__ valid, int want, int m, int* failures) {
+    const int q = blockIdx.x * blockDim.x + threadIdx.x;
+    if (q >= m) return;
+    if (used[q] > valid[q] && cnt[q] < static_cast<uint32_t>(want)) atomicAdd(failures, 1);
 }
 
 }  // namespace
 
-cudaError_t launch_buffer_floor(const uint32_t* cnt, const float* buf_s, uint32_t cap, int want, int m,
-                                uint32_t* thr, cudaStream_t stream) {
-    buffer_floor_kernel<<<m, 512, 0, stream>>>(cnt, buf_s, cap, want, m, thr);
+cudaError_t launch_buffer_floor(const uint32_t* cnt, const float* buf_s, uint32_t cap, int want,
+                                int r_stat, int m, uint32_t* thr, uint32_t* thr_stat,
+                                cudaStream_t stream) {
+    buffer_floor_kernel<<<m, 512, 0, stream>>>(cnt, buf_s, cap, want, r_stat, m, thr, thr_stat);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_floor_check(const uint32_t* cnt, const uint32_t* used, const uint32_t* valid,
+                               int want, int m, int* failures, cudaStream_t stream) {
+    floor_check_kernel<<<(m + 255) / 256, 256, 0, stream>>>(cnt, used, valid, want, m, failures);
     return cudaGetLastError();
 }
 

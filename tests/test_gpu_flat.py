@@ -230,3 +230,21 @@ def test_large_k_clamp_and_uniform():
     ids, dist = search(db, q, 5000, "l2")
     assert ids.shape == (12, 1024)
     assert_exact(ids, dist, db, q, 1024, "l2")
+
+
+def test_large_k_statistical_floor_redo():
+    """The rows nearest to the query sit in tile 0, which every floor sample
+    contains: the statistical floor from the sample is then far above the
+    200th-best row, the check after the full pass catches it and the batch is
+    redone with the valid floor -- the result stays exact."""
+    rng = np.random.default_rng(zlib.crc32(b"stat-floor-redo"))
+    n, dim, k = 2_000_000, 16, 100
+    db = rng.standard_normal((n, dim)).astype(np.float32) + 4.0
+    centre = np.zeros(dim, np.float32)
+    db[:200] = centre + 0.01 * rng.standard_normal((200, dim)).astype(np.float32)
+    q = np.stack([centre + 0.001, rng.standard_normal(dim).astype(np.float32) + 4.0])
+    tm = []
+    ids, dist = search(db, q, k, "l2", timing=tm)
+    assert_exact(ids, dist, db, q, k, "l2")
+    assert tm[0].screen_launches == 2          # the redo ran
+    assert set(ids[0].tolist()) <= set(range(200))

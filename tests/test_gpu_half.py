@@ -89,3 +89,22 @@ def test_config5_like_bf16_large_k():
     ids, dist = run(db, q, 1024, "l2", "bf16")
     tru_i, _ = O.flat_search_f64(db, q, 1024, O.L2)
     assert recall(ids, tru_i) >= 0.99
+
+
+def test_statistical_floor_redo_16bit():
+    """As the fp32 case: the query's 100 nearest rows fill tile 0, the
+    statistical floor fails the check and the batch is redone."""
+    rng = np.random.default_rng(zlib.crc32(b"stat-floor-redo-16"))
+    n, dim, k = 1_000_000, 64, 100
+    db = rng.standard_normal((n, dim)).astype(np.float32) + 3.0
+    centre = np.zeros(dim, np.float32)
+    db[:100] = centre + 0.01 * rng.standard_normal((100, dim)).astype(np.float32)
+    q = np.stack([centre, rng.standard_normal(dim).astype(np.float32) + 3.0]).astype(np.float32)
+    idx = M.FlatIndex(dim, "l2", "bf16")
+    idx.add(db)
+    idx.set_timing(True)
+    ids, dist = idx.search(q, k)
+    assert idx.last_timing().screen_launches == 2
+    assert set(ids[0].tolist()) == set(range(100))
+    tru_i, _ = O.flat_search_f64(db, q, k, O.L2)
+    assert recall(ids, tru_i) >= 0.99
