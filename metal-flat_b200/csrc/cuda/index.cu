@@ -547,6 +547,7 @@ struct LargePlan {
     int stride_b = 1, sample_b = 0;
     int chunks_a = 0, tpc_a = 0;   // stage-A chunking (>= lists, spread over the SMs)
     int r_stat = 0;                // rank of the statistical floor in the stage-B sample (0: none)
+    int r_guess = 0;               // rank of stage B's statistical floor in the stage-A union
     uint32_t cap = 0;
     int batch = 0;
 };
@@ -586,6 +587,12 @@ LargePlan plan_large(int64_t n, int k, int m, int kp1, int want, int lists_per_c
                 const double mean = static_cast<double>(want) / P.stride_b;
                 const int r = static_cast<int>(std::ceil(mean + 6.0 * std::sqrt(mean))) + 1;
                 P.r_stat = r < want ? r : 0;
+                // stage B only needs its sample's top `want`, i.e. rows down to about
+                // the global (want * stride_b)-th; the stage-A sample holds about
+                // want * stride_b / stride_a of those
+                const double mean_a = static_cast<double>(want) * P.stride_b / P.stride_a;
+                const int ra = static_cast<int>(std::ceil(mean_a + 6.0 * std::sqrt(mean_a))) + 1;
+                P.r_guess = ra < want ? ra : 0;
             }
             // the floor is about the (want * stride_b)-th best row overall; the
             // stage-B buffer holds about want * stride_a / stride_b rows
@@ -621,7 +628,7 @@ LargePlan plan_large(int64_t n, int k, int m, int kp1, int want, int lists_per_c
 template <class ListPass, class BufferPass>
 int estimate_floor(mflat_cu_index* ix, const LargePlan& P, const ScreenParams& base, int want,
                    int kp1, int lists_per_chunk, ListPass list_pass, BufferPass buffer_pass,
-                   uint32_t* thr_stat, cudaStream_t st) {
+                   uint32_t* thr_stat, int* words, cudaStream_t st) {
     ScreenParams pa = base;
     pa.use_floor = 0;
     pa.tile_stride = P.stride_a;
@@ -629,8 +636,10 @@ int estimate_floor(mflat_cu_index* ix, const LargePlan& P, const ScreenParams& b
     pa.tiles_per_chunk = P.tpc_a;
     pa.n_chunks = P.chunks_a;
     CU_TRY(list_pass(pa, kp1), "floor pre-pass launch");
+    const bool guess = P.two_stage && P.r_guess > 0;
     CU_TRY(launch_prepass_floor(pa.part_score, pa.part_id, pa.n_chunks * lists_per_chunk, base.m,
-                                base.m_pad, kp1, want, base.thr, st),
+                                base.m_pad, kp1, want, guess ? P.r_guess : 0, base.thr,
+                                guess ? thr_stat : nullptr, st),
            "floor launch");
     if (!P.two_stage) return ST_OK;
     ScreenParams pb = base;
@@ -641,11 +650,26 @@ int estimate_floor(mflat_cu_index* ix, const LargePlan& P, const ScreenParams& b
     plan_chunks(pb.n_qtiles, P.sample_b, ix->num_sms, kMaxChunks, n_chunks, tpc);
     pb.n_chunks = n_chunks;
     pb.tiles_per_chunk = tpc;
-    CU_TRY(cudaMemsetAsync(base.buf_cnt, 0, static_cast<size_t>(base.m_pad) * sizeof(uint32_t), st), "counts");
-    CU_TRY(buffer_pass(pb), "floor buffer pass launch");
-    CU_TRY(launch_buffer_floor(base.buf_cnt, base.buf_s, base.cap, want, P.r_stat, base.m, base.thr,
-                               thr_stat, st),
-           "floor select launch");
+    // Stage B runs above the stage-A guess (about want * stride_b / stride_a
+    // union rows, plus six standard deviations); when it kept fewer than `want`
+    // rows for some query the guess was too high and stage B is redone above
+    // the valid stage-A floor.
+    for (int attempt = 0; attempt < 2; ++attempt) {
+        const bool g = guess && attempt == 0;
+        pb.thr = g ? thr_stat : base.thr;
+        CU_TRY(cudaMemsetAsync(base.buf_cnt, 0, static_cast<size_t>(base.m_pad) * sizeof(uint32_t), st),
+               "counts");
+        CU_TRY(buffer_pass(pb), "floor buffer pass launch");
+        if (g) CU_TRY(cudaMemsetAsync(words + 3, 0, sizeof(int), st), "status word");
+        CU_TRY(launch_buffer_floor(base.buf_cnt, base.buf_s, base.cap, want, P.r_stat, base.m, base.thr,
+                                   thr_stat, g ? words + 3 : nullptr, st),
+               "floor select launch");
+        if (!g) break;
+        CU_TRY(cudaMemcpyAsync(&ix->host_words[7], words + 3, sizeof(int), cudaMemcpyDeviceToHost, st),
+               "status");
+        CU_TRY(cudaStreamSynchronize(st), "floor estimate");
+        if (ix->host_words[7] == 0) break;
+    }
     return ST_OK;
 }
 
@@ -740,7 +764,7 @@ int search_large(mflat_cu_index* ix, const float* queries, int m, int k_out, int
                 ix, P, sp, 2 * k_out, kKP1, 1,
                 [&](const ScreenParams& q, int kp) { return launch_pass(ix, q, kp, st); },
                 [&](const ScreenParams& q) { return launch_pass(ix, q, 0, st); },
-                ix->thr_stat.as<uint32_t>(), st);
+                ix->thr_stat.as<uint32_t>(), words, st);
             if (rc != ST_OK) return rc;
         }
         sp.use_floor = 1;
@@ -935,7 +959,8 @@ int search_half(mflat_cu_index* ix, const float* queries, int m, int k_out, int3
                    "counts");
             const int rc = estimate_floor(
                 ix, P, sp, k_out, kKP1, 2, [&](const ScreenParams& q, int kpp) { return launch(q, kpp); },
-                [&](const ScreenParams& q) { return launch(q, 0); }, ix->thr_stat.as<uint32_t>(), st);
+                [&](const ScreenParams& q) { return launch(q, 0); }, ix->thr_stat.as<uint32_t>(), words,
+                st);
             if (rc != ST_OK) return rc;
         }
         sp.use_floor = 1;

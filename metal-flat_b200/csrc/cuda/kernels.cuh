@@ -155,9 +155,10 @@ cudaError_t launch_select_large(const LargeSelectParams& p, cudaStream_t stream)
 // with screen distances (L2: max(0, ||q||^2 - s); IP / Cosine: s).
 cudaError_t launch_select_recall(int kp, const SelectParams& p, const float* qsq, cudaStream_t stream);
 cudaError_t launch_prepass_floor(const float* part_s, const int32_t* part_i, int n_lists, int m,
-                                 int m_pad, int kp1, int want, uint32_t* thr, cudaStream_t stream);
+                                 int m_pad, int kp1, int want, int r_guess, uint32_t* thr,
+                                 uint32_t* thr_guess, cudaStream_t stream);
 cudaError_t launch_buffer_floor(const uint32_t* cnt, const float* buf_s, uint32_t cap, int want,
-                                int r_stat, int m, uint32_t* thr, uint32_t* thr_stat,
+                                int r_stat, int m, uint32_t* thr, uint32_t* thr_stat, int* short_count,
                                 cudaStream_t stream);
 cudaError_t launch_floor_check(const uint32_t* cnt, const uint32_t* used, const uint32_t* valid,
                                int want, int m, int* failures, cudaStream_t stream);

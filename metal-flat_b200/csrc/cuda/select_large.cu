@@ -259,16 +259,22 @@ __global__ void __launch_bounds__(kSelThreads) select_large_kernel(const LargeSe
 // union of its L lists (each the KP1 best rows of one sample chunk).  At least
 // `want` sampled rows score at or above it, so it is <= the global want-th
 // best.  thr[q] = 0 (no floor) when the union holds fewer than `want` rows.
+// thr_guess (when non-null) gets max(thr, r_guess-th best): a statistical
+// floor for the next, denser sample pass (see buffer_floor_kernel).
 constexpr int kFloorMax = kFloorMaxEntries;
 
 __global__ void __launch_bounds__(256) prepass_floor_kernel(const float* __restrict__ part_s,
                                                             const int32_t* __restrict__ part_i,
                                                             int n_lists, int m, int m_pad, int kp1,
-                                                            int want, uint32_t* thr) {
+                                                            int want, int r_guess, uint32_t* thr,
+                                                            uint32_t* thr_guess) {
     const int q = blockIdx.x;
     if (q >= m_pad) return;
     if (q >= m) {
-        if (threadIdx.x == 0) thr[q] = 0u;
+        if (threadIdx.x == 0) {
+            thr[q] = 0u;
+            if (thr_guess) thr_guess[q] = 0u;
+        }
         return;
     }
     __shared__ float vals[kFloorMax];
@@ -288,12 +294,22 @@ __global__ void __launch_bounds__(256) prepass_floor_kernel(const float* __restr
     }
     atomicAdd(&sh_valid, valid);
     __syncthreads();
-    if (sh_valid < want) {
-        if (threadIdx.x == 0) thr[q] = 0u;
-        return;
+    const int have = sh_valid;
+    uint32_t valid_floor = 0u;
+    if (have >= want) {
+        radix_select(vals, total, want, hist, &sh_prefix, &sh_remaining);
+        valid_floor = sh_prefix;
+        __syncthreads();
     }
-    radix_select(vals, total, want, hist, &sh_prefix, &sh_remaining);
-    if (threadIdx.x == 0) thr[q] = sh_prefix;
+    uint32_t guess = valid_floor;
+    if (thr_guess && r_guess > 0 && have >= r_guess) {
+        radix_select(vals, total, r_guess, hist, &sh_prefix, &sh_remaining);
+        guess = max(guess, sh_prefix);
+    }
+    if (threadIdx.x == 0) {
+        thr[q] = valid_floor;
+        if (thr_guess) thr_guess[q] = guess;
+    }
 }
 
 // Sharper floor from a buffer-mode pass over a sample: the want-th best score
@@ -313,7 +329,7 @@ __global__ void __launch_bounds__(256) prepass_floor_kernel(const float* __restr
 __global__ void __launch_bounds__(512) buffer_floor_kernel(const uint32_t* __restrict__ cnt,
                                                            const float* __restrict__ buf_s, uint32_t cap,
                                                            int want, int r_stat, int m, uint32_t* thr,
-                                                           uint32_t* thr_stat) {
+                                                           uint32_t* thr_stat, int* short_count) {
     const int q = blockIdx.x;
     if (q >= m) return;
     __shared__ uint32_t hist[256];
@@ -326,6 +342,8 @@ __global__ void __launch_bounds__(512) buffer_floor_kernel(const uint32_t* __res
         radix_select(s, static_cast<int>(n), want, hist, &sh_prefix, &sh_remaining);
         valid = max(valid, sh_prefix);
         __syncthreads();
+    } else if (short_count && threadIdx.x == 0) {
+        atomicAdd(short_count, 1);    // the sample pass's floor kept too few rows
     }
     uint32_t stat = valid;
     if (r_stat > 0 && n >= static_cast<uint32_t>(r_stat)) {
@@ -350,9 +368,10 @@ __global__ void floor_check_kernel(const uint32_t* __restrict__ cnt, const uint3
 }  // namespace
 
 cudaError_t launch_buffer_floor(const uint32_t* cnt, const float* buf_s, uint32_t cap, int want,
-                                int r_stat, int m, uint32_t* thr, uint32_t* thr_stat,
+                                int r_stat, int m, uint32_t* thr, uint32_t* thr_stat, int* short_count,
                                 cudaStream_t stream) {
-    buffer_floor_kernel<<<m, 512, 0, stream>>>(cnt, buf_s, cap, want, r_stat, m, thr, thr_stat);
+    buffer_floor_kernel<<<m, 512, 0, stream>>>(cnt, buf_s, cap, want, r_stat, m, thr, thr_stat,
+                                                short_count);
     return cudaGetLastError();
 }
 
@@ -369,9 +388,11 @@ cudaError_t launch_select_large(const LargeSelectParams& p, cudaStream_t stream)
 }
 
 cudaError_t launch_prepass_floor(const float* part_s, const int32_t* part_i, int n_lists, int m,
-                                 int m_pad, int kp1, int want, uint32_t* thr, cudaStream_t stream) {
+                                 int m_pad, int kp1, int want, int r_guess, uint32_t* thr,
+                                 uint32_t* thr_guess, cudaStream_t stream) {
     if (n_lists * kp1 > kFloorMax || want < 1) return cudaErrorInvalidValue;
-    prepass_floor_kernel<<<m_pad, 256, 0, stream>>>(part_s, part_i, n_lists, m, m_pad, kp1, want, thr);
+    prepass_floor_kernel<<<m_pad, 256, 0, stream>>>(part_s, part_i, n_lists, m, m_pad, kp1, want,
+                                                    r_guess, thr, thr_guess);
     return cudaGetLastError();
 }
 

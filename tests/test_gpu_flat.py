@@ -248,3 +248,18 @@ def test_large_k_statistical_floor_redo():
     assert_exact(ids, dist, db, q, k, "l2")
     assert tm[0].screen_launches == 2          # the redo ran
     assert set(ids[0].tolist()) <= set(range(200))
+
+
+def test_large_k_stage_b_guess_redo():
+    """70 rows near the query sit in tile 0, which every sample contains: the
+    stage-A guess for the stage-B floor lands among them, stage B keeps fewer
+    than 2k rows, and stage B is redone above the valid stage-A floor."""
+    rng = np.random.default_rng(zlib.crc32(b"stage-b-guess"))
+    n, dim, k = 2_000_000, 16, 100
+    db = rng.standard_normal((n, dim)).astype(np.float32)
+    centre = np.full(dim, 0.5, np.float32)
+    db[:70] = centre + 0.01 * rng.standard_normal((70, dim)).astype(np.float32)
+    q = np.stack([centre, rng.standard_normal(dim).astype(np.float32)])
+    ids, dist = search(db, q, k, "l2")
+    assert_exact(ids, dist, db, q, k, "l2")
+    assert set(range(70)) <= set(ids[0].tolist())
