@@ -118,7 +118,10 @@ MFLAT_API int mflat_flat_device(const mflat_flat_index_t*);
 /* Device-resident variants: every pointer is device memory on the index's
  * device; `stream` is a cudaStream_t (NULL = the legacy default stream).  The
  * call enqueues work on `stream` and returns without synchronising; results
- * are valid once `stream` reaches that point.  *out_k_used is host memory. */
+ * are valid once `stream` reaches that point.  Exception: searches that use
+ * per-query candidate buffers (k > 21 on FP32; k > 16, or a large m * n, on
+ * FP16 / BF16) check status words on the host and return after the search.
+ * *out_k_used is host memory. */
 MFLAT_API mflat_status_t mflat_flat_add_device(mflat_flat_index_t*, const float* d_vectors,
         int n, void* stream);
 MFLAT_API mflat_status_t mflat_flat_search_device(mflat_flat_index_t*, const float* d_queries,
