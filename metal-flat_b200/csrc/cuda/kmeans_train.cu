@@ -11,7 +11,8 @@
 //      reference's single-thread CPU k-means (CoarseQuantizer.mm:47-55);
 //   3. empty cells keep their old centroid here; the host reseeds them from
 //      its mt19937 in cell order (Internal.h:90-98) through
-//      mflat_cu_kmeans_reseed, because the draws continue the host's stream.
+//      mflat_cu_kmeans_fetch_rows + mflat_cu_kmeans_set_rows, because the
+//      draws continue the host's stream.
 // finish() assigns every point with the final centroids and builds the CSR
 // inverted-list scaffold (CoarseQuantizer.mm:134-143): cellStart = exclusive
 // prefix sum of the cell histogram, reorderedIds = point ids grouped by cell,
