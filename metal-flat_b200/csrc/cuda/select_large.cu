@@ -49,16 +49,50 @@ __device__ void radix_select(const float* __restrict__ s, int n, int want, uint3
             if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
         }
         __syncthreads();
-        if (threadIdx.x == 0) {
-            int rem = *sh_remaining;
-            uint32_t acc = 0;
-            int d = 255;
-            for (; d > 0; --d) {
-                if (acc + hist[d] >= static_cast<uint32_t>(rem)) break;
-                acc += hist[d];
+        if (threadIdx.x < 32) {
+            // Digit d of the want-th largest key: the highest d whose count of
+            // keys in digits [d, 255] reaches `rem` (d = 0 when none of 255..1
+            // does), and acc = the count in digits above d.  Warp 0 scans the
+            // 256 bins, 8 per lane, from the top.
+            const int lane = threadIdx.x;
+            const uint32_t rem = static_cast<uint32_t>(*sh_remaining);
+            uint32_t t = 0;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) t += hist[8 * lane + j];
+            uint32_t incl = t;   // sum over lanes >= lane
+#pragma unroll
+            for (int off = 1; off < 32; off <<= 1) {
+                const uint32_t v = __shfl_down_sync(0xffffffffu, incl, off);
+                if (lane + off < 32) incl += v;
             }
-            *sh_prefix = prefix | (static_cast<uint32_t>(d) << shift);
-            *sh_remaining = rem - static_cast<int>(acc);
+            uint32_t acc = incl - t;   // keys in digits above this lane's bins
+            int found = -1;
+            uint32_t found_acc = 0;
+            if (acc < rem && rem <= acc + t) {
+                for (int j = 7; j >= 0; --j) {
+                    const int d = 8 * lane + j;
+                    if (d == 0) break;
+                    if (acc + hist[d] >= rem) {
+                        found = d;
+                        found_acc = acc;
+                        break;
+                    }
+                    acc += hist[d];
+                }
+            }
+            const unsigned who = __ballot_sync(0xffffffffu, found >= 0);
+            const uint32_t total = __shfl_sync(0xffffffffu, incl, 0);
+            int d = 0;
+            uint32_t above = total - hist[0];
+            if (who) {
+                const int src = __ffs(who) - 1;
+                d = __shfl_sync(0xffffffffu, found, src);
+                above = __shfl_sync(0xffffffffu, found_acc, src);
+            }
+            if (lane == 0) {
+                *sh_prefix = prefix | (static_cast<uint32_t>(d) << shift);
+                *sh_remaining = static_cast<int>(rem - above);
+            }
         }
         mask |= 255u << shift;
         __syncthreads();
