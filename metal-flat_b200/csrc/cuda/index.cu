@@ -382,11 +382,12 @@ int kp_for(int k) { return k <= 21 ? 32 : 0; }
 
 // Database chunks per query tile: whole work units on every SM.
 void plan_chunks(int n_qtiles, int n_tiles, int num_sms, int max_chunks, int& n_chunks,
-                 int& tiles_per_chunk) {
-    int best_s = 1;
-    double best_eff = -1.0;
+                 int& tiles_per_chunk, int min_chunks = 1) {
     const int smax = std::min(max_chunks, n_tiles);
-    for (int s = 1; s <= smax; ++s) {
+    const int smin = std::max(1, std::min(min_chunks, smax));
+    int best_s = smin;
+    double best_eff = -1.0;
+    for (int s = smin; s <= smax; ++s) {
         const int tpc = (n_tiles + s - 1) / s;
         const int sc = (n_tiles + tpc - 1) / tpc;
         const int64_t units = static_cast<int64_t>(n_qtiles) * sc;
@@ -397,6 +398,24 @@ void plan_chunks(int n_qtiles, int n_tiles, int num_sms, int max_chunks, int& n_
     }
     tiles_per_chunk = (n_tiles + best_s - 1) / best_s;
     n_chunks = (n_tiles + tiles_per_chunk - 1) / tiles_per_chunk;
+}
+
+// Bytes of one 256-row database tile as the screens read it.
+size_t tile_bytes(const mflat_cu_index* ix) {
+    return static_cast<size_t>(kBN) * ix->d_pad * (ix->storage != 0 ? 2 : 8);
+}
+
+// Chunking of a buffer-mode pass (no per-chunk lists, so no fan-in limit):
+// chunks of at most ~8 MB of rows.  The CTAs working on the same chunk share
+// its tiles through L2, but in buffer mode their progress drifts apart (the
+// appends differ per query tile); with small chunks the rows still in use by
+// the leading and the trailing CTAs stay within L2 instead of being fetched
+// from HBM again by each query tile.
+void plan_buffer_chunks(int n_qtiles, int n_tiles, int num_sms, size_t tile_bytes, int& n_chunks,
+                        int& tiles_per_chunk) {
+    const int max_tpc = static_cast<int>(std::max<size_t>(16, (size_t(8) << 20) / std::max<size_t>(tile_bytes, 1)));
+    const int min_chunks = (n_tiles + max_tpc - 1) / max_tpc;
+    plan_chunks(n_qtiles, n_tiles, num_sms, n_tiles, n_chunks, tiles_per_chunk, min_chunks);
 }
 
 }  // namespace
@@ -647,7 +666,7 @@ int estimate_floor(mflat_cu_index* ix, const LargePlan& P, const ScreenParams& b
     pb.tile_stride = P.stride_b;
     pb.n_tiles = P.sample_b;
     int n_chunks = 1, tpc = P.sample_b;
-    plan_chunks(pb.n_qtiles, P.sample_b, ix->num_sms, kMaxChunks, n_chunks, tpc);
+    plan_buffer_chunks(pb.n_qtiles, P.sample_b, ix->num_sms, tile_bytes(ix), n_chunks, tpc);
     pb.n_chunks = n_chunks;
     pb.tiles_per_chunk = tpc;
     // Stage B runs above the stage-A guess (about want * stride_b / stride_a
@@ -771,7 +790,7 @@ int search_large(mflat_cu_index* ix, const float* queries, int m, int k_out, int
         sp.tile_stride = 1;
         sp.n_tiles = n_tiles;
         int n_chunks = 1, tpc = n_tiles;
-        plan_chunks(sp.n_qtiles, n_tiles, ix->num_sms, kMaxChunks, n_chunks, tpc);
+        plan_buffer_chunks(sp.n_qtiles, n_tiles, ix->num_sms, tile_bytes(ix), n_chunks, tpc);
         sp.n_chunks = n_chunks;
         sp.tiles_per_chunk = tpc;
 
@@ -967,7 +986,7 @@ int search_half(mflat_cu_index* ix, const float* queries, int m, int k_out, int3
         sp.tile_stride = 1;
         sp.n_tiles = n_tiles;
         int n_chunks = 1, tpc = n_tiles;
-        plan_chunks(sp.n_qtiles, n_tiles, ix->num_sms, kMaxChunks, n_chunks, tpc);
+        plan_buffer_chunks(sp.n_qtiles, n_tiles, ix->num_sms, tile_bytes(ix), n_chunks, tpc);
         sp.n_chunks = n_chunks;
         sp.tiles_per_chunk = tpc;
         LargeSelectParams ls{};
