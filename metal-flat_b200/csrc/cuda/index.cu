@@ -592,12 +592,16 @@ LargePlan plan_large(int64_t n, int k, int m, int kp1, int want, int lists_per_c
             P.prepass = true;
             P.stride_a = P.stride_b;
             P.sample_a = P.sample_b;
-            // a list-mode pass over 1/256 of the tiles, then a buffer-mode pass
-            // over 1/stride_b sharpens its floor, when the sparse sample is big enough
-            if ((n_tiles + 255) / 256 >= 2 * P.lists && P.stride_b == 16) {
-                P.two_stage = true;
-                P.stride_a = 256;
-                P.sample_a = (n_tiles + 255) / 256;
+            // a list-mode pass over 1/stride_a of the tiles (the sparsest of
+            // 1/256, 1/128, 1/64 that still gives every list two tiles), then a
+            // buffer-mode pass over 1/stride_b sharpens its floor
+            for (int sa = 256; sa >= 64 && P.stride_b == 16; sa /= 2) {
+                if ((n_tiles + sa - 1) / sa >= 2 * P.lists) {
+                    P.two_stage = true;
+                    P.stride_a = sa;
+                    P.sample_a = (n_tiles + sa - 1) / sa;
+                    break;
+                }
             }
             if (P.two_stage) {
                 // about want / stride_b of the sampled rows are in the global

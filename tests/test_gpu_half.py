@@ -91,6 +91,18 @@ def test_config5_like_bf16_large_k():
     assert recall(ids, tru_i) >= 0.99
 
 
+def test_two_stage_denser_stage_a_16bit():
+    """3M rows at k = 1024: stage A samples every 64th tile (1/256 would give
+    fewer than two tiles per list); the kernel's result matches the exact
+    search of the rounded data."""
+    rng = np.random.default_rng(zlib.crc32(b"two-stage-stride-64-16"))
+    db = rng.standard_normal((3_000_000, 32)).astype(np.float32)
+    q = rng.standard_normal((6, 32)).astype(np.float32)
+    ids, dist = run(db, q, 1024, "l2", "bf16")
+    ref_i, ref_d = O.flat_search_f64(rounded(db, "bf16", "l2"), rounded(q, "bf16", "l2"), 1025, O.L2)
+    assert O.exact_ids_match(ids, dist, ref_i, ref_d, rel=1e-4) == 0
+
+
 def test_statistical_floor_redo_16bit():
     """As the fp32 case: the query's 100 nearest rows fill tile 0, the
     statistical floor fails the check and the batch is redone."""
