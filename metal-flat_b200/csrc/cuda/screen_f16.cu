@@ -239,6 +239,17 @@ screen_f16_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
         const int wq = warp & 3;
         const int row_in_tile = wq * 32 + lane;
         const uint32_t lane_addr = tmem_base + (static_cast<uint32_t>(wq * 32) << 16);
+        // Accumulator b (and its bias slot) goes back to the MMA warp as soon as
+        // the warp's last tcgen05.ld of the tile has completed and that chunk's
+        // bias loads are issued, before the last chunk is scored: the refill of
+        // b (tile t + 2) then overlaps that scoring.  The arrival releases the
+        // preceding shared-memory reads, and the bias copy into the slot is
+        // issued only after the MMA thread has observed it.
+        auto release_acc = [&](uint32_t b) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&S.acc_empty[b]);
+        };
         uint32_t tcount = 0;
         bool ok = true;
         for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
@@ -291,6 +302,7 @@ screen_f16_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
                         tmem_ld_32x32b_x32(taddr + c * 32, r);
                         if (!raw) load_bias_shared(cb, cb_tile + c * 32);
                         tmem_wait_ld_regs(r);
+                        if (c == kCols / 32 - 1) release_acc(b);
                         if constexpr (kBuf) {
                             if (raw) buffer_chunk_raw(r, floor_adj, br, id_tile + c * 32);
                             else buffer_chunk(r, cb, p.alpha, floor_adj, br, id_tile + c * 32);
@@ -323,6 +335,8 @@ screen_f16_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
                         if (c + 2 < kCols / 32) {
                             __syncwarp();
                             tmem_ld_32x32b_x32(taddr + (c + 2) * 32, ra);
+                        } else {
+                            release_acc(b);
                         }
                         if constexpr (kBuf) {
                             if (raw) buffer_chunk_raw(rb, floor_adj, br, id_tile + (c + 1) * 32);
@@ -333,9 +347,6 @@ screen_f16_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
                         }
                     }
                 }
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&S.acc_empty[b]);
             }
             if (!ok) break;
             if (!kBuf && live) {
