@@ -167,22 +167,77 @@ __device__ __forceinline__ void append_passing(const float (&sc)[32], float floo
     }
 }
 
+// Per-thread stage of up to kStage appends, held in registers.  Staged entries
+// are published -- one atomic reserves their slots, then the stores -- when the
+// stage would overflow and at the end of each unit, so the atomic's round trip
+// (which all warps of the tile wait for before the accumulator is released)
+// leaves the per-chunk slow path.  A chunk with more than kStage passing columns
+// is appended directly.
+struct AppendStage {
+    static constexpr uint32_t kStage = 2;
+    float s0, s1;
+    int i0, i1;
+    uint32_t n;
+
+    __device__ __forceinline__ void init() {
+        n = 0;
+        s0 = s1 = 0.0f;
+        i0 = i1 = 0;
+    }
+    // static register slots chosen by a compare (no local memory)
+    __device__ __forceinline__ void put(float v, int id) {
+        if (n == 0) { s0 = v; i0 = id; }
+        else { s1 = v; i1 = id; }
+        ++n;
+    }
+    __device__ __forceinline__ void flush(const BufferRow& br) {
+        if (n == 0) return;
+        const uint32_t base = atomicAdd(br.cnt, n);
+        if (base < br.cap) { br.s[base] = s0; br.id[base] = i0; }
+        if (n > 1 && base + 1 < br.cap) { br.s[base + 1] = s1; br.id[base + 1] = i1; }
+        n = 0;
+    }
+};
+
+__device__ __forceinline__ void stage_passing(const float (&sc)[32], float floor_adj,
+                                              const BufferRow& br, AppendStage& st, int id0) {
+    const uint32_t mask = passing_mask(sc, floor_adj);
+    const uint32_t np = __popc(mask);
+    if (st.n + np > AppendStage::kStage) {
+        st.flush(br);
+        if (np > AppendStage::kStage) {
+            append_passing(sc, floor_adj, br, id0);
+            return;
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        if ((mask >> (4 * i)) & 0xFu) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int j = 4 * i + e;
+                if ((mask >> j) & 1u) st.put(sc[j], id0 + j);
+            }
+        }
+    }
+}
+
 __device__ __forceinline__ void buffer_chunk(const uint32_t (&r)[32], const float4 (&cb)[8],
                                              float alpha, float floor_adj, const BufferRow& br,
-                                             int id0) {
+                                             AppendStage& st, int id0) {
     float sc[32];
     chunk_scores(r, cb, alpha, sc);
-    if (max_tree32(sc) > floor_adj) append_passing(sc, floor_adj, br, id0);
+    if (max_tree32(sc) > floor_adj) stage_passing(sc, floor_adj, br, st, id0);
 }
 
 // Inner-product variant for chunks wholly inside the database: the bias is 0,
 // so the accumulator is the score (no bias load, no FFMA).
 __device__ __forceinline__ void buffer_chunk_raw(const uint32_t (&r)[32], float floor_adj,
-                                                 const BufferRow& br, int id0) {
+                                                 const BufferRow& br, AppendStage& st, int id0) {
     float sc[32];
 #pragma unroll
     for (int j = 0; j < 32; ++j) sc[j] = __uint_as_float(r[j]);
-    if (max_tree32(sc) > floor_adj) append_passing(sc, floor_adj, br, id0);
+    if (max_tree32(sc) > floor_adj) stage_passing(sc, floor_adj, br, st, id0);
 }
 
 template <int KP>

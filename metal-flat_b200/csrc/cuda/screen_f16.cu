@@ -262,6 +262,8 @@ screen_f16_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
             TopList<KP> L;
             L.init();
             BufferRow br{};
+            AppendStage st;
+            st.init();
             if constexpr (kBuf) {
                 const int rr = live ? row : 0;
                 br = BufferRow{p.buf_cnt + rr, p.buf_s + static_cast<int64_t>(rr) * p.cap,
@@ -304,8 +306,8 @@ screen_f16_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
                         tmem_wait_ld_regs(r);
                         if (c == kCols / 32 - 1) release_acc(b);
                         if constexpr (kBuf) {
-                            if (raw) buffer_chunk_raw(r, floor_adj, br, id_tile + c * 32);
-                            else buffer_chunk(r, cb, p.alpha, floor_adj, br, id_tile + c * 32);
+                            if (raw) buffer_chunk_raw(r, floor_adj, br, st, id_tile + c * 32);
+                            else buffer_chunk(r, cb, p.alpha, floor_adj, br, st, id_tile + c * 32);
                         } else {
                             if (raw) scan_chunk_raw<KP>(r, floor_adj, L, id_tile + c * 32);
                             else scan_chunk<KP>(r, cb, p.alpha, floor_adj, L, id_tile + c * 32);
@@ -324,8 +326,8 @@ screen_f16_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
                         __syncwarp();
                         tmem_ld_32x32b_x32(taddr + (c + 1) * 32, rb);
                         if constexpr (kBuf) {
-                            if (raw) buffer_chunk_raw(ra, floor_adj, br, id_tile + c * 32);
-                            else buffer_chunk(ra, cb, p.alpha, floor_adj, br, id_tile + c * 32);
+                            if (raw) buffer_chunk_raw(ra, floor_adj, br, st, id_tile + c * 32);
+                            else buffer_chunk(ra, cb, p.alpha, floor_adj, br, st, id_tile + c * 32);
                         } else {
                             if (raw) scan_chunk_raw<KP>(ra, floor_adj, L, id_tile + c * 32);
                             else scan_chunk<KP>(ra, cb, p.alpha, floor_adj, L, id_tile + c * 32);
@@ -339,8 +341,8 @@ screen_f16_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
                             release_acc(b);
                         }
                         if constexpr (kBuf) {
-                            if (raw) buffer_chunk_raw(rb, floor_adj, br, id_tile + (c + 1) * 32);
-                            else buffer_chunk(rb, cb, p.alpha, floor_adj, br, id_tile + (c + 1) * 32);
+                            if (raw) buffer_chunk_raw(rb, floor_adj, br, st, id_tile + (c + 1) * 32);
+                            else buffer_chunk(rb, cb, p.alpha, floor_adj, br, st, id_tile + (c + 1) * 32);
                         } else {
                             if (raw) scan_chunk_raw<KP>(rb, floor_adj, L, id_tile + (c + 1) * 32);
                             else scan_chunk<KP>(rb, cb, p.alpha, floor_adj, L, id_tile + (c + 1) * 32);
@@ -348,6 +350,7 @@ screen_f16_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
                     }
                 }
             }
+            if constexpr (kBuf) st.flush(br);   // the unit's staged appends
             if (!ok) break;
             if (!kBuf && live) {
                 const int64_t o = (static_cast<int64_t>(ch * kEpiWG + g) * p.m_pad + row) * KP;

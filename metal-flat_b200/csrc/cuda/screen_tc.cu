@@ -304,6 +304,8 @@ screen_tf32x3_kernel(const __grid_constant__ CUtensorMap tm_a_hi,
             TopList<KP> L;
             L.init();
             BufferRow br{};
+            AppendStage st;
+            st.init();
             if constexpr (kBuf) {
                 const int rr = live ? row : 0;
                 br = BufferRow{p.buf_cnt + rr, p.buf_s + static_cast<int64_t>(rr) * p.cap,
@@ -345,7 +347,7 @@ screen_tf32x3_kernel(const __grid_constant__ CUtensorMap tm_a_hi,
                     __syncwarp();
                     tmem_ld_32x32b_x32(taddr + (c + 1) * 32, rb);
                     load_bias(cbv, cb_tile + (c + 1) * 32);
-                    if constexpr (kBuf) buffer_chunk(ra, ca, p.alpha, floor_adj, br, id_tile + c * 32);
+                    if constexpr (kBuf) buffer_chunk(ra, ca, p.alpha, floor_adj, br, st, id_tile + c * 32);
                     else scan_chunk<KP>(ra, ca, p.alpha, floor_adj, L, id_tile + c * 32);
                     tmem_wait_ld_regs(rb);
                     if (c + 2 < kBN / 32) {
@@ -354,13 +356,14 @@ screen_tf32x3_kernel(const __grid_constant__ CUtensorMap tm_a_hi,
                         load_bias(ca, cb_tile + (c + 2) * 32);
                     }
                     if constexpr (kBuf)
-                        buffer_chunk(rb, cbv, p.alpha, floor_adj, br, id_tile + (c + 1) * 32);
+                        buffer_chunk(rb, cbv, p.alpha, floor_adj, br, st, id_tile + (c + 1) * 32);
                     else scan_chunk<KP>(rb, cbv, p.alpha, floor_adj, L, id_tile + (c + 1) * 32);
                 }
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&S.acc_empty[b]);
             }
+            if constexpr (kBuf) st.flush(br);   // the unit's staged appends
             if (!ok) break;
             if (!kBuf && live) {
                 const int64_t o = (static_cast<int64_t>(ch) * p.m_pad + row) * KP;
