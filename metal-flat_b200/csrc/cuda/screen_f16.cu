@@ -8,9 +8,12 @@
 //   * the query tile stays resident in shared memory when it fits
 //     (d <= 384); otherwise it is streamed with the database tile, one
 //     k-block of each per ring stage (d = 768 for config 2);
-//   * two epilogue warpgroups split each tile's 256 columns (the MMA of a
-//     d = 128 tile lasts only ~1k cycles); in list mode each keeps its own
-//     top-KP, written as two lists per (query, chunk) for the select stage.
+//   * the epilogue warpgroups split each tile's 256 columns (the MMA of a
+//     d = 128 tile lasts only ~1k cycles): four in buffer mode, two in list
+//     mode, where each keeps its own top-KP, written as two lists per
+//     (query, chunk) for the select stage;
+//   * each warp hands its accumulator back after its last TMEM load of the
+//     tile, before scoring that chunk.
 #include "epilogue.cuh"
 #include "kernels.cuh"
 #include "ptx.cuh"
