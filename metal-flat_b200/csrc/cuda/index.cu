@@ -380,42 +380,9 @@ void order_after(cudaStream_t waiter, cudaStream_t producer) {
 // band, so that the exact fallback stays rare.
 int kp_for(int k) { return k <= 21 ? 32 : 0; }
 
-// Database chunks per query tile: whole work units on every SM.
-void plan_chunks(int n_qtiles, int n_tiles, int num_sms, int max_chunks, int& n_chunks,
-                 int& tiles_per_chunk, int min_chunks = 1) {
-    const int smax = std::min(max_chunks, n_tiles);
-    const int smin = std::max(1, std::min(min_chunks, smax));
-    int best_s = smin;
-    double best_eff = -1.0;
-    for (int s = smin; s <= smax; ++s) {
-        const int tpc = (n_tiles + s - 1) / s;
-        const int sc = (n_tiles + tpc - 1) / tpc;
-        const int64_t units = static_cast<int64_t>(n_qtiles) * sc;
-        const int64_t waves = (units + num_sms - 1) / num_sms;
-        const double eff = static_cast<double>(units) / static_cast<double>(waves * num_sms);
-        if (eff > best_eff + 0.02) { best_eff = eff; best_s = s; }
-        if (best_eff > 0.97 && units >= num_sms) break;
-    }
-    tiles_per_chunk = (n_tiles + best_s - 1) / best_s;
-    n_chunks = (n_tiles + tiles_per_chunk - 1) / tiles_per_chunk;
-}
-
 // Bytes of one 256-row database tile as the screens read it.
 size_t tile_bytes(const mflat_cu_index* ix) {
     return static_cast<size_t>(kBN) * ix->d_pad * (ix->storage != 0 ? 2 : 8);
-}
-
-// Chunking of a buffer-mode pass (no per-chunk lists, so no fan-in limit):
-// chunks of at most ~8 MB of rows.  The CTAs working on the same chunk share
-// its tiles through L2, but in buffer mode their progress drifts apart (the
-// appends differ per query tile); with small chunks the rows still in use by
-// the leading and the trailing CTAs stay within L2 instead of being fetched
-// from HBM again by each query tile.
-void plan_buffer_chunks(int n_qtiles, int n_tiles, int num_sms, size_t tile_bytes, int& n_chunks,
-                        int& tiles_per_chunk) {
-    const int max_tpc = static_cast<int>(std::max<size_t>(16, (size_t(8) << 20) / std::max<size_t>(tile_bytes, 1)));
-    const int min_chunks = (n_tiles + max_tpc - 1) / max_tpc;
-    plan_chunks(n_qtiles, n_tiles, num_sms, n_tiles, n_chunks, tiles_per_chunk, min_chunks);
 }
 
 }  // namespace
@@ -548,99 +515,12 @@ int run_screen(mflat_cu_index* ix, const float* queries, int m, int kp, int on_d
 // candidate buffers stay within a fixed budget.
 namespace {
 
-constexpr int64_t kAllRowsBuffered = 32768;        // below this, no pre-pass
-
 // Bytes the candidate buffers of one query batch may take: a quarter of the
 // device's free memory, at most 16 GB.
 size_t buffer_budget() {
     size_t free_b = 0, total_b = 0;
     if (cudaMemGetInfo(&free_b, &total_b) != cudaSuccess) return size_t(4) << 30;
     return std::max<size_t>(size_t(1) << 30, std::min<size_t>(size_t(16) << 30, free_b / 4));
-}
-
-struct LargePlan {
-    bool prepass = false;          // floor estimate before the main pass
-    bool two_stage = false;        // stage A (list, sparse) + stage B (buffer, denser)
-    int lists = 0;                 // stage-A lists (chunks)
-    int stride_a = 1, sample_a = 0;
-    int stride_b = 1, sample_b = 0;
-    int chunks_a = 0, tpc_a = 0;   // stage-A chunking (>= lists, spread over the SMs)
-    int r_stat = 0;                // rank of the statistical floor in the stage-B sample (0: none)
-    int r_guess = 0;               // rank of stage B's statistical floor in the stage-A union
-    uint32_t cap = 0;
-    int batch = 0;
-};
-
-// want: rank whose sampled score becomes the floor (2k exact path, k recall).
-// lists_per_chunk: lists one list-mode chunk produces (f16 kernel: 2).
-LargePlan plan_large(int64_t n, int k, int m, int kp1, int want, int lists_per_chunk, int num_sms) {
-    LargePlan P;
-    const int n_tiles = static_cast<int>((n + kBN - 1) / kBN);
-    const int64_t n_round = (n + 255) / 256 * 256;
-    if (n <= kAllRowsBuffered) {
-        P.cap = static_cast<uint32_t>(n_round);
-    } else {
-        // union of lists * kp1 >= 2 * want sampled scores; floor = its want-th best
-        const int lists_total = std::min(4096 / kp1, std::max(1, (2 * want + kp1 - 1) / kp1));
-        P.lists = std::max(1, (lists_total + lists_per_chunk - 1) / lists_per_chunk);
-        P.stride_b = 16;
-        while (P.stride_b > 1 && (n_tiles + P.stride_b - 1) / P.stride_b < 2 * P.lists) P.stride_b /= 2;
-        P.sample_b = (n_tiles + P.stride_b - 1) / P.stride_b;
-        if (P.sample_b < P.lists) {                      // too small to sample: buffer all
-            P.cap = static_cast<uint32_t>(n_round);
-        } else {
-            P.prepass = true;
-            P.stride_a = P.stride_b;
-            P.sample_a = P.sample_b;
-            // a list-mode pass over 1/stride_a of the tiles (the sparsest of
-            // 1/256, 1/128, 1/64 that still gives every list two tiles), then a
-            // buffer-mode pass over 1/stride_b sharpens its floor
-            for (int sa = 256; sa >= 64 && P.stride_b == 16; sa /= 2) {
-                if ((n_tiles + sa - 1) / sa >= 2 * P.lists) {
-                    P.two_stage = true;
-                    P.stride_a = sa;
-                    P.sample_a = (n_tiles + sa - 1) / sa;
-                    break;
-                }
-            }
-            if (P.two_stage) {
-                // about want / stride_b of the sampled rows are in the global
-                // top-want; six standard deviations above that (see
-                // buffer_floor_kernel) the floor admits ~r_stat * stride_b rows
-                const double mean = static_cast<double>(want) / P.stride_b;
-                const int r = static_cast<int>(std::ceil(mean + 6.0 * std::sqrt(mean))) + 1;
-                P.r_stat = r < want ? r : 0;
-                // stage B only needs its sample's top `want`, i.e. rows down to about
-                // the global (want * stride_b)-th; the stage-A sample holds about
-                // want * stride_b / stride_a of those
-                const double mean_a = static_cast<double>(want) * P.stride_b / P.stride_a;
-                const int ra = static_cast<int>(std::ceil(mean_a + 6.0 * std::sqrt(mean_a))) + 1;
-                P.r_guess = ra < want ? ra : 0;
-            }
-            // the floor is about the (want * stride_b)-th best row overall; the
-            // stage-B buffer holds about want * stride_a / stride_b rows
-            const int64_t expect = static_cast<int64_t>(want) * P.stride_b;
-            int64_t cap = std::max<int64_t>(4 * expect, 4096);
-            cap = std::min<int64_t>((cap + 255) / 256 * 256, n_round);
-            P.cap = static_cast<uint32_t>(cap);
-        }
-    }
-    const size_t per_q = static_cast<size_t>(P.cap) * 8 + 64;
-    P.batch = static_cast<int>(std::max<size_t>(kBM, std::min<size_t>(m, buffer_budget() / per_q)));
-    P.batch = std::min(P.batch, m);
-    if (P.prepass) {
-        // Stage A needs >= `lists` chunks for its union; more chunks only enlarge
-        // the union (a sharper floor) and keep every SM busy when few query
-        // tiles share the pass.
-        const int n_qt = (P.batch + kBM - 1) / kBM;
-        const int max_a = std::max(P.lists, kFloorMaxEntries / (kp1 * lists_per_chunk));
-        plan_chunks(n_qt, P.sample_a, num_sms, max_a, P.chunks_a, P.tpc_a);
-        if (P.chunks_a < P.lists) {
-            P.tpc_a = (P.sample_a + P.lists - 1) / P.lists;
-            P.chunks_a = (P.sample_a + P.tpc_a - 1) / P.tpc_a;
-        }
-    }
-    return P;
 }
 
 // Floor estimate for one query batch (see plan_large): stage A list-mode
@@ -714,7 +594,7 @@ cudaError_t launch_pass(mflat_cu_index* ix, const ScreenParams& sp, int kp, cuda
 int search_large(mflat_cu_index* ix, const float* queries, int m, int k_out, int32_t* d_ids,
                  float* d_dist, int on_device, cudaStream_t st) {
     constexpr int kKP1 = 32;
-    const LargePlan P = plan_large(ix->n, k_out, m, kKP1, 2 * k_out, 1, ix->num_sms);
+    const LargePlan P = plan_large(ix->n, k_out, m, kKP1, 2 * k_out, 1, ix->num_sms, buffer_budget());
     const int d_pad = ix->d_pad;
     const int n_tiles = static_cast<int>((ix->n + kBN - 1) / kBN);
     const float* qsrc = queries;
@@ -894,7 +774,7 @@ int search_half(mflat_cu_index* ix, const float* queries, int m, int k_out, int3
     if (list_mode) {
         P.batch = m;
     } else {
-        P = plan_large(ix->n, k_out, m, kKP1, k_out, 2, ix->num_sms);   // two lists (column halves) per chunk
+        P = plan_large(ix->n, k_out, m, kKP1, k_out, 2, ix->num_sms, buffer_budget());   // two lists (column halves) per chunk
     }
     const int bm_pad = (P.batch + kBM - 1) / kBM * kBM;
     CU_TRY(ix->q16.ensure(static_cast<size_t>(bm_pad) * d_pad * 2), "query conversion");

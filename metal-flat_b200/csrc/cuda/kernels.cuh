@@ -25,16 +25,14 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include "plan.h"
+
 namespace mflat_cu {
 
-constexpr int kBM = 128;          // queries per tile (TMEM lanes)
-constexpr int kBN = 256;          // database rows per tile (UMMA N)
 constexpr int kBK = 32;           // fp32 elements per k-block (128 bytes)
 constexpr int kMaxDPadResident = 128;   // A (queries) kept resident in smem up to this
-constexpr int kMaxChunks = 256;   // candidate lists per query (select kernel fan-in)
 constexpr int kSelectMaxThreads = 256;   // one select thread per list
 constexpr int kFbChunks = 64;     // database chunks of the exact fallback scan
-constexpr int kFloorMaxEntries = 4096;   // list entries per query the floor select takes
 
 enum Metric : int { kL2 = 0, kIP = 1, kCosine = 2 };
 
