@@ -294,9 +294,10 @@ screen_f16_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
                 const uint32_t taddr = lane_addr + b * kBN + g * kCols;
                 // inner product on columns wholly inside the database: bias 0
                 const bool raw = p.alpha == 1.0f && static_cast<int64_t>(id_tile) + kCols <= p.n;
-                if constexpr (kEpiWG == 4) {
-                    // 4 warps per SMSP: one chunk at a time, latency hidden by
-                    // the other warps (keeps the thread within 96 registers)
+                if constexpr (kBuf) {
+                    // buffer mode, 4 warps per SMSP: one chunk at a time, latency
+                    // hidden by the other warps (keeps the thread within 96 registers)
+                    static_assert(kEpiWG == 4, "buffer mode runs four epilogue warpgroups");
                     __syncwarp();
                     tc_fence_after();
 #pragma unroll 1
@@ -308,33 +309,25 @@ screen_f16_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
                         if (!raw) load_bias_shared(cb, cb_tile + c * 32);
                         tmem_wait_ld_regs(r);
                         if (c == kCols / 32 - 1) release_acc(b);
-                        if constexpr (kBuf) {
-                            if (raw) buffer_chunk_raw(r, floor_adj, br, st, id_tile + c * 32);
-                            else buffer_chunk(r, cb, p.alpha, floor_adj, br, st, id_tile + c * 32);
-                        } else {
-                            if (raw) scan_chunk_raw<KP>(r, floor_adj, L, id_tile + c * 32);
-                            else scan_chunk<KP>(r, cb, p.alpha, floor_adj, L, id_tile + c * 32);
-                        }
+                        if (raw) buffer_chunk_raw(r, floor_adj, br, st, id_tile + c * 32);
+                        else buffer_chunk(r, cb, p.alpha, floor_adj, br, st, id_tile + c * 32);
                     }
                 } else {
+                    // list mode, 2 warps per SMSP: the next chunk's TMEM load is in
+                    // flight while a chunk is scored
                     uint32_t ra[32], rb[32];
                     float4 cb[8];
                     __syncwarp();
                     tc_fence_after();
                     tmem_ld_32x32b_x32(taddr, ra);
-    #pragma unroll 1
+#pragma unroll 1
                     for (int c = 0; c < kCols / 32; c += 2) {
                         if (!raw) load_bias_shared(cb, cb_tile + c * 32);
                         tmem_wait_ld_regs(ra);
                         __syncwarp();
                         tmem_ld_32x32b_x32(taddr + (c + 1) * 32, rb);
-                        if constexpr (kBuf) {
-                            if (raw) buffer_chunk_raw(ra, floor_adj, br, st, id_tile + c * 32);
-                            else buffer_chunk(ra, cb, p.alpha, floor_adj, br, st, id_tile + c * 32);
-                        } else {
-                            if (raw) scan_chunk_raw<KP>(ra, floor_adj, L, id_tile + c * 32);
-                            else scan_chunk<KP>(ra, cb, p.alpha, floor_adj, L, id_tile + c * 32);
-                        }
+                        if (raw) scan_chunk_raw<KP>(ra, floor_adj, L, id_tile + c * 32);
+                        else scan_chunk<KP>(ra, cb, p.alpha, floor_adj, L, id_tile + c * 32);
                         if (!raw) load_bias_shared(cb, cb_tile + (c + 1) * 32);
                         tmem_wait_ld_regs(rb);
                         if (c + 2 < kCols / 32) {
@@ -343,13 +336,8 @@ screen_f16_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
                         } else {
                             release_acc(b);
                         }
-                        if constexpr (kBuf) {
-                            if (raw) buffer_chunk_raw(rb, floor_adj, br, st, id_tile + (c + 1) * 32);
-                            else buffer_chunk(rb, cb, p.alpha, floor_adj, br, st, id_tile + (c + 1) * 32);
-                        } else {
-                            if (raw) scan_chunk_raw<KP>(rb, floor_adj, L, id_tile + (c + 1) * 32);
-                            else scan_chunk<KP>(rb, cb, p.alpha, floor_adj, L, id_tile + (c + 1) * 32);
-                        }
+                        if (raw) scan_chunk_raw<KP>(rb, floor_adj, L, id_tile + (c + 1) * 32);
+                        else scan_chunk<KP>(rb, cb, p.alpha, floor_adj, L, id_tile + (c + 1) * 32);
                     }
                 }
             }
