@@ -24,7 +24,8 @@ np.random.default_rng([seed, 10**7]).
 Timing: `value` = Q*K / max-over-ranks device time (queries already in HBM;
 device-pointer C-ABI call on torch's stream, CUDA events); `e2e` = the same
 through the host-pointer C-ABI call mflat_flat_search (pinned host queries in,
-results out, copies inside the timed region).  N > 1 runs under torchrun: rank
+results out into pinned buffers reused across steps, copies inside the timed
+region).  N > 1 runs under torchrun: rank
 r holds rows [r*N/P, (r+1)*N/P), the library all-gathers the per-rank top-k
 over NCCL and merges on the device.  --impl reference times the CPU baseline
 (oracle/cpu_baseline.py: multithreaded BLAS sgemm + partial top-k with the
@@ -381,9 +382,13 @@ def main():
                "d2h_bytes_per_step": int(out.nbytes)}
     else:
         qp = torch.from_numpy(qh).pin_memory().numpy()
+        # result buffers: page-locked and reused across steps, as a serving
+        # caller would hold them (the C ABI writes into caller-owned buffers)
+        ids_p = torch.empty(wl.nq * wl.k, dtype=torch.int32, pin_memory=True).numpy()
+        dist_p = torch.empty(wl.nq * wl.k, dtype=torch.float32, pin_memory=True).numpy()
         t0 = time.perf_counter()
         for _ in range(args.steps):
-            ids_h, dist_h = idx.search(qp, wl.k)
+            ids_h, dist_h = idx.search(qp, wl.k, out=(ids_p, dist_p))
         barrier()
         e2e_s = max_over_ranks(time.perf_counter() - t0)
         e2e = {"value": wl.nq * args.steps / e2e_s, "unit": unit,

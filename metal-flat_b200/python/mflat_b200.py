@@ -221,12 +221,30 @@ class FlatIndex:
     def reset(self) -> None:
         _check(self._lib.mflat_flat_reset(self._h), "reset")
 
-    def search(self, queries, k: int):
+    def search(self, queries, k: int, out=None):
+        """Top-k rows of each query: (ids, dist), each m x k_used (nearest first).
+
+        out: optional (ids, dist) pair of caller-owned, writeable, C-contiguous
+        int32 / float32 arrays with room for m * k entries (the C ABI's output
+        contract).  The results are written there and views of them returned,
+        so a caller can reuse (for example page-locked) buffers across calls.
+        """
         q = _f32(queries)
         m = q.shape[0]
         cap = max(1, m * max(1, k))
-        ids = np.empty(cap, np.int32)
-        dist = np.empty(cap, np.float32)
+        if out is None:
+            ids = np.empty(cap, np.int32)
+            dist = np.empty(cap, np.float32)
+        else:
+            ids, dist = out
+            for a, dt, name in ((ids, np.int32, "ids"), (dist, np.float32, "dist")):
+                if (not isinstance(a, np.ndarray) or a.dtype != dt or not a.flags.c_contiguous
+                        or not a.flags.writeable):
+                    raise ValueError(f"out {name}: a writeable C-contiguous {np.dtype(dt).name} "
+                                     "array is required")
+                if a.size < cap:
+                    raise ValueError(f"out {name}: {a.size} entries, the search needs {cap}")
+            ids, dist = ids.reshape(-1), dist.reshape(-1)
         used = ctypes.c_int(0)
         _check(self._lib.mflat_flat_search(self._h, _ptr(q, ctypes.c_float), m, k,
                                            _ptr(ids, ctypes.c_int32), _ptr(dist, ctypes.c_float),
