@@ -122,6 +122,14 @@ SearchResult FlatIndex::search(const float* queries, int m, int k) {
     return out;
 }
 
+int FlatIndex::searchInto(const float* queries, int m, int k, int32_t* ids, float* distances) {
+    if (m <= 0 || mImpl->dim <= 0) return 0;
+    k = mImpl->clampK(k);
+    raise_status(mflat_cu_index_search(mImpl->need(), queries, m, k, ids, distances, 0, nullptr),
+                 "search");
+    return k;
+}
+
 int FlatIndex::searchDevice(const float* d_queries, int m, int k, int32_t* d_ids, float* d_dist,
                             void* stream) {
     if (m <= 0 || mImpl->dim <= 0) return 0;

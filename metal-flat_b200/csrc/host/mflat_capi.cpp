@@ -206,6 +206,11 @@ MFLAT_API mflat_status_t mflat_flat_search(mflat_flat_index_t* h, const float* q
     if (m < 0 || k < 1) return MFLAT_ERR_BAD_ARG;
     return guarded([&] {
         std::lock_guard<std::mutex> lk(h->mu);
+        if (oi && od) {      // both outputs given: the results go straight into them
+            const int used = h->idx.searchInto(q, m, k, oi, od);
+            if (ok) *ok = used;
+            return MFLAT_OK;
+        }
         return emit(h->idx.search(q, m, k), m, oi, od, ok);
     });
 }

@@ -23,11 +23,12 @@
 #include <memory>
 #include <vector>
 
+#include "metalflat/Export.h"
 #include "metalflat/FlatIndex.h"
 
 namespace mflat {
 
-class CoarseQuantizer {
+class MFLAT_CXX_API CoarseQuantizer {
 public:
     enum class KmeansBackend { Auto, ForceGpuAssign };
 
@@ -79,6 +80,6 @@ private:
 // The seed permutation of the k-means training: 0..n-1 shuffled by a
 // front-to-back Fisher-Yates pass whose swap offsets are drawn from `rng` by
 // bitmask rejection (exposed for tests).
-void kmeansSeedPermutation(int n, uint32_t seed, std::vector<int>& perm);
+MFLAT_CXX_API void kmeansSeedPermutation(int n, uint32_t seed, std::vector<int>& perm);
 
 }  // namespace mflat

@@ -17,6 +17,7 @@
 #include <stdexcept>
 #include <vector>
 
+#include "metalflat/Export.h"
 #include "metalflat/Metric.h"
 
 namespace mflat {
@@ -33,7 +34,7 @@ struct SearchResult {
 enum class Storage { FP32 = 0, FP16 = 1, BF16 = 2 };
 
 // Thrown when the CUDA device (or NCCL) fails or is absent.
-class DeviceError : public std::runtime_error {
+class MFLAT_CXX_API DeviceError : public std::runtime_error {
 public:
     using std::runtime_error::runtime_error;
 };
@@ -43,7 +44,7 @@ struct SearchTiming {
     int screen_launches = 0, launches = 0, fallback_queries = 0;
 };
 
-class FlatIndex {
+class MFLAT_CXX_API FlatIndex {
 public:
     static constexpr int kMaxK = 1024;
 
@@ -66,6 +67,10 @@ public:
     // ---- additive ----
     Storage storage() const;
     int     device() const;
+    // As search, into caller-owned host buffers holding >= m * k entries
+    // (page-locked ones are filled by DMA); results are nearest-first at row
+    // stride k_used, the return value.  m <= 0 returns 0 and writes nothing.
+    int  searchInto(const float* queries, int m, int k, int32_t* ids, float* distances);
     void addDevice(const float* d_vectors, int n, void* stream);
     // Device pointers; enqueues on `stream`; returns the k actually used
     // (outputs are written at that row stride).
@@ -102,11 +107,11 @@ private:
 
 // Header of a file written by FlatIndex::save; false when the file cannot be
 // read or is not a flat index file.
-bool readFlatFileInfo(const char* path, int& dim, Metric& metric, Storage& storage, int& n);
+MFLAT_CXX_API bool readFlatFileInfo(const char* path, int& dim, Metric& metric, Storage& storage, int& n);
 
 // k-means assignment step: out[i] = argmin_c sqL2_f32(points[i], centroids[c])
 // with the reference's fp32 sequential sqL2 and lowest-index tie rule.
-void kmeansAssign(const float* points, int n, const float* centroids, int ncentroids, int dim,
+MFLAT_CXX_API void kmeansAssign(const float* points, int n, const float* centroids, int ncentroids, int dim,
                   int32_t* out, int device = -1);
 
 }  // namespace mflat

@@ -7,14 +7,16 @@
 // Handlers run synchronously on the logging thread and must not throw.
 #pragma once
 
+#include "metalflat/Export.h"
+
 namespace mflat {
 
 enum class LogLevel : int { Info = 0, Warn = 1, Error = 2, Off = 3 };
 
 using LogHandler = void (*)(LogLevel level, const char* msg, void* user);
 
-void     setLogHandler(LogHandler handler, void* user = nullptr);
-void     setLogLevel(LogLevel threshold);
-LogLevel logLevel();
+MFLAT_CXX_API void     setLogHandler(LogHandler handler, void* user = nullptr);
+MFLAT_CXX_API void     setLogLevel(LogLevel threshold);
+MFLAT_CXX_API LogLevel logLevel();
 
 }  // namespace mflat
