@@ -141,9 +141,22 @@ def comm_unique_id() -> bytes:
     return buf.raw
 
 
-def kmeans_assign(points, centroids, device: int = -1) -> np.ndarray:
+def _out_array(a, n: int, dt, name: str) -> np.ndarray:
+    """A caller-owned result buffer: writeable, C-contiguous, dtype dt, >= n entries."""
+    if (not isinstance(a, np.ndarray) or a.dtype != dt or not a.flags.c_contiguous
+            or not a.flags.writeable):
+        raise ValueError(f"out {name}: a writeable C-contiguous {np.dtype(dt).name} array is required")
+    if a.size < n:
+        raise ValueError(f"out {name}: {a.size} entries, the call needs {n}")
+    return a.reshape(-1)
+
+
+def kmeans_assign(points, centroids, device: int = -1, out=None) -> np.ndarray:
+    """Nearest centroid of each point (bit-exact fp32 sqL2, lowest index on
+    ties).  out: optional caller-owned int32 buffer of >= n entries."""
     p, c = _f32(points), _f32(centroids)
-    out = np.empty(p.shape[0], np.int32)
+    out = (np.empty(p.shape[0], np.int32) if out is None
+           else _out_array(out, p.shape[0], np.int32, "assign")[: p.shape[0]])
     _check(lib().mflat_kmeans_assign(_ptr(p, ctypes.c_float), p.shape[0], _ptr(c, ctypes.c_float),
                                      c.shape[0], p.shape[1], _ptr(out, ctypes.c_int32), device),
            "kmeans_assign")
@@ -236,15 +249,8 @@ class FlatIndex:
             ids = np.empty(cap, np.int32)
             dist = np.empty(cap, np.float32)
         else:
-            ids, dist = out
-            for a, dt, name in ((ids, np.int32, "ids"), (dist, np.float32, "dist")):
-                if (not isinstance(a, np.ndarray) or a.dtype != dt or not a.flags.c_contiguous
-                        or not a.flags.writeable):
-                    raise ValueError(f"out {name}: a writeable C-contiguous {np.dtype(dt).name} "
-                                     "array is required")
-                if a.size < cap:
-                    raise ValueError(f"out {name}: {a.size} entries, the search needs {cap}")
-            ids, dist = ids.reshape(-1), dist.reshape(-1)
+            ids = _out_array(out[0], cap, np.int32, "ids")
+            dist = _out_array(out[1], cap, np.float32, "dist")
         used = ctypes.c_int(0)
         _check(self._lib.mflat_flat_search(self._h, _ptr(q, ctypes.c_float), m, k,
                                            _ptr(ids, ctypes.c_int32), _ptr(dist, ctypes.c_float),

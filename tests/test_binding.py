@@ -100,3 +100,28 @@ def test_search_rejects_read_only_buffers():
     out_i.flags.writeable = False
     with pytest.raises(ValueError):
         idx.search(np.zeros((5, 4), np.float32), 10, out=(out_i, np.empty(50, np.float32)))
+
+
+class FakeKmeansLib:
+    """mflat_kmeans_assign stand-in: point i -> centroid i % c."""
+
+    def mflat_kmeans_assign(self, p, n, c, nc, dim, out, device):
+        for i in range(n):
+            out[i] = i % nc
+        return 0
+
+
+def test_kmeans_assign_into_caller_buffer(monkeypatch):
+    monkeypatch.setattr(M, "lib", lambda: FakeKmeansLib())
+    pts = np.zeros((10, 3), np.float32)
+    cen = np.zeros((4, 3), np.float32)
+    got = M.kmeans_assign(pts, cen)
+    assert np.array_equal(got, np.arange(10) % 4)
+    buf = np.full(16, -1, np.int32)
+    got = M.kmeans_assign(pts, cen, out=buf)
+    assert got.shape == (10,) and np.shares_memory(got, buf)
+    assert np.array_equal(buf[:10], np.arange(10) % 4) and np.all(buf[10:] == -1)
+    with pytest.raises(ValueError):
+        M.kmeans_assign(pts, cen, out=np.empty(9, np.int32))
+    with pytest.raises(ValueError):
+        M.kmeans_assign(pts, cen, out=np.empty(10, np.int64))
