@@ -165,7 +165,7 @@ def exact_ids_match(got_ids, got_dist, ref_ids, ref_dist, rel=1e-6):
     """North-star id criterion: returned ids must equal the oracle's except
     where the oracle's adjacent distances differ by less than `rel` relative
     (inside such a near-tie run the order is not pinned).  `ref_ids` /
-    `ref_dist` may carry extra columns past k (pass k+1 to also judge the
+    `ref_dist` may carry extra columns past k (pass k+1 to also check the
     boundary).  Returns the number of positions j < k whose id differs and is
     not explained by a near-tie with a neighbouring oracle position."""
     got_ids = np.asarray(got_ids)
