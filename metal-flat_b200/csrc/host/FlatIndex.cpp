@@ -171,7 +171,7 @@ void FlatIndex::setShard(int rank, int world, const uint8_t* comm_id, int64_t id
 
 namespace {
 
-constexpr int32_t kFlatMagic = 0x4d46464c;   // 'MFFL'
+constexpr int32_t kFlatMagic = 0x4c46464d;   // the bytes "MFFL" at the start of the file (little-endian)
 constexpr int32_t kFlatVersion = 1;
 constexpr size_t kIoChunkBytes = size_t(64) << 20;
 

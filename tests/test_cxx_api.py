@@ -39,8 +39,8 @@ def probe(tmp_path_factory):
     return run
 
 
-def header(magic=0x4D46464C, version=1, dim=96, metric=1, storage=2, n=12345):
-    return struct.pack("<8i", magic, version, dim, metric, storage, n, 0, 0)
+def header(magic=b"MFFL", version=1, dim=96, metric=1, storage=2, n=12345):
+    return magic + struct.pack("<7i", version, dim, metric, storage, n, 0, 0)
 
 
 def test_cxx_api_links_and_fails_loudly_without_device(probe, tmp_path):
@@ -55,7 +55,7 @@ def test_cxx_api_links_and_fails_loudly_without_device(probe, tmp_path):
 
 
 @pytest.mark.parametrize("blob", [
-    header(magic=0x12345678), header(version=2), header(dim=0), header(metric=3),
+    header(magic=b"LFFM"), header(magic=b"\0\0\0\0"), header(version=2), header(dim=0), header(metric=3),
     header(storage=5), header(n=-1), b"MF",
 ])
 def test_header_reader_rejects_bad_files(probe, tmp_path, blob):

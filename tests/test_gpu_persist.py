@@ -25,8 +25,10 @@ def test_save_load_roundtrip(tmp_path, storage, metric):
     idx.add(b)
     path = str(tmp_path / f"flat_{storage}_{metric}.mffl")
     idx.save(path)
+    with open(path, "rb") as f:
+        assert f.read(4) == b"MFFL"
     hdr = np.fromfile(path, np.int32, count=8)
-    assert list(hdr) == [0x4d46464c, 1, dim, M.METRICS[metric], M.STORAGES[storage], 4500, 0, 0]
+    assert list(hdr[1:]) == [1, dim, M.METRICS[metric], M.STORAGES[storage], 4500, 0, 0]
     elem = 4 if storage == "fp32" else 2
     assert (tmp_path / f"flat_{storage}_{metric}.mffl").stat().st_size == 32 + 4500 * dim * elem
     back = M.FlatIndex.load(path)
