@@ -148,13 +148,12 @@ def test_persistence_argument_checks_without_device(built_lib, tmp_path):
     bad.write_bytes(b"not an index file at all, 32+ bytes long.......")
     assert L.mflat_flat_load(str(bad).encode(), -1, ctypes.byref(st)) is None and st.value == 7
     # right magic, unsupported version
-    hdr = np.array([0x4d46464c, 9, 4, 0, 0, 0, 0, 0], np.int32)
     ver = tmp_path / "ver.mffl"
-    ver.write_bytes(hdr.tobytes())
+    ver.write_bytes(b"MFFL" + np.array([9, 4, 0, 0, 0, 0, 0], np.int32).tobytes())
     assert L.mflat_flat_load(str(ver).encode(), -1, ctypes.byref(st)) is None and st.value == 7
     # a valid header without a device: the handle cannot be made ready
     ok = tmp_path / "ok.mffl"
-    ok.write_bytes(np.array([0x4d46464c, 1, 4, 0, 0, 0, 0, 0], np.int32).tobytes())
+    ok.write_bytes(b"MFFL" + np.array([1, 4, 0, 0, 0, 0, 0], np.int32).tobytes())
     h = L.mflat_flat_load(str(ok).encode(), -1, ctypes.byref(st))
     if has_gpu():
         assert h and st.value == 0
