@@ -89,9 +89,9 @@ public:
     void setShard(int rank, int world, const uint8_t* comm_id, int64_t id_base);
 
     // Persistence (in the style of the reference's GraphIndex::save / load,
-    // src/GraphIndex.mm:424-452).  File: int32 header {'MFFL', version 1, dim,
-    // metric, storage, n, 0, 0}, then n x dim stored elements (fp32, or the
-    // fp16 / bf16 bit patterns).  save() returns false on an I/O failure.
+    // src/GraphIndex.mm:424-452).  File: a 32-byte header (the bytes "MFFL",
+    // then int32 version 1, dim, metric, storage, n, 0, 0), then n x dim stored
+    // elements (fp32, or the fp16 / bf16 bit patterns).  save() returns false on an I/O failure.
     // load() replaces this index's rows; it returns false (index unchanged)
     // when the file is unreadable or its dim / metric / storage differ.
     bool save(const char* path) const;
