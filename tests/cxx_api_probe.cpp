@@ -4,6 +4,7 @@
 // boundary, and the host-side pieces (log level, index-file header,
 // k-means seed permutation) behave as specified.  argv[1]: an index file.
 #include <cstdio>
+#include <stdexcept>
 #include <vector>
 
 #include "metalflat/CoarseQuantizer.h"
@@ -40,6 +41,28 @@ int main(int argc, char** argv) {
     const bool ok = argc > 1 && mflat::readFlatFileInfo(argv[1], dim, metric, storage, n);
     std::printf("info %d %d %d %d %d\n", ok ? 1 : 0, dim, static_cast<int>(metric),
                 static_cast<int>(storage), n);
+
+    try {
+        mflat::CoarseQuantizer bad(0);
+        std::printf("coarse_dim0 constructed\n");
+    } catch (const std::invalid_argument&) {
+        std::printf("coarse_dim0 invalid_argument\n");
+    }
+    mflat::CoarseQuantizer cq(8);
+    std::printf("coarse %d %d %d\n", cq.dim(), cq.nlist(), cq.size());
+    try {
+        cq.setShard(2, 2, nullptr, nullptr);
+        std::printf("coarse_shard accepted\n");
+    } catch (const std::invalid_argument&) {
+        std::printf("coarse_shard invalid_argument\n");
+    }
+    std::vector<float> pts(8 * 64, 0.5f);
+    try {
+        cq.train(pts.data(), 64, 4, 2);
+        std::printf("coarse_train returned\n");
+    } catch (const mflat::DeviceError&) {
+        std::printf("coarse_train DeviceError\n");
+    }
 
     std::vector<int> perm;
     mflat::kmeansSeedPermutation(37, 12345u, perm);

@@ -52,6 +52,10 @@ def test_cxx_api_links_and_fails_loudly_without_device(probe, tmp_path):
     assert r["search"] == ["DeviceError"] and r["searchInto"] == ["DeviceError"]
     assert r["empty"] == ["0"]                           # m = 0: nothing to do, no device needed
     assert r["info"] == ["1", "96", "1", "2", "12345"]
+    assert r["coarse_dim0"] == ["invalid_argument"]
+    assert r["coarse"] == ["8", "0", "0"]
+    assert r["coarse_shard"] == ["invalid_argument"]
+    assert r["coarse_train"] == ["DeviceError"]
 
 
 @pytest.mark.parametrize("blob", [
