@@ -22,15 +22,27 @@ np.random.default_rng([seed, 10**6]), mixture centres from
 np.random.default_rng([seed, 10**7]).
 
 Timing: `value` = Q*K / max-over-ranks device time (queries already in HBM;
-device-pointer C-ABI call on torch's stream, CUDA events); `e2e` = the same
-through the host-pointer C-ABI call mflat_flat_search (pinned host queries in,
-results out into pinned buffers reused across steps, copies inside the timed
-region).  N > 1 runs under torchrun: rank
-r holds rows [r*N/P, (r+1)*N/P), the library all-gathers the per-rank top-k
-over NCCL and merges on the device.  --impl reference times the CPU baseline
-(oracle/cpu_baseline.py: multithreaded BLAS sgemm + partial top-k with the
-reference's semantics; the reference's own search runs only on Apple Metal)
-on a bounded query sample of the same workload.
+device-pointer C-ABI call on torch's stream, CUDA events; the library's
+per-search timing events are only recorded during the loop and read after it,
+so nothing waits on the host between steps); `e2e` = the same through the
+host-pointer C-ABI call mflat_flat_search (pinned host queries in, results out
+into pinned buffers reused across steps, copies inside the timed region).
+N > 1 runs under torchrun: rank r holds rows [r*N/P, (r+1)*N/P), the library
+all-gathers the per-rank top-k over NCCL and merges on the device.
+
+Parity (outside the timed region): a subsample of the queries (config 4: of
+the points) is checked against the exact oracle (oracle/scale.py: fp64 top-k,
+ties to the lowest id; sequential-fp32 k-means argmin), which each rank feeds
+with the rows it ingests; rank 0 merges the ranks' oracle pools and compares
+with the search's own result, so every multi-GPU run also checks the NCCL
+merge.  The line carries "parity": ids that differ outside 1e-6 relative
+near-ties and the largest relative distance error (fp32 configs), recall@k
+(16-bit configs), or mismatched assignments (config 4).
+
+--impl reference times the CPU baseline (oracle/cpu_baseline.py: a
+multithreaded BLAS sgemm + top-k brute force with the reference's semantics;
+the reference's own search runs only on Apple Metal) on a sample of the same
+workload's queries against the full database, on rank 0.
 """
 from __future__ import annotations
 
@@ -100,15 +112,35 @@ class Workload:
             x /= np.linalg.norm(x, axis=1, keepdims=True)
         return x.astype(np.float32, copy=False)
 
+    def _block(self, b):
+        return self._draw(np.random.default_rng([self.cfg["seed"], b]), BLOCK)
+
+    def blocks(self, lo, hi, threads=None):
+        """Yield (row0, rows) covering [lo, hi) in order, in pieces of at most
+        BLOCK rows; the generator blocks are drawn on a thread pool ahead of
+        the consumer (numpy's generators release the GIL)."""
+        from concurrent.futures import ThreadPoolExecutor
+        b0, b1 = lo // BLOCK, (hi + BLOCK - 1) // BLOCK
+        threads = threads or min(16, os.cpu_count() or 1)
+        if hi <= lo:
+            return
+        self.centres() if self.cfg["dist"] == "mixture" else None
+        with ThreadPoolExecutor(threads) as ex:
+            futs = {}
+            nxt = b0
+            for b in range(b0, b1):
+                while nxt < b1 and nxt < b + threads:
+                    futs[nxt] = ex.submit(self._block, nxt)
+                    nxt += 1
+                blk = futs.pop(b).result()
+                a0, a1 = max(lo, b * BLOCK), min(hi, (b + 1) * BLOCK)
+                yield a0, blk[a0 - b * BLOCK:a1 - b * BLOCK]
+
     def rows(self, lo, hi):
         """Database rows (or k-means points) [lo, hi)."""
-        out = np.empty((hi - lo, self.dim), np.float32)
-        b = lo // BLOCK
-        while b * BLOCK < hi:
-            blk = self._draw(np.random.default_rng([self.cfg["seed"], b]), BLOCK)
-            a0, a1 = max(lo, b * BLOCK), min(hi, (b + 1) * BLOCK)
-            out[a0 - lo:a1 - lo] = blk[a0 - b * BLOCK:a1 - b * BLOCK]
-            b += 1
+        out = np.empty((max(0, hi - lo), self.dim), np.float32)
+        for a0, r in self.blocks(lo, hi):
+            out[a0 - lo:a0 - lo + r.shape[0]] = r
         return out
 
     def queries(self):
@@ -183,12 +215,15 @@ def measured_peaks():
     return 1590.0, 6650.0, "fallback"
 
 
-def profiled_traffic(cfg_id):
-    """Per-launch DRAM bytes of the screen kernel from a committed ncu summary."""
+def profiled_traffic(cfg_id, kernel):
+    """Per-launch DRAM bytes of `kernel` on this config from a committed ncu
+    summary (None when no capture of this kernel exists)."""
     path = os.path.join(ROOT, "profiles", f"screen_traffic_c{cfg_id}.json")
     if os.path.exists(path):
         with open(path) as f:
-            return json.load(f).get("dram_bytes_per_launch")
+            d = json.load(f)
+        if d.get("kernel") == kernel:
+            return d.get("dram_bytes_per_launch")
     return None
 
 
@@ -205,58 +240,192 @@ def config_dict(wl, cfg_id, world):
             "queries": wl.nq, "k": wl.k, "metric": c["metric"], "storage": c["storage"],
             "global_batch": wl.nq if not c.get("kmeans") else wl.n,
             "l2_flush": "inputs larger than L2 (database >= 51 MB streamed per step; "
-                        "config 3: 10.24 GB hi/lo planes)" if wl.n * wl.dim * 4 > 126e6
+                        "config 3: 10.24 GB of screen planes)" if wl.n * wl.dim * 4 > 126e6
                         else "database fits L2 (config 1: 51 MB); no flush between steps",
             "parallelism": (f"row-shard x{world} + NCCL all-gather merge" if world > 1 else "1 GPU")
             if not c.get("kmeans") else (f"point-shard x{world}, no collective" if world > 1 else "1 GPU")}
 
 
-def cpu_metric(c):
-    from_metric = {"l2": 0, "ip": 1}
-    return from_metric[c["metric"]]
+ORACLE_METRIC = {"l2": 0, "ip": 1, "cosine": 2}
+CPU_SAMPLE = {1: 1000, 2: 1000, 3: 1000, 4: 16384, 5: 256}   # queries (config 4: points)
+PARITY_SAMPLE = {1: 1000, 2: 256, 3: 256, 4: 100, 5: 256}    # config 4: every 100th point
 
 
-def cpu_baseline_run(wl, sample, repeats=1):
-    """Time the CPU port on `sample` queries (or k-means points) against the full data."""
+def cpu_baseline_run(wl, sample, warm=0):
+    """Time the CPU brute force (all host threads) on `sample` queries (config 4:
+    points) against the full database (centroid set).  Only the search itself
+    is timed: the database blocks are generated (or drawn from memory) between
+    the timed pieces.  Returns (seconds, algorithmic GFLOP)."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import cpu_baseline as B
     c = wl.cfg
-    db = wl.rows(0, wl.n) if not c.get("kmeans") else wl.queries()
-    q = wl.queries()[:sample] if not c.get("kmeans") else wl.rows(0, sample)
-    metric = cpu_metric(c)
-    dn = np.einsum("ij,ij->i", db, db, dtype=np.float64).astype(np.float32) if metric == 0 else None
-    B.search(db, q[:max(1, sample // 8)], wl.k, metric, dnorm=dn)
-    times = []
-    for _ in range(repeats):
+    if c.get("kmeans"):
+        cents = wl.queries()
+        pts = wl.rows(0, sample)
+        if warm:
+            B.kmeans_assign(pts[:warm], cents)
         t0 = time.perf_counter()
-        B.search(db, q, wl.k, metric, dnorm=dn)
-        times.append(time.perf_counter() - t0)
-    return times
+        B.kmeans_assign(pts, cents)
+        dt = time.perf_counter() - t0
+        return dt, 2.0 * sample * cents.shape[0] * wl.dim / 1e9
+    metric = ORACLE_METRIC[c["metric"]]
+    q = wl.queries()[:sample]
+    if metric == 2:
+        import oracle as O
+        q = O.normalize_rows(q)
+    topk = B.TopK(q, wl.k, 0 if metric == 0 else 1)
+    dt = 0.0
+    for a0, rows in wl.blocks(0, wl.n):
+        if metric == 2:
+            rows = O.normalize_rows(rows)
+        if warm and a0 == 0:
+            B.TopK(q[:warm], wl.k, 0 if metric == 0 else 1).add(rows[:65536], 0)
+        for j in range(0, rows.shape[0], 65536):
+            t0 = time.perf_counter()
+            topk.add(rows[j:j + 65536], a0 + j)
+            dt += time.perf_counter() - t0
+    t0 = time.perf_counter()
+    topk.result()
+    dt += time.perf_counter() - t0
+    return dt, 2.0 * sample * wl.n * wl.dim / 1e9
+
+
+class ReferenceDB:
+    """The full database held once in host memory for the reference arm's
+    repeated steps (configs 1-4; config 5 streams its blocks instead)."""
+
+    def __init__(self, wl):
+        self.wl = wl
+        self.db = None if wl.n > 20_000_000 or wl.cfg.get("kmeans") else wl.rows(0, wl.n)
+
+    def step(self, sample, warm=False):
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import cpu_baseline as B
+        wl = self.wl
+        if self.db is None:
+            return cpu_baseline_run(wl, sample)
+        metric = ORACLE_METRIC[wl.cfg["metric"]]
+        q = wl.queries()[:sample]
+        db = self.db
+        if metric == 2:
+            import oracle as O
+            q, db = O.normalize_rows(q), O.normalize_rows(db)
+        t0 = time.perf_counter()
+        B.search(db, q, wl.k, 0 if metric == 0 else 1)
+        return time.perf_counter() - t0, 2.0 * sample * wl.n * wl.dim / 1e9
 
 
 def run_reference(args, wl, cfg_id, rank, world):
-    """CPU baseline arm: rank 0 only, a bounded query sample per step."""
+    """CPU baseline arm: rank 0 only, a sample of the queries per step."""
     if rank != 0:
         return
-    sample = args.ref_sample
-    times = cpu_baseline_run(wl, sample, repeats=args.steps + args.warmup)[args.warmup:]
+    sample = args.ref_sample or CPU_SAMPLE[cfg_id]
+    if not wl.cfg.get("kmeans"):
+        sample = min(sample, wl.nq)
+    ref = ReferenceDB(wl)
+    for _ in range(args.warmup):      # warm-up steps: a small sample (untimed)
+        ref.step(max(1, min(sample, 64)))
+    times, gflop = [], 0.0
+    for _ in range(args.steps):
+        t, g = ref.step(sample)
+        times.append(t)
+        gflop = g
     tot = sum(times)
     value = sample * len(times) / tot
     unit = "queries/s" if not wl.cfg.get("kmeans") else "points/s"
+    what = "points" if wl.cfg.get("kmeans") else "queries"
+    cores = os.cpu_count() or 1
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": unit,
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": 1000.0 * tot / len(times), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": f"synthetic (seed {wl.cfg['seed']})", "config": config_dict(wl, cfg_id, world),
-        "cpu_baseline": {"value": value, "unit": unit, "cores": os.cpu_count() or 1, "kind": "port",
-                         "sample": f"{sample} queries per step against the full database "
-                                   "(BLAS sgemm + partial top-k, all host threads)"},
+        "cpu_baseline": {"value": value, "unit": unit, "cores": cores, "kind": "port",
+                         "sample": f"{sample} {what} per step against the full "
+                                   f"{'centroid set' if wl.cfg.get('kmeans') else 'database'} "
+                                   "(BLAS sgemm + top-k, all host threads)",
+                         "gflops": gflop * len(times) / tot},
         "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "the reference's search path is Metal/MPS (Apple only): unavailable on this box; "
                 "the timed baseline is the CPU port of its semantics",
     }
     print(json.dumps(line), flush=True)
+
+
+class Parity:
+    """Oracle side of the parity check, fed with the rows this rank ingests."""
+
+    def __init__(self, wl, cfg_id, rank, world, lo, hi, enabled):
+        self.enabled = enabled
+        self.wl, self.cfg_id, self.rank, self.world = wl, cfg_id, rank, world
+        self.lo, self.hi = lo, hi
+        self.se = None
+        if not enabled:
+            return
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import scale as S
+        self.S = S
+        c = wl.cfg
+        if c.get("kmeans"):
+            self.stride = PARITY_SAMPLE[cfg_id]
+        else:
+            self.nchk = min(PARITY_SAMPLE[cfg_id], wl.nq)
+            self.se = S.StreamingExact(wl.queries()[:self.nchk], wl.k, ORACLE_METRIC[c["metric"]])
+
+    def feed(self, a0, rows):
+        if self.se is not None:
+            self.se.add(rows, a0)
+
+    def check_search(self, dist, got_ids, got_dist):
+        """Rank 0 compares got_* (first nchk queries) with the merged oracle."""
+        if not self.enabled:
+            return None
+        import oracle as O
+        pools = [self.se.pools()]
+        if self.world > 1:
+            gathered = [None] * self.world if self.rank == 0 else None
+            dist.gather_object(self.se.pools(), gathered, dst=0)
+            pools = gathered
+        if self.rank != 0:
+            return None
+        ref_i, ref_d = self.se.result(self.S.merge_pools(pools))
+        c = self.wl.cfg
+        out = {"checked": int(self.nchk), "oracle": "exact fp64 top-k over the fp32 rows "
+               "(oracle/scale.py: fp32 BLAS screen + proven margin + fp64 re-score)"}
+        if c["storage"] == "fp32":
+            bad = O.exact_ids_match(got_ids, got_dist, ref_i, ref_d, rel=1e-6)
+            fin = np.isfinite(ref_d)
+            rel = np.abs(got_dist[fin] - ref_d[fin]) / np.maximum(np.abs(ref_d[fin]), 1e-30)
+            out.update(bad_ids=int(bad), max_rel_dist_err=float(rel.max()) if rel.size else 0.0,
+                       criterion="ids equal outside 1e-6 relative near-ties; distances within 1e-5")
+            out["ok"] = bool(bad == 0 and out["max_rel_dist_err"] <= 1e-5)
+        else:
+            hits = sum(len(np.intersect1d(got_ids[i], ref_i[i][ref_i[i] >= 0]))
+                       for i in range(self.nchk))
+            total = int((ref_i >= 0).sum())
+            out.update(recall=hits / max(total, 1), criterion="recall@k >= 0.99")
+            out["ok"] = bool(out["recall"] >= 0.99)
+        return out
+
+    def check_kmeans(self, dist, pts, got):
+        """Every stride-th global point this rank holds; counts gathered to rank 0."""
+        if not self.enabled:
+            return None
+        first = (self.lo + self.stride - 1) // self.stride * self.stride
+        sel = np.arange(first, self.hi, self.stride) - self.lo
+        ref = self.S.kmeans_assign_screened(pts[sel], self.wl.queries())
+        counts = [int(sel.size), int((ref != got[sel]).sum())]
+        if self.world > 1:
+            t = __import__("torch").tensor(counts, dtype=__import__("torch").int64)
+            dist.all_reduce(t)
+            counts = [int(t[0]), int(t[1])]
+        if self.rank != 0:
+            return None
+        return {"checked": counts[0], "mismatched": counts[1], "ok": counts[1] == 0,
+                "oracle": "sequential fp32 sqL2 argmin, lowest index on ties "
+                          "(oracle/scale.py kmeans_assign_screened)",
+                "criterion": "assignments bit-exact"}
 
 
 def main():
@@ -266,8 +435,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="mflat", choices=["mflat", "reference"])
     ap.add_argument("--config", type=int, default=3, choices=sorted(CONFIGS))
-    ap.add_argument("--ref-sample", type=int, default=32)
+    ap.add_argument("--ref-sample", type=int, default=0,
+                    help="reference arm: queries (config 4: points) per step (default: per config)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-parity", action="store_true", help="skip the oracle check (profiling)")
     ap.add_argument("--n-db", type=int, default=None,
                     help="profiling only: smaller database (rows) for ncu captures")
     ap.add_argument("--n-q", type=int, default=None, help="profiling only: fewer queries")
@@ -294,6 +465,7 @@ def main():
     lo, hi = rank * wl.n // world, (rank + 1) * wl.n // world
     stream = torch.cuda.current_stream()
     sp = stream.cuda_stream
+    parity = Parity(wl, args.config, rank, world, lo, hi, not args.no_parity)
 
     def barrier():
         torch.cuda.synchronize()
@@ -324,8 +496,9 @@ def main():
         units_per_step, idx = wl.n, None
     else:
         idx = M.FlatIndex(wl.dim, c["metric"], c["storage"], device=local)
-        for a in range(lo, hi, BLOCK):
-            idx.add(wl.rows(a, min(hi, a + BLOCK)))
+        for a0, rows in wl.blocks(lo, hi):
+            idx.add(rows)
+            parity.feed(a0, rows)
         if world > 1:
             obj = [M.comm_unique_id() if rank == 0 else None]
             dist.broadcast_object_list(obj, src=0)
@@ -342,30 +515,38 @@ def main():
         step()
     barrier()
 
-    # ---- device-resident timed region (value) with live per-kernel timing
+    # ---- device-resident timed region (value).  The library's timing events
+    # are recorded per search and read after the loop (no host wait inside).
     if idx is not None:
         idx.set_timing(True)
-    screen_ms, total_ms, launches = [], [], 0
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
         barrier()
         ev0.record(stream)
         for _ in range(args.steps):
             step()
-            if idx is not None:
-                t = idx.last_timing()
-                screen_ms.append(t.screen_ms)
-                total_ms.append(t.total_ms)
-                launches += t.launches
-            else:
-                launches += 4
         ev1.record(stream)
         barrier()
-    if idx is not None:
-        idx.set_timing(False)
     dev_s = max_over_ranks(ev0.elapsed_time(ev1) / 1000.0)
     value = units_per_step * args.steps / dev_s
     unit = "queries/s" if not kmeans else "points/s"
+    if idx is not None:
+        tsum, n_timed = idx.timing_sum()
+        idx.set_timing(False)
+        launches = tsum.launches
+        screen_ms_mean = tsum.screen_ms / max(n_timed, 1)
+        total_ms_mean = tsum.total_ms / max(n_timed, 1)
+        fallback_queries = tsum.fallback_queries
+    else:
+        launches = 4 * args.steps
+        fallback_queries = None
+
+    # ---- parity of the timed search's own output (outside the timed region)
+    if kmeans:
+        par = parity.check_kmeans(dist, pts_h, d_out.cpu().numpy())
+    else:
+        nchk = parity.nchk if parity.enabled else 0
+        par = parity.check_search(dist, d_ids[:nchk].cpu().numpy(), d_dist[:nchk].cpu().numpy())
 
     # ---- end-to-end through the host-pointer C ABI (pinned host buffers)
     barrier()
@@ -402,6 +583,7 @@ def main():
     fp32 = c["storage"] == "fp32"
     passes = 3.0 if fp32 else 1.0
     peak = bf16_peak / 2.0 if fp32 else bf16_peak
+    kernel = "screen_tf32x3_kernel" if fp32 else "screen_f16_kernel"
     if kmeans:
         flops = passes * 2.0 * n_local * qh.shape[0] * wl.dim
         t_s = dev_s / args.steps
@@ -409,13 +591,14 @@ def main():
     else:
         flops = passes * 2.0 * wl.nq * n_local * wl.dim
         large = wl.k > (21 if fp32 else 16)
-        t_s = statistics.mean(total_ms if large else screen_ms) / 1000.0
+        t_s = (total_ms_mean if large else screen_ms_mean) / 1000.0
         what = ("whole search incl. floor pre-pass and select (large k)" if large
-                else "screen kernel alone") + ", CUDA events on the launching stream"
+                else "screen kernel alone") + (", CUDA events on the launching stream, "
+                                               f"mean over the {args.steps} timed searches")
     achieved = flops / t_s / 1e12
     roofline = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                "frac": achieved / peak, "traffic": profiled_traffic(args.config),
-                "kernel": "screen_tf32x3_kernel" if fp32 else "screen_f16_kernel",
+                "frac": achieved / peak, "traffic": profiled_traffic(args.config, kernel),
+                "kernel": kernel,
                 "note": (f"{'tf32-equivalent: 3 x ' if fp32 else ''}2*Q*N*d per launch "
                          f"(Q={wl.nq if not kmeans else n_local}, N={n_local if not kmeans else qh.shape[0]}, "
                          f"d={wl.dim}); peak = {src} bf16 dense{' / 2 (kind::tf32 rate)' if fp32 else ''}"
@@ -430,14 +613,19 @@ def main():
         "config": config_dict(wl, args.config, world), "roofline": roofline, "e2e": e2e,
         "gpu_launches": launches, "clocks": clk.summary(),
     }
+    if par is not None:
+        line["parity"] = par
+    if fallback_queries is not None:
+        line["fallback_queries"] = fallback_queries
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
-        sample = {1: 64, 2: 16, 3: 64, 4: 20000, 5: 4}[args.config]
-        t = cpu_baseline_run(wl, sample)[0]
+        sample = CPU_SAMPLE[args.config] if kmeans else min(CPU_SAMPLE[args.config], wl.nq)
+        t, gflop = cpu_baseline_run(wl, sample, warm=8)
         line["cpu_baseline"] = {
             "value": sample / t, "unit": unit, "cores": os.cpu_count() or 1, "kind": "port",
             "sample": f"{sample} {'points' if kmeans else 'queries'} against the full "
-                      f"{'centroid set' if kmeans else 'database'} (BLAS sgemm + partial top-k, "
-                      "all host threads), scaled to per-second"}
+                      f"{'centroid set' if kmeans else 'database'} (BLAS sgemm + top-k, "
+                      "all host threads), scaled to per-second",
+            "gflops": gflop / t}
     if rank == 0:
         print(json.dumps(line), flush=True)
     if idx is not None:

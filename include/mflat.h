@@ -149,7 +149,9 @@ MFLAT_API mflat_status_t mflat_flat_search_noalloc(mflat_flat_index_t*, const fl
         int m, int k, int32_t* d_out_ids, float* d_out_distances, int* out_k_used, void* stream);
 
 /* Device-side timing of the most recent search (milliseconds, CUDA events
- * on the launching stream) once enabled with mflat_flat_set_timing(h, 1). */
+ * on the launching stream) once enabled with mflat_flat_set_timing(h, 1).
+ * Searches only record their events; the times are read when asked for, so
+ * timing does not hold back a stream of asynchronous searches. */
 typedef struct {
     float total_ms;                 /* first to last kernel of the search          */
     float screen_ms;                /* tensor-core distance + fused top-k kernel   */
@@ -160,6 +162,10 @@ typedef struct {
 } mflat_timing_t;
 MFLAT_API mflat_status_t mflat_flat_set_timing(mflat_flat_index_t*, int enable);
 MFLAT_API mflat_status_t mflat_flat_last_timing(const mflat_flat_index_t*, mflat_timing_t* out);
+/* Additive (no counterpart in the reference): the field-wise sums over every
+ * search since timing was last enabled, and their number. */
+MFLAT_API mflat_status_t mflat_flat_timing_sum(const mflat_flat_index_t*, mflat_timing_t* out,
+                                               int* n_searches);
 
 /* k-means assignment step (CoarseQuantizer, reference src/Internal.h:321-359
  * and src/CoarseQuantizer.mm:122-130): out_assign[i] = argmin_c sqL2_f32(p_i, c)

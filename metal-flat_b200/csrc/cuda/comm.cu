@@ -20,9 +20,12 @@
 #include "index_impl.cuh"
 #include "kernels.cuh"
 #include "mflat_cuda.h"
+#include "ptx.cuh"
 
 namespace mflat_cu {
 namespace {
+
+constexpr int kMaxRanks = 256;
 
 struct NcclApi {
     bool ok = false;
@@ -71,43 +74,92 @@ int nccl_fail(const char* what, ncclResult_t r) {
     return fail(ST_DEVICE, buf);
 }
 
-// One thread per query: P-way merge of the gathered per-rank lists
-// ([P][m][k], each nearest-first, ids global) into [m][k].
+// P-way merge of the gathered per-rank lists ([P][m][k], each nearest-first,
+// ids global) into [m][k], one block per query, as a tree of two-way merges
+// in shared memory.  Entries become 64-bit keys whose unsigned order is the
+// result order (nearer first, then lower id; 0 = empty slot), so a merge is a
+// plain descending merge of distinct keys.  Each output position of a
+// two-way merge finds its split with a binary search along its diagonal (the
+// merge-path co-rank), so every thread works independently: log2(P) levels of
+// k outputs per pair.  Shared memory: 1.5 x (P rounded up to a power of two) x
+// k x 8 bytes.
+__device__ __forceinline__ uint64_t merge_key(float d, int32_t id, bool l2) {
+    if (id < 0) return 0ull;
+    return (static_cast<uint64_t>(score_key(l2 ? -d : d)) << 32) |
+           static_cast<uint32_t>(~static_cast<uint32_t>(id));
+}
+
+// Output t of the top-k of descending x and y (k keys each).
+__device__ __forceinline__ uint64_t merge_at(const uint64_t* x, const uint64_t* y, int k, int t) {
+    int lo = t > k ? t - k : 0;
+    int hi = t < k ? t : k;
+    while (lo < hi) {                 // first a with x[a] not ahead of y[t - 1 - a]
+        const int mid = (lo + hi) >> 1;
+        if (x[mid] > y[t - 1 - mid]) lo = mid + 1;
+        else hi = mid;
+    }
+    const uint64_t xa = lo < k ? x[lo] : 0ull;
+    const uint64_t yb = t - lo < k ? y[t - lo] : 0ull;
+    return xa > yb ? xa : yb;
+}
+
 __global__ void merge_ranks_kernel(const int32_t* __restrict__ gids, const float* __restrict__ gdist,
-                                   int world, int m, int k, int metric, int32_t* __restrict__ out_ids,
-                                   float* __restrict__ out_dist) {
-    const int qi = blockIdx.x * blockDim.x + threadIdx.x;
-    if (qi >= m) return;
-    int head[8];
-    for (int p = 0; p < world; ++p) head[p] = 0;
-    const float empty = metric == kL2 ? __int_as_float(0x7f800000) : -__int_as_float(0x7f800000);
-    for (int j = 0; j < k; ++j) {
-        int bp = -1;
-        int32_t bid = -1;
-        float bd = 0.0f;
-        for (int p = 0; p < world; ++p) {
-            if (head[p] >= k) continue;
-            const int64_t o = (static_cast<int64_t>(p) * m + qi) * k + head[p];
-            const int32_t id = gids[o];
-            if (id < 0) continue;
-            const float d = gdist[o];
-            bool take = bp < 0;
-            if (!take) {
-                if (d != bd) take = metric == kL2 ? (d < bd) : (d > bd);
-                else take = id < bid;
-            }
-            if (take) { bp = p; bid = id; bd = d; }
+                                   int world, int p2, int m, int k, int metric,
+                                   int32_t* __restrict__ out_ids, float* __restrict__ out_dist) {
+    extern __shared__ uint64_t sm_keys[];
+    const int qi = blockIdx.x;
+    const bool l2 = metric == kL2;
+    uint64_t* a = sm_keys;                                   // p2 lists
+    uint64_t* b = sm_keys + static_cast<size_t>(p2) * k;     // p2 / 2 lists
+    for (int e = threadIdx.x; e < p2 * k; e += blockDim.x) {
+        const int p = e / k;
+        uint64_t key = 0ull;
+        if (p < world) {
+            const int64_t o = (static_cast<int64_t>(p) * m + qi) * k + (e - p * k);
+            key = merge_key(gdist[o], gids[o], l2);
         }
-        const int64_t oo = static_cast<int64_t>(qi) * k + j;
-        if (bp < 0) {
-            out_ids[oo] = -1;
-            out_dist[oo] = empty;
+        a[e] = key;
+    }
+    __syncthreads();
+    for (int n = p2; n > 1; n >>= 1) {
+        const int outs = (n >> 1) * k;
+        for (int e = threadIdx.x; e < outs; e += blockDim.x) {
+            const int j = e / k;
+            const int t = e - j * k;
+            b[e] = merge_at(a + static_cast<size_t>(2 * j) * k, a + static_cast<size_t>(2 * j + 1) * k, k, t);
+        }
+        __syncthreads();
+        uint64_t* tmp = a;
+        a = b;
+        b = tmp;
+    }
+    const float empty = l2 ? __int_as_float(0x7f800000) : -__int_as_float(0x7f800000);
+    for (int t = threadIdx.x; t < k; t += blockDim.x) {
+        const uint64_t key = a[t];
+        const int64_t o = static_cast<int64_t>(qi) * k + t;
+        if (key == 0ull) {
+            out_ids[o] = -1;
+            out_dist[o] = empty;
         } else {
-            out_ids[oo] = bid;
-            out_dist[oo] = bd;
-            ++head[bp];
+            const uint32_t h = static_cast<uint32_t>(key >> 32);
+            const float s = __uint_as_float((h & 0x80000000u) ? (h & 0x7fffffffu) : ~h);
+            out_ids[o] = static_cast<int32_t>(~static_cast<uint32_t>(key));
+            out_dist[o] = l2 ? -s : s;
         }
     }
+}
+
+constexpr size_t kMergeSmemMax = 200u << 10;
+
+int merge_p2(int world) {
+    int p2 = 1;
+    while (p2 < world) p2 <<= 1;
+    return p2;
+}
+
+size_t merge_smem(int world, int k) {
+    const int p2 = merge_p2(world);
+    return static_cast<size_t>(p2) * k * 8 + static_cast<size_t>(p2 / 2) * k * 8;
 }
 
 }  // namespace
@@ -154,7 +206,9 @@ int wait_collective(mflat_cu_index* ix, cudaStream_t st) {
 
 int shard_merge(mflat_cu_index* ix, int m, int k_out, int32_t* ids, float* dist, cudaStream_t st) {
     if (!ix->comm || ix->world <= 1) return ST_OK;
-    if (ix->world > 8) return fail(ST_BAD_ARG, "at most 8 ranks");
+    if (merge_smem(ix->world, k_out) > kMergeSmemMax)
+        return fail(ST_BAD_ARG, "too many ranks for this k: the on-device merge holds 1.5 x ranks"
+                                " (rounded up to a power of two) x k x 8 bytes in 200 KB");
     const size_t cnt = static_cast<size_t>(m) * k_out;
     CU_TRY(ix->gather_ids.ensure(cnt * ix->world * sizeof(int32_t)), "gather buffer");
     CU_TRY(ix->gather_dist.ensure(cnt * ix->world * sizeof(float)), "gather buffer");
@@ -164,16 +218,41 @@ int shard_merge(mflat_cu_index* ix, int m, int k_out, int32_t* ids, float* dist,
     nccl().AllGather(ids, ix->gather_ids.p, cnt, ncclInt32, comm, st);
     nccl().AllGather(dist, ix->gather_dist.p, cnt, ncclFloat32, comm, st);
     if ((r = nccl().GroupEnd()) != ncclSuccess) return nccl_fail("all-gather", r);
-    merge_ranks_kernel<<<blocks_for(m, 128), 128, 0, st>>>(
-        ix->gather_ids.as<int32_t>(), ix->gather_dist.as<float>(), ix->world, m, k_out,
-        ix->metric == kL2 ? kL2 : kIP, ids, dist);
-    CU_TRY(cudaGetLastError(), "merge launch");
+    CU_TRY(launch_merge_ranks(ix->gather_ids.as<int32_t>(), ix->gather_dist.as<float>(), ix->world, m,
+                              k_out, ix->metric == kL2 ? kL2 : kIP, ids, dist, st),
+           "merge launch");
     return ST_OK;
+}
+
+cudaError_t launch_merge_ranks(const int32_t* gids, const float* gdist, int world, int m, int k,
+                               int metric, int32_t* out_ids, float* out_dist, cudaStream_t st) {
+    const size_t smem = merge_smem(world, k);
+    if (world < 1 || k < 1 || smem > kMergeSmemMax) return cudaErrorInvalidValue;
+    if (m == 0) return cudaSuccess;
+    cudaError_t e = cudaFuncSetAttribute(merge_ranks_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    const int p2 = merge_p2(world);
+    const int work = p2 * k;
+    const int threads = work >= 256 ? 256 : (work + 31) / 32 * 32;
+    merge_ranks_kernel<<<m, threads, smem, st>>>(gids, gdist, world, p2, m, k, metric, out_ids, out_dist);
+    return cudaGetLastError();
 }
 
 }  // namespace mflat_cu
 
 using namespace mflat_cu;
+
+extern "C" int mflat_cu_merge_ranks(const int32_t* d_gids, const float* d_gdist, int world, int m,
+                                    int k, int metric, int32_t* d_out_ids, float* d_out_dist,
+                                    void* stream) {
+    if (!d_gids || !d_gdist || !d_out_ids || !d_out_dist || world < 1 || m < 0 || k < 1)
+        return fail(ST_BAD_ARG, "bad argument");
+    CU_TRY(launch_merge_ranks(d_gids, d_gdist, world, m, k, metric == kL2 ? kL2 : kIP, d_out_ids,
+                              d_out_dist, static_cast<cudaStream_t>(stream)),
+           "merge launch");
+    return ST_OK;
+}
 
 extern "C" int mflat_cu_comm_unique_id(uint8_t* out_id) {
     if (!out_id) return fail(ST_BAD_ARG, "null argument");
@@ -195,7 +274,7 @@ extern "C" int mflat_cu_index_set_shard(mflat_cu_index_t* ix, int rank, int worl
     comm_release(ix);
     if (world == 1) return ST_OK;
     if (!comm_id) return fail(ST_BAD_ARG, "null communicator id");
-    if (world > 8) return fail(ST_BAD_ARG, "at most 8 ranks");
+    if (world > kMaxRanks) return fail(ST_BAD_ARG, "too many ranks");
     if (!nccl().ok) return fail(ST_DEVICE, "NCCL (libnccl.so.2) not available");
     ncclUniqueId id;
     std::memcpy(id.internal, comm_id, 128);

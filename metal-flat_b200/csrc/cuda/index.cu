@@ -410,11 +410,12 @@ void plan_screen_chunks(int n_qtiles, int n_tiles, int num_sms, int max_chunks, 
     plan_chunks(n_qtiles, n_tiles, num_sms, max_chunks, n_chunks, tiles_per_chunk);
 }
 
-int check_device_error(mflat_cu_index* ix) {
+int check_device_error(mflat_cu_index* ix, cudaStream_t st) {
     if (ix->host_words[0] != 0) {
         const int code = ix->host_words[0];
         ix->host_words[0] = 0;
-        cudaMemsetAsync(ix->err, 0, sizeof(int), ix->stream);
+        // cleared on the stream of the next kernels, ordered before them
+        cudaMemsetAsync(ix->err, 0, sizeof(int), st);
         char buf[128];
         std::snprintf(buf, sizeof buf, "device kernel reported error code %d (%s)", code,
                       code == kErrTimeout ? "bounded wait timed out" : "bad launch configuration");
@@ -696,7 +697,7 @@ int search_large(mflat_cu_index* ix, const float* queries, int m, int k_out, int
         ls.db_hi = ix->db_hi;
         ls.db_lo = ix->db_lo;
         ls.xmax_bits = ix->xmax_bits;
-        ls.gamma = static_cast<float>((3.0 * d_pad + 16.0) * std::ldexp(1.0, -21));
+        ls.gamma = screen_gamma(d_pad);
         ls.id_base = ix->world > 1 ? ix->id_base : 0;
         ls.out_ids = d_ids + static_cast<int64_t>(b0) * k_out;
         ls.out_dist = d_dist + static_cast<int64_t>(b0) * k_out;
@@ -732,10 +733,7 @@ int search_large(mflat_cu_index* ix, const float* queries, int m, int k_out, int
         overflows += ix->host_words[4];
         unproven += ix->host_words[5];
     }
-    if (ix->timing) {
-        cudaEventRecord(ix->ev[3], st);
-        cudaEventSynchronize(ix->ev[3]);
-    }
+    if (ix->timing) cudaEventRecord(ix->ev[3], st);
     // Overflows and unproven queries are rare; surface them as errors.
     if (overflows > 0) return fail(ST_INTERNAL, "candidate buffer overflow (too many rows tie with the k-th best)");
     if (unproven > 0) return fail(ST_INTERNAL, "exactness could not be proven for some queries (near-ties)");
@@ -914,10 +912,7 @@ int search_half(mflat_cu_index* ix, const float* queries, int m, int k_out, int3
         }
         overflows += ix->host_words[4];
     }
-    if (ix->timing) {
-        cudaEventRecord(ix->ev[3], st);
-        cudaEventSynchronize(ix->ev[3]);
-    }
+    if (ix->timing) cudaEventRecord(ix->ev[3], st);
     ix->last.screen_launches = 1 + redone;
     ix->last.launches = list_mode ? 3 : (P.prepass ? (P.two_stage ? 7 : 5) : 3);
     if (overflows > 0)
@@ -981,6 +976,110 @@ int index_add(mflat_cu_index_t* ix, const void* vectors, int64_t n, int on_devic
 }  // namespace mflat_cu
 
 // =====================================================================
+namespace mflat_cu {
+
+// fp32 storage, k <= 21: list-mode screen (top-32 per query and chunk), then
+// the merge + exactness proof + fp64 re-rank, and the exact full scan for the
+// (rare) queries whose proof fails.
+int search_list_exact(mflat_cu_index* ix, const float* queries, int m, int k_out, int32_t* d_ids,
+                      float* d_dist, int on_device, cudaStream_t st) {
+    const int kp = kp_for(k_out);
+    ScreenRun run;
+    int rc = run_screen(ix, queries, m, kp, on_device, st, run);
+    if (rc != ST_OK) return rc;
+    ix->last.screen_launches = 1;
+    CU_TRY(ix->flag_list.ensure(static_cast<size_t>(m) * sizeof(int)), "fallback list");
+    CU_TRY(cudaMemsetAsync(ix->flag_count, 0, sizeof(int), st), "fallback count");
+
+    SelectParams sel{};
+    sel.m = m;
+    sel.m_pad = run.m_pad;
+    sel.dim = ix->dim;
+    sel.d_pad = ix->d_pad;
+    sel.k_out = k_out;
+    sel.n_chunks = run.n_chunks;
+    sel.metric = ix->metric == kL2 ? kL2 : kIP;
+    sel.n = ix->n;
+    sel.part_score = run.part_s;
+    sel.part_id = run.part_i;
+    sel.q_hi = run.q_hi;
+    sel.q_lo = run.q_lo;
+    sel.qnorm = run.qnorm;
+    sel.db_hi = ix->db_hi;
+    sel.db_lo = ix->db_lo;
+    sel.xmax_bits = ix->xmax_bits;
+    sel.gamma = screen_gamma(ix->d_pad);
+    sel.id_base = ix->world > 1 ? ix->id_base : 0;
+    sel.out_ids = d_ids;
+    sel.out_dist = d_dist;
+    sel.flag_count = ix->flag_count;
+    sel.flag_list = ix->flag_list.as<int>();
+    sel.err = ix->err;
+    const size_t fb = static_cast<size_t>(m) * kFbChunks * k_out;
+    CU_TRY(ix->fb_s.ensure(fb * sizeof(double)), "fallback scratch");
+    CU_TRY(ix->fb_i.ensure(fb * sizeof(int32_t)), "fallback scratch");
+    sel.fb_s = ix->fb_s.as<double>();
+    sel.fb_i = ix->fb_i.as<int32_t>();
+    CU_TRY(launch_select_exact(kp, sel, st), "select launch");
+    CU_TRY(launch_fallback_exact(sel, ix->num_sms, st), "fallback launch");
+    ix->last.launches = run.launches + 3;
+    if (ix->timing) {
+        CU_TRY(cudaMemcpyAsync(&ix->host_words[8 + ix->ring_next], ix->flag_count, sizeof(int),
+                               cudaMemcpyDeviceToHost, st),
+               "fallback count");
+        cudaEventRecord(ix->ev[3], st);
+    }
+    return ST_OK;
+}
+
+}  // namespace mflat_cu
+
+namespace mflat_cu {
+
+// Read a pending timing slot (waits for its last event) and add it to the sums.
+void fold_slot(const mflat_cu_index* ix, int slot) {
+    auto& sl = ix->ring[slot];
+    if (!sl.pending) return;
+    sl.pending = false;
+    if (cudaEventSynchronize(sl.ev[3]) != cudaSuccess) return;
+    cudaEventElapsedTime(&sl.t.total_ms, sl.ev[0], sl.ev[3]);
+    cudaEventElapsedTime(&sl.t.screen_ms, sl.ev[1], sl.ev[2]);
+    cudaEventElapsedTime(&sl.t.select_ms, sl.ev[2], sl.ev[3]);
+    sl.t.fallback_queries = ix->host_words[8 + slot];
+    ix->sum.total_ms += sl.t.total_ms;
+    ix->sum.screen_ms += sl.t.screen_ms;
+    ix->sum.select_ms += sl.t.select_ms;
+    ix->sum.screen_launches += sl.t.screen_launches;
+    ix->sum.launches += sl.t.launches;
+    ix->sum.fallback_queries += sl.t.fallback_queries;
+    ix->sum_n += 1;
+}
+
+// Oldest first, so the sums add up in search order.
+void fold_all_slots(const mflat_cu_index* ix) {
+    for (int i = 0; i < kTimingRing; ++i) fold_slot(ix, (ix->ring_next + i) % kTimingRing);
+}
+
+void timing_begin(mflat_cu_index* ix) {
+    if (!ix->timing) return;
+    const int slot = ix->ring_next;
+    fold_slot(ix, slot);                 // reused after kTimingRing searches: long finished
+    ix->ev = ix->ring[slot].ev;
+    ix->host_words[8 + slot] = 0;
+    ix->last = mflat_cu_timing_t{};
+}
+
+void timing_end(mflat_cu_index* ix) {
+    if (!ix->timing) return;
+    const int slot = ix->ring_next;
+    ix->ring[slot].t = ix->last;
+    ix->ring[slot].pending = true;
+    ix->ring_last = slot;
+    ix->ring_next = (slot + 1) % kTimingRing;
+}
+
+}  // namespace mflat_cu
+
 extern "C" {
 
 const char* mflat_cu_last_error(void) { return last_error_message(); }
@@ -1026,14 +1125,13 @@ int mflat_cu_index_create(int device, int dim, int metric, int storage, mflat_cu
         (e = cudaMalloc(&ix->xmax_bits, sizeof(unsigned))) != cudaSuccess ||
         (e = cudaMalloc(&ix->err, sizeof(int))) != cudaSuccess ||
         (e = cudaMalloc(&ix->flag_count, sizeof(int))) != cudaSuccess ||
-        (e = cudaHostAlloc(&ix->host_words, 8 * sizeof(int), cudaHostAllocDefault)) != cudaSuccess) {
+        (e = cudaHostAlloc(&ix->host_words, kHostWords * sizeof(int), cudaHostAllocDefault)) != cudaSuccess) {
         mflat_cu_index_destroy(ix);
         return fail(e == cudaErrorMemoryAllocation ? ST_ALLOC : ST_DEVICE, "index setup", e);
     }
-    for (auto& ev : ix->ev) cudaEventCreate(&ev);
     cudaMemsetAsync(ix->xmax_bits, 0, sizeof(unsigned), ix->stream);
     cudaMemsetAsync(ix->err, 0, sizeof(int), ix->stream);
-    std::memset(ix->host_words, 0, 8 * sizeof(int));
+    std::memset(ix->host_words, 0, kHostWords * sizeof(int));
     if ((e = cudaStreamSynchronize(ix->stream)) != cudaSuccess) {
         mflat_cu_index_destroy(ix);
         return fail(ST_DEVICE, "index setup", e);
@@ -1062,8 +1160,9 @@ void mflat_cu_index_destroy(mflat_cu_index_t* ix) {
                       &ix->fb_i, &ix->buf_cnt, &ix->buf_s, &ix->buf_i, &ix->lk_words,
                       &ix->q16, &ix->qsq})
         b->release();
-    for (auto& ev : ix->ev)
-        if (ev) cudaEventDestroy(ev);
+    for (auto& slot : ix->ring)
+        for (auto& ev : slot.ev)
+            if (ev) cudaEventDestroy(ev);
     if (ix->stream) cudaStreamDestroy(ix->stream);
     delete ix;
 }
@@ -1125,13 +1224,38 @@ int mflat_cu_index_reset(mflat_cu_index_t* ix) {
 
 int mflat_cu_index_set_timing(mflat_cu_index_t* ix, int enable) {
     if (!ix) return fail(ST_BAD_ARG, "bad argument");
+    DeviceGuard g(ix->device);
+    fold_all_slots(ix);
+    if (enable && !ix->ring[0].ev[0]) {
+        for (auto& slot : ix->ring)
+            for (auto& ev : slot.ev) CU_TRY(cudaEventCreate(&ev), "timing events");
+    }
+    if (enable) {
+        ix->sum = mflat_cu_timing_t{};
+        ix->sum_n = 0;
+        ix->ring_last = -1;
+        ix->ring_next = 0;
+    }
     ix->timing = enable != 0;
     return ST_OK;
 }
 
 int mflat_cu_index_last_timing(const mflat_cu_index_t* ix, mflat_cu_timing_t* out) {
     if (!ix || !out) return fail(ST_BAD_ARG, "bad argument");
-    *out = ix->last;
+    *out = mflat_cu_timing_t{};
+    if (ix->ring_last < 0) return ST_OK;
+    DeviceGuard g(ix->device);
+    fold_slot(ix, ix->ring_last);
+    *out = ix->ring[ix->ring_last].t;
+    return ST_OK;
+}
+
+int mflat_cu_index_timing_sum(const mflat_cu_index_t* ix, mflat_cu_timing_t* out, int* n_searches) {
+    if (!ix || !out) return fail(ST_BAD_ARG, "bad argument");
+    DeviceGuard g(ix->device);
+    fold_all_slots(ix);
+    *out = ix->sum;
+    if (n_searches) *n_searches = ix->sum_n;
     return ST_OK;
 }
 
@@ -1140,9 +1264,10 @@ int mflat_cu_index_search(mflat_cu_index_t* ix, const float* queries, int m, int
     if (!ix || (!queries && m > 0) || m < 0 || k_out < 1) return fail(ST_BAD_ARG, "bad argument");
     if (m == 0) return ST_OK;
     DeviceGuard g(ix->device);
+    NvtxRange range("mflat.search");
     cudaStream_t st = on_device ? static_cast<cudaStream_t>(stream) : ix->stream;
     if (on_device) {
-        const int rc = check_device_error(ix);   // the previous asynchronous call
+        const int rc = check_device_error(ix, st);   // the previous asynchronous call
         if (rc != ST_OK) return rc;
     }
     const int64_t mk = static_cast<int64_t>(m) * k_out;
@@ -1154,124 +1279,41 @@ int mflat_cu_index_search(mflat_cu_index_t* ix, const float* queries, int m, int
         d_ids = ix->out_ids.as<int32_t>();
         d_dist = ix->out_dist.as<float>();
     }
-    const float empty = ix->metric == kL2 ? kInf : -kInf;
-    ix->last = mflat_cu_timing_t{};
-    int launches = 0;
-
+    timing_begin(ix);
+    int rc = ST_OK;
     if (ix->n == 0) {
+        if (ix->timing)
+            for (int i = 0; i < 3; ++i) cudaEventRecord(ix->ev[i], st);
+        const float empty = ix->metric == kL2 ? kInf : -kInf;
         fill_empty_kernel<<<blocks_for(mk, 256), 256, 0, st>>>(d_ids, d_dist, mk, empty);
-        ++launches;
         CU_TRY(cudaGetLastError(), "fill");
-    } else if (ix->storage != 0) {
-        const int rc = search_half(ix, queries, m, k_out, d_ids, d_dist, on_device, st);
-        if (rc != ST_OK) return rc;
-        if (ix->world > 1) {
-            const int rc2 = shard_merge(ix, m, k_out, d_ids, d_dist, st);
-            if (rc2 != ST_OK) return rc2;
-        }
-        if (!on_device) {
-            CU_TRY(cudaMemcpyAsync(out_ids, d_ids, mk * sizeof(int32_t), cudaMemcpyDeviceToHost, st), "download");
-            CU_TRY(cudaMemcpyAsync(out_dist, d_dist, mk * sizeof(float), cudaMemcpyDeviceToHost, st), "download");
-            const int rc3 = wait_stream_checked(ix, st);
-            if (rc3 != ST_OK) return rc3;
-        }
-        if (ix->timing) {
-            CU_TRY(cudaEventSynchronize(ix->ev[3]), "timing");
-            cudaEventElapsedTime(&ix->last.total_ms, ix->ev[0], ix->ev[3]);
-            cudaEventElapsedTime(&ix->last.screen_ms, ix->ev[1], ix->ev[2]);
-            cudaEventElapsedTime(&ix->last.select_ms, ix->ev[2], ix->ev[3]);
-        }
-        return check_device_error(ix);
-    } else {
-        const int kp = kp_for(k_out);
-        if (kp == 0) {
-            const int rc = search_large(ix, queries, m, k_out, d_ids, d_dist, on_device, st);
-            if (rc != ST_OK) return rc;
-            if (ix->world > 1) {
-                const int rc2 = shard_merge(ix, m, k_out, d_ids, d_dist, st);
-                if (rc2 != ST_OK) return rc2;
-            }
-            if (!on_device) {
-                CU_TRY(cudaMemcpyAsync(out_ids, d_ids, mk * sizeof(int32_t), cudaMemcpyDeviceToHost, st), "download");
-                CU_TRY(cudaMemcpyAsync(out_dist, d_dist, mk * sizeof(float), cudaMemcpyDeviceToHost, st), "download");
-                const int rc3 = wait_stream_checked(ix, st);
-                if (rc3 != ST_OK) return rc3;
-            }
-            if (ix->timing) {
-                cudaEventElapsedTime(&ix->last.total_ms, ix->ev[0], ix->ev[3]);
-                cudaEventElapsedTime(&ix->last.screen_ms, ix->ev[1], ix->ev[2]);
-                cudaEventElapsedTime(&ix->last.select_ms, ix->ev[2], ix->ev[3]);
-            }
-            return check_device_error(ix);
-        }
-        ScreenRun run;
-        int rc = run_screen(ix, queries, m, kp, on_device, st, run);
-        if (rc != ST_OK) return rc;
-        launches += run.launches;
-        ix->last.screen_launches = 1;
-        CU_TRY(ix->flag_list.ensure(static_cast<size_t>(m) * sizeof(int)), "fallback list");
-        cudaMemsetAsync(ix->flag_count, 0, sizeof(int), st);
-
-        SelectParams sel{};
-        sel.m = m;
-        sel.m_pad = run.m_pad;
-        sel.dim = ix->dim;
-        sel.d_pad = ix->d_pad;
-        sel.k_out = k_out;
-        sel.n_chunks = run.n_chunks;
-        sel.metric = ix->metric == kL2 ? kL2 : kIP;
-        sel.n = ix->n;
-        sel.part_score = run.part_s;
-        sel.part_id = run.part_i;
-        sel.q_hi = run.q_hi;
-        sel.q_lo = run.q_lo;
-        sel.qnorm = run.qnorm;
-        sel.db_hi = ix->db_hi;
-        sel.db_lo = ix->db_lo;
-        sel.xmax_bits = ix->xmax_bits;
-        // tf32 split error (2.5 * 2^-21 per product) plus fp32 accumulation of
-        // 3 * d_pad products, with an 8x safety factor on the latter.
-        sel.gamma = static_cast<float>((3.0 * ix->d_pad + 16.0) * std::ldexp(1.0, -21));
-        sel.id_base = ix->world > 1 ? ix->id_base : 0;
-        sel.out_ids = d_ids;
-        sel.out_dist = d_dist;
-        sel.flag_count = ix->flag_count;
-        sel.flag_list = ix->flag_list.as<int>();
-        sel.err = ix->err;
-        const size_t fb = static_cast<size_t>(m) * kFbChunks * k_out;
-        CU_TRY(ix->fb_s.ensure(fb * sizeof(double)), "fallback scratch");
-        CU_TRY(ix->fb_i.ensure(fb * sizeof(int32_t)), "fallback scratch");
-        sel.fb_s = ix->fb_s.as<double>();
-        sel.fb_i = ix->fb_i.as<int32_t>();
-        CU_TRY(launch_select_exact(kp, sel, st), "select launch");
-        ++launches;
-        CU_TRY(launch_fallback_exact(sel, ix->num_sms, st), "fallback launch");
-        launches += 2;
-        cudaMemcpyAsync(&ix->host_words[1], ix->flag_count, sizeof(int), cudaMemcpyDeviceToHost, st);
         if (ix->timing) cudaEventRecord(ix->ev[3], st);
+        ix->last.launches = 1;
+    } else if (ix->storage != 0) {
+        rc = search_half(ix, queries, m, k_out, d_ids, d_dist, on_device, st);
+    } else if (kp_for(k_out) == 0) {
+        rc = search_large(ix, queries, m, k_out, d_ids, d_dist, on_device, st);
+    } else {
+        rc = search_list_exact(ix, queries, m, k_out, d_ids, d_dist, on_device, st);
     }
+    if (rc != ST_OK) return rc;
     if (ix->world > 1) {
-        const int rc = shard_merge(ix, m, k_out, d_ids, d_dist, st);
+        NvtxRange mr("mflat.shard_merge");
+        rc = shard_merge(ix, m, k_out, d_ids, d_dist, st);
         if (rc != ST_OK) return rc;
-        launches += 1;
+        ix->last.launches += 1;
     }
-    cudaMemcpyAsync(&ix->host_words[0], ix->err, sizeof(int), cudaMemcpyDeviceToHost, st);
-    ix->last.launches = launches;
+    CU_TRY(cudaMemcpyAsync(&ix->host_words[0], ix->err, sizeof(int), cudaMemcpyDeviceToHost, st),
+           "status");
     if (!on_device) {
         CU_TRY(cudaMemcpyAsync(out_ids, d_ids, mk * sizeof(int32_t), cudaMemcpyDeviceToHost, st), "download");
         CU_TRY(cudaMemcpyAsync(out_dist, d_dist, mk * sizeof(float), cudaMemcpyDeviceToHost, st), "download");
-        int rc = wait_stream_checked(ix, st);
+        rc = wait_stream_checked(ix, st);
         if (rc != ST_OK) return rc;
-        rc = check_device_error(ix);
+        rc = check_device_error(ix, st);
         if (rc != ST_OK) return rc;
     }
-    if (ix->timing && ix->n > 0) {
-        CU_TRY(cudaEventSynchronize(ix->ev[3]), "timing");
-        cudaEventElapsedTime(&ix->last.total_ms, ix->ev[0], ix->ev[3]);
-        cudaEventElapsedTime(&ix->last.screen_ms, ix->ev[1], ix->ev[2]);
-        cudaEventElapsedTime(&ix->last.select_ms, ix->ev[2], ix->ev[3]);
-        ix->last.fallback_queries = ix->host_words[1];
-    }
+    timing_end(ix);
     return ST_OK;
 }
 

@@ -3,6 +3,7 @@
 #pragma once
 
 #include <cuda_runtime.h>
+#include <nvtx3/nvToolsExt.h>
 
 #include <cstdint>
 #include <string>
@@ -11,6 +12,9 @@
 #include "mflat_cuda.h"
 
 namespace mflat_cu {
+
+constexpr int kTimingRing = 32;   // searches whose timing events may be in flight
+constexpr int kHostWords = 8 + kTimingRing;
 
 enum : int { ST_OK = 0, ST_BAD_ARG = 2, ST_ALLOC = 3, ST_INTERNAL = 5, ST_DEVICE = 6 };
 
@@ -39,6 +43,15 @@ struct DeviceGuard {
     int prev = -1;
     explicit DeviceGuard(int dev);
     ~DeviceGuard();
+};
+
+// NVTX range for the host side of one operation (add, search, all-gather,
+// merge); costs nothing unless a profiler is attached.
+struct NvtxRange {
+    explicit NvtxRange(const char* name) { nvtxRangePushA(name); }
+    ~NvtxRange() { nvtxRangePop(); }
+    NvtxRange(const NvtxRange&) = delete;
+    NvtxRange& operator=(const NvtxRange&) = delete;
 };
 
 inline unsigned blocks_for(int64_t n, int t) { return static_cast<unsigned>((n + t - 1) / t); }
@@ -70,13 +83,29 @@ struct mflat_cu_index {
     unsigned* xmax_bits = nullptr;
     int* err = nullptr;           // device error word
     int* flag_count = nullptr;    // queries routed to the exact full scan
-    int* host_words = nullptr;    // pinned: [0] err, [1] flag_count
+    int* host_words = nullptr;    // pinned: [0] err, [4..7] status words, [8 + slot] fallback
+                                  // query count of timing slot `slot`
     mflat_cu::DevBuf stage_in, q_in, q_hi, q_lo, qnorm, part_s, part_i, flag_list, out_ids, out_dist;
     mflat_cu::DevBuf thr, thr_stat, fb_s, fb_i;
     mflat_cu::DevBuf buf_cnt, buf_s, buf_i, lk_words;   // large-k candidate buffers
     mflat_cu::DevBuf q16, qsq;                          // 16-bit queries, ||q||^2
+    // Timing (mflat_cu_index_set_timing): each search records 4 events into
+    // one slot of a ring and returns without waiting for them; a slot is read
+    // (and its device times added to `sum`) only when it is reused, or by
+    // last_timing / timing_sum, so timing does not serialise back-to-back
+    // searches.  `ev` points at the slot of the search in progress; `last`
+    // collects that search's launch counts.
     bool timing = false;
-    cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
+    cudaEvent_t* ev = nullptr;
+    struct TimingSlot {
+        cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
+        mflat_cu_timing_t t{};
+        bool pending = false;
+    };
+    mutable TimingSlot ring[mflat_cu::kTimingRing];
+    int ring_next = 0, ring_last = -1;
+    mutable mflat_cu_timing_t sum{};
+    mutable int sum_n = 0;
     mflat_cu_timing_t last{};
     bool force_simt = false;
     // row sharding (comm.cu)
@@ -92,7 +121,12 @@ namespace mflat_cu {
 // top-KP lists on stream `st`.  `queries` is device memory when on_device.
 int run_screen(mflat_cu_index* ix, const float* queries, int m, int kp, int on_device,
                cudaStream_t st, ScreenRun& out, int max_chunks = kMaxChunks);
-int check_device_error(mflat_cu_index* ix);
+int check_device_error(mflat_cu_index* ix, cudaStream_t st);
+// Timing ring (no-ops unless timing is on): begin points ix->ev at a free
+// slot; end (after the search's last event is recorded on the stream) marks
+// the slot pending with the counts in ix->last.
+void timing_begin(mflat_cu_index* ix);
+void timing_end(mflat_cu_index* ix);
 void comm_release(mflat_cu_index* ix);
 // Plain communicator helpers (k-means training over sharded points).
 int comm_create(void** out, int rank, int world, const uint8_t* comm_id);
@@ -100,6 +134,9 @@ void comm_destroy(void* comm);
 int comm_allgather_bytes(void* comm, const void* send, void* recv, size_t bytes, cudaStream_t st);
 int comm_wait(void** comm, cudaStream_t st);
 int shard_merge(mflat_cu_index* ix, int m, int k_out, int32_t* ids, float* dist, cudaStream_t st);
+// Merge of gathered per-rank lists [world][m][k] into [m][k] (comm.cu).
+cudaError_t launch_merge_ranks(const int32_t* gids, const float* gdist, int world, int m, int k,
+                               int metric, int32_t* out_ids, float* out_dist, cudaStream_t st);
 // Synchronise `st`; with a communicator attached, watch it for peer failure.
 int wait_stream_checked(mflat_cu_index* ix, cudaStream_t st);
 const char* last_error_message();

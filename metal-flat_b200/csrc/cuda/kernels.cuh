@@ -36,6 +36,14 @@ constexpr int kFbChunks = 64;     // database chunks of the exact fallback scan
 
 enum Metric : int { kL2 = 0, kIP = 1, kCosine = 2 };
 
+// Relative error bound gamma of a screen dot product over d_pad elements:
+// |dot' - q.x| <= gamma * ||q|| * ||x||.  3xTF32: split error 2.5 * 2^-21 per
+// product plus fp32 accumulation of 3 * d_pad products, with an 8x safety
+// factor on the latter.
+inline float screen_gamma(int d_pad) {
+    return static_cast<float>((3.0 * d_pad + 16.0) * 4.76837158203125e-07);   // 2^-21
+}
+
 struct ScreenParams {
     int m;                 // queries
     int m_pad;             // multiple of kBM

@@ -83,7 +83,7 @@ extern "C" int mflat_cu_kmeans_assign(const float* points, int64_t n, const floa
     sel.db_hi = ix->db_hi;
     sel.db_lo = ix->db_lo;
     sel.xmax_bits = ix->xmax_bits;
-    sel.gamma = static_cast<float>((3.0 * ix->d_pad + 16.0) * std::ldexp(1.0, -21));
+    sel.gamma = screen_gamma(ix->d_pad);
     sel.flag_count = ix->flag_count;
     sel.flag_list = ix->flag_list.as<int>();
     sel.err = ix->err;
@@ -95,5 +95,5 @@ extern "C" int mflat_cu_kmeans_assign(const float* points, int64_t n, const floa
                "download");
     // The cached index's scratch is reused by the next call: finish first.
     CU_TRY(cudaStreamSynchronize(st), "assignment");
-    return check_device_error(ix);
+    return check_device_error(ix, st);
 }

@@ -64,6 +64,19 @@ MFLAT_CU_API int mflat_cu_index_search_noalloc(mflat_cu_index_t* ix, const float
                                                void* stream);
 MFLAT_CU_API int mflat_cu_index_set_timing(mflat_cu_index_t* ix, int enable);
 MFLAT_CU_API int mflat_cu_index_last_timing(const mflat_cu_index_t* ix, mflat_cu_timing_t* out);
+/* Sums of every search's timing since timing was last enabled (waits for the
+ * searches still running); *n_searches = how many. */
+MFLAT_CU_API int mflat_cu_index_timing_sum(const mflat_cu_index_t* ix, mflat_cu_timing_t* out,
+                                           int* n_searches);
+
+/* The on-device merge of a sharded search on its own: d_gids / d_gdist hold
+ * `world` lists per query ([world][m][k], each nearest-first, ids global, -1
+ * padded); writes the merged [m][k] (nearer first, then lower id).  Device
+ * pointers, enqueued on `stream`.  world rounded up to a power of two times
+ * k times 12 bytes must fit in 200 KB. */
+MFLAT_CU_API int mflat_cu_merge_ranks(const int32_t* d_gids, const float* d_gdist, int world, int m,
+                                      int k, int metric, int32_t* d_out_ids, float* d_out_dist,
+                                      void* stream);
 
 /* k-means assignment step: bit-exact argmin of the fp32 sequential sqL2. */
 MFLAT_CU_API int mflat_cu_kmeans_assign(const float* points, int64_t n, const float* centroids,

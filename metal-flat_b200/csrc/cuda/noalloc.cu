@@ -20,7 +20,10 @@
 // streams, or two indexes on one device -- race on the array; serialise them.
 // The first call on a device resolves the array's device address with
 // cudaGetSymbolAddress (the host-side name is only a stand-in); make that first
-// call before any stream capture.
+// call before any stream capture.  This entry point always runs the
+// tensor-core screen (the MFLAT_SCREEN=simt cross-check does not apply to it)
+// and records no timing events (mflat_cu_index_last_timing keeps describing
+// the index's last regular search).
 #include <cuda_runtime.h>
 
 #include <cmath>
@@ -106,9 +109,9 @@ extern "C" int mflat_cu_index_search_noalloc(mflat_cu_index_t* ix, const float* 
     unsigned char* base = nullptr;
     int rc = scratch_base(ix->device, &base);
     if (rc != ST_OK) return rc;
-    rc = check_device_error(ix);   // the previous asynchronous call on this index
-    if (rc != ST_OK) return rc;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
+    rc = check_device_error(ix, st);   // the previous asynchronous call on this index
+    if (rc != ST_OK) return rc;
     const int64_t mk = static_cast<int64_t>(m) * k_out;
     const float empty = ix->metric == kL2 ? INFINITY : -INFINITY;
     if (ix->n == 0) {
@@ -180,7 +183,7 @@ extern "C" int mflat_cu_index_search_noalloc(mflat_cu_index_t* ix, const float* 
     sel.db_hi = ix->db_hi;
     sel.db_lo = ix->db_lo;
     sel.xmax_bits = ix->xmax_bits;
-    sel.gamma = static_cast<float>((3.0 * d_pad + 16.0) * std::ldexp(1.0, -21));
+    sel.gamma = screen_gamma(d_pad);
     sel.out_ids = d_ids;
     sel.out_dist = d_dist;
     sel.flag_count = ix->flag_count;

@@ -16,6 +16,7 @@
 #include <cfloat>
 
 #include "kernels.cuh"
+#include "ptx.cuh"
 
 namespace mflat_cu {
 namespace {
@@ -88,81 +89,141 @@ __device__ __forceinline__ double exact_score(int metric, const float* qh, const
     return acc;
 }
 
-template <int KP>
-__global__ void __launch_bounds__(kSelectMaxThreads) select_exact_kernel(const SelectParams p) {
-    const int qi = blockIdx.x;
-    if (qi >= p.m) return;
-    __shared__ Cand red[33];
-    __shared__ float sel_s[KP];
-    __shared__ int sel_id[KP];
-    __shared__ double ex_s[KP];
-    __shared__ int s_ok;
+// ---------------------------------------------------------------------------
+// Warp-level merge of the per-chunk candidate lists.  A candidate is packed
+// into a 64-bit key whose unsigned order is the selection order: the high
+// word is the order-preserving key of the screen score (score desc), the low
+// word ~id (id asc among equal scores); 0 marks an empty slot.  A warp holds
+// one sorted list of 32 keys, one per lane (lane 0 = best).  Merging in the
+// next chunk's sorted list keeps the 32 largest of the union: max(a[i],
+// b[31 - i]) is a bitonic sequence holding exactly those, and five
+// half-cleaner stages sort it again.  Lists are read with one coalesced load
+// per chunk; nothing in the merge depends on a load of an earlier round.
+constexpr unsigned kFull = 0xffffffffu;
 
-    // 1. tournament merge of the per-chunk lists (each sorted best-first)
-    const int t = threadIdx.x;
-    int head = 0;
-    const int64_t base = (static_cast<int64_t>(t) * p.m_pad + qi) * KP;
-    for (int r = 0; r < KP; ++r) {
-        Cand c{-DBL_MAX, -1, t};
-        if (t < p.n_chunks && head < KP) {
-            c.s = p.part_score[base + head];
-            c.id = p.part_id[base + head];
-        }
-        const Cand w = block_best(c, red);
-        if (t == 0) {
-            sel_s[r] = static_cast<float>(w.s);
-            sel_id[r] = w.id;
-        }
-        if (w.id >= 0 && w.owner == t) ++head;
+__device__ __forceinline__ uint64_t cand_key(float s, int id) {
+    if (id < 0) return 0ull;
+    return (static_cast<uint64_t>(score_key(s)) << 32) | static_cast<uint32_t>(~static_cast<uint32_t>(id));
+}
+__device__ __forceinline__ float key_score(uint64_t k) {
+    const uint32_t h = static_cast<uint32_t>(k >> 32);
+    return __uint_as_float((h & 0x80000000u) ? (h & 0x7fffffffu) : ~h);
+}
+__device__ __forceinline__ int key_id(uint64_t k) {
+    return k == 0ull ? -1 : static_cast<int>(~static_cast<uint32_t>(k));
+}
+
+__device__ __forceinline__ uint64_t merge_top32(uint64_t a, uint64_t b, int lane) {
+    const uint64_t br = __shfl_sync(kFull, b, 31 - lane);
+    uint64_t v = a > br ? a : br;
+#pragma unroll
+    for (int st = 16; st >= 1; st >>= 1) {
+        const uint64_t o = __shfl_xor_sync(kFull, v, st);
+        v = (lane & st) == 0 ? (v > o ? v : o) : (v < o ? v : o);
     }
-    __syncthreads();
+    return v;
+}
 
-    // 2. proof that the true top-k is inside the candidates
-    int n_valid = 0;
-    for (int i = 0; i < KP; ++i) n_valid += sel_id[i] >= 0 ? 1 : 0;
-    if (t == 0) {
-        int ok = 1;
-        if (n_valid >= KP && p.k_out <= KP) {
-            const double xmax = static_cast<double>(__uint_as_float(*p.xmax_bits));
-            const double E = error_bound(p.metric, p.qnorm[qi], xmax, p.gamma);
-            ok = static_cast<double>(sel_s[KP - 1]) < static_cast<double>(sel_s[p.k_out - 1]) - 2.0 * E;
+// Top 32 keys over the query's n_lists lists of KP entries (each sorted best
+// first); lane i returns the i-th best.  Lanes >= KP of a list read nothing.
+template <int KP>
+__device__ __forceinline__ uint64_t warp_merge_lists(const float* __restrict__ part_s,
+                                                     const int32_t* __restrict__ part_i, int n_lists,
+                                                     int m_pad, int qi, int lane) {
+    uint64_t top = 0ull;
+    constexpr int kU = 4;
+    for (int c0 = 0; c0 < n_lists; c0 += kU) {
+        uint64_t kk[kU];
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+            kk[u] = 0ull;
+            const int c = c0 + u;
+            if (c < n_lists && lane < KP) {
+                const int64_t o = (static_cast<int64_t>(c) * m_pad + qi) * KP + lane;
+                kk[u] = cand_key(__ldg(part_s + o), __ldg(part_i + o));
+            }
         }
-        if (!ok) {
+#pragma unroll
+        for (int u = 0; u < kU; ++u)
+            if (c0 + u < n_lists) top = (c0 + u == 0) ? kk[u] : merge_top32(top, kk[u], lane);
+    }
+    return top;
+}
+
+// Bitonic sort of one (score, id) pair per lane into better-first order
+// (score desc, id asc, id < 0 last): lane 0 ends with the best.
+__device__ __forceinline__ void warp_sort_better_first(double& s, int& id, int lane) {
+#pragma unroll
+    for (int size = 2; size <= 32; size <<= 1) {
+#pragma unroll
+        for (int st = size >> 1; st >= 1; st >>= 1) {
+            const double os = __shfl_xor_sync(kFull, s, st);
+            const int oid = __shfl_xor_sync(kFull, id, st);
+            const Cand me{s, id, 0}, other{os, oid, 0};
+            // blocks of `size` alternate direction until the last merge
+            const bool ascending = (lane & size) == 0;
+            const bool lower = (lane & st) == 0;
+            // the pair's lower lane keeps the better entry in an ascending
+            // (better-first) block, the worse one in a descending block
+            if (lower == ascending ? better(other, me) : better(me, other)) {
+                s = os;
+                id = oid;
+            }
+        }
+    }
+}
+
+// One warp per query: merge the chunk lists into the top KP candidates, prove
+// that the true top-k is among them, re-score them exactly in fp64 and write
+// the k nearest in (distance, id) order.  Queries whose proof fails are
+// listed for the exact full scan and written by it.
+template <int KP>
+__global__ void __launch_bounds__(128) select_exact_kernel(const SelectParams p) {
+    const int lane = threadIdx.x & 31;
+    const int qi = blockIdx.x * 4 + (threadIdx.x >> 5);
+    if (qi >= p.m) return;                      // uniform per warp
+    uint64_t top = warp_merge_lists<KP>(p.part_score, p.part_id, p.n_chunks, p.m_pad, qi, lane);
+    if (lane >= KP) top = 0ull;                 // only the merged top-KP are proven candidates
+    const float s_screen = key_score(top);
+    const int id = key_id(top);
+    const int n_valid = __popc(__ballot_sync(kFull, id >= 0));
+
+    // proof that the true top-k is inside the candidates
+    bool ok = true;
+    if (n_valid >= KP && p.k_out <= KP) {
+        const float sk = __shfl_sync(kFull, s_screen, p.k_out - 1);
+        const float skp = __shfl_sync(kFull, s_screen, KP - 1);
+        const double xmax = static_cast<double>(__uint_as_float(*p.xmax_bits));
+        const double E = error_bound(p.metric, p.qnorm[qi], xmax, p.gamma);
+        ok = static_cast<double>(skp) < static_cast<double>(sk) - 2.0 * E;
+    }
+    if (!ok) {
+        if (lane == 0) {
             const int slot = atomicAdd(p.flag_count, 1);
             p.flag_list[slot] = qi;
         }
-        s_ok = ok;
+        return;
     }
-    __syncthreads();
-    if (!s_ok) return;
 
-    // 3. exact fp64 re-score of the candidates
-    const float* qh = p.q_hi + static_cast<int64_t>(qi) * p.d_pad;
-    const float* ql = p.q_lo + static_cast<int64_t>(qi) * p.d_pad;
-    if (t < n_valid) {
-        const int64_t id = sel_id[t];
-        ex_s[t] = exact_score(p.metric, qh, ql, p.db_hi + id * p.d_pad, p.db_lo + id * p.d_pad, p.dim);
+    // exact fp64 re-score (lane = candidate), then (distance, id) order
+    double ex = -DBL_MAX;
+    if (id >= 0) {
+        const float* qh = p.q_hi + static_cast<int64_t>(qi) * p.d_pad;
+        const float* ql = p.q_lo + static_cast<int64_t>(qi) * p.d_pad;
+        const int64_t r = id;
+        ex = exact_score(p.metric, qh, ql, p.db_hi + r * p.d_pad, p.db_lo + r * p.d_pad, p.dim);
     }
-    __syncthreads();
-
-    // 4. order by (exact score desc, id asc) and emit nearest-first
-    if (t < n_valid) {
-        const Cand me{ex_s[t], sel_id[t], t};
-        int rank = 0;
-        for (int u = 0; u < n_valid; ++u) {
-            const Cand o{ex_s[u], sel_id[u], u};
-            if (better(o, me)) ++rank;
+    int rid = id;
+    warp_sort_better_first(ex, rid, lane);
+    if (lane < p.k_out) {
+        const int64_t o = static_cast<int64_t>(qi) * p.k_out + lane;
+        if (rid >= 0) {
+            p.out_ids[o] = static_cast<int32_t>(rid + p.id_base);
+            p.out_dist[o] = static_cast<float>(p.metric == kL2 ? -ex : ex);
+        } else {
+            p.out_ids[o] = -1;
+            p.out_dist[o] = p.metric == kL2 ? __int_as_float(0x7f800000) : -__int_as_float(0x7f800000);
         }
-        if (rank < p.k_out) {
-            const int64_t o = static_cast<int64_t>(qi) * p.k_out + rank;
-            p.out_ids[o] = static_cast<int32_t>(me.id + p.id_base);
-            p.out_dist[o] = static_cast<float>(p.metric == kL2 ? -me.s : me.s);
-        }
-    }
-    for (int pos = n_valid + t; pos < p.k_out; pos += blockDim.x) {
-        const int64_t o = static_cast<int64_t>(qi) * p.k_out + pos;
-        p.out_ids[o] = -1;
-        p.out_dist[o] = p.metric == kL2 ? __int_as_float(0x7f800000) : -__int_as_float(0x7f800000);
     }
 }
 
@@ -361,45 +422,36 @@ __global__ void __launch_bounds__(128) kmeans_fallback_kernel(const SelectParams
     }
 }
 
-// Recall path (fp16 / bf16 storage): the screen's scores are the answer.
+// Recall path (fp16 / bf16 storage): the screen's scores are the answer.  One
+// warp per query merges the lists (k_out <= KP); lane r writes rank r.
 template <int KP>
-__global__ void __launch_bounds__(kSelectMaxThreads) select_recall_kernel(const SelectParams p, const float* qsq) {
-    const int qi = blockIdx.x;
+__global__ void __launch_bounds__(128) select_recall_kernel(const SelectParams p, const float* qsq) {
+    const int lane = threadIdx.x & 31;
+    const int qi = blockIdx.x * 4 + (threadIdx.x >> 5);
     if (qi >= p.m) return;
-    __shared__ Cand red[33];
-    const int t = threadIdx.x;
-    int head = 0;
-    const int64_t base = (static_cast<int64_t>(t) * p.m_pad + qi) * KP;
-    const float empty = p.metric == kL2 ? __int_as_float(0x7f800000) : -__int_as_float(0x7f800000);
-    for (int r = 0; r < p.k_out; ++r) {
-        Cand c{-DBL_MAX, -1, t};
-        if (t < p.n_chunks && head < KP) {
-            c.s = p.part_score[base + head];
-            c.id = p.part_id[base + head];
+    const uint64_t top = warp_merge_lists<KP>(p.part_score, p.part_id, p.n_chunks, p.m_pad, qi, lane);
+    if (lane < p.k_out) {
+        const int64_t o = static_cast<int64_t>(qi) * p.k_out + lane;
+        const int id = key_id(top);
+        if (id >= 0) {
+            const float s = key_score(top);
+            p.out_ids[o] = static_cast<int32_t>(id + p.id_base);
+            p.out_dist[o] = p.metric == kL2
+                                ? fmaxf(0.0f, static_cast<float>(static_cast<double>(qsq[qi]) - s))
+                                : s;
+        } else {
+            p.out_ids[o] = -1;
+            p.out_dist[o] = p.metric == kL2 ? __int_as_float(0x7f800000) : -__int_as_float(0x7f800000);
         }
-        const Cand w = block_best(c, red);
-        if (t == 0) {
-            const int64_t o = static_cast<int64_t>(qi) * p.k_out + r;
-            if (w.id >= 0) {
-                p.out_ids[o] = static_cast<int32_t>(w.id + p.id_base);
-                p.out_dist[o] = p.metric == kL2
-                                    ? fmaxf(0.0f, static_cast<float>(static_cast<double>(qsq[qi]) - w.s))
-                                    : static_cast<float>(w.s);
-            } else {
-                p.out_ids[o] = -1;
-                p.out_dist[o] = empty;
-            }
-        }
-        if (w.id >= 0 && w.owner == t) ++head;
     }
 }
 
-// One thread per candidate list in the tournament merge.
-inline int select_threads(int n_lists) { return n_lists > 128 ? kSelectMaxThreads : 128; }
+// Four queries (warps) per block.
+inline unsigned select_blocks(int m) { return static_cast<unsigned>((m + 3) / 4); }
 
 template <int KP>
 cudaError_t launch_select_kp(const SelectParams& p, cudaStream_t stream) {
-    select_exact_kernel<KP><<<p.m, select_threads(p.n_chunks), 0, stream>>>(p);
+    select_exact_kernel<KP><<<select_blocks(p.m), 128, 0, stream>>>(p);
     return cudaGetLastError();
 }
 
@@ -429,9 +481,9 @@ cudaError_t launch_kmeans_select(const SelectParams& p, int32_t* out, int grid_f
 cudaError_t launch_select_recall(int kp, const SelectParams& p, const float* qsq, cudaStream_t stream) {
     if (p.n_chunks > kMaxChunks || p.n_chunks < 1 || p.k_out > kp) return cudaErrorInvalidValue;
     switch (kp) {
-        case 4: select_recall_kernel<4><<<p.m, select_threads(p.n_chunks), 0, stream>>>(p, qsq); break;
-        case 8: select_recall_kernel<8><<<p.m, select_threads(p.n_chunks), 0, stream>>>(p, qsq); break;
-        case 16: select_recall_kernel<16><<<p.m, select_threads(p.n_chunks), 0, stream>>>(p, qsq); break;
+        case 4: select_recall_kernel<4><<<select_blocks(p.m), 128, 0, stream>>>(p, qsq); break;
+        case 8: select_recall_kernel<8><<<select_blocks(p.m), 128, 0, stream>>>(p, qsq); break;
+        case 16: select_recall_kernel<16><<<select_blocks(p.m), 128, 0, stream>>>(p, qsq); break;
         default: return cudaErrorInvalidValue;
     }
     return cudaGetLastError();

@@ -151,6 +151,22 @@ void FlatIndex::setTiming(bool enable) {
     raise_status(mflat_cu_index_set_timing(mImpl->need(), enable ? 1 : 0), "timing");
 }
 
+SearchTiming FlatIndex::timingSum(int* n) const {
+    SearchTiming t;
+    mflat_cu_timing_t c{};
+    int cnt = 0;
+    if (mImpl->dev && mflat_cu_index_timing_sum(mImpl->dev, &c, &cnt) == 0) {
+        t.total_ms = c.total_ms;
+        t.screen_ms = c.screen_ms;
+        t.select_ms = c.select_ms;
+        t.screen_launches = c.screen_launches;
+        t.launches = c.launches;
+        t.fallback_queries = c.fallback_queries;
+    }
+    if (n) *n = cnt;
+    return t;
+}
+
 SearchTiming FlatIndex::lastTiming() const {
     SearchTiming t;
     mflat_cu_timing_t c{};

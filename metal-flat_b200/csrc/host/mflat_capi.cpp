@@ -232,7 +232,8 @@ MFLAT_API mflat_status_t mflat_flat_search_device(mflat_flat_index_t* h, const f
 MFLAT_API mflat_status_t mflat_flat_search_noalloc(mflat_flat_index_t* h, const float* q, int m,
                                                    int k, int32_t* oi, float* od, int* ok,
                                                    void* stream) {
-    if (!h || !q) return MFLAT_ERR_NULL_ARG;
+    // a null query pointer is accepted for m == 0, as the device layer does
+    if (!h || (!q && m > 0)) return MFLAT_ERR_NULL_ARG;
     if (m < 0 || k < 1) return MFLAT_ERR_BAD_ARG;
     if (m > 0 && (!oi || !od)) return MFLAT_ERR_NULL_ARG;
     return guarded([&] {
@@ -250,6 +251,21 @@ MFLAT_API mflat_status_t mflat_flat_set_timing(mflat_flat_index_t* h, int enable
         h->idx.setTiming(enable != 0);
         return MFLAT_OK;
     });
+}
+
+MFLAT_API mflat_status_t mflat_flat_timing_sum(const mflat_flat_index_t* h, mflat_timing_t* out,
+                                               int* n_searches) {
+    if (!h || !out) return MFLAT_ERR_NULL_ARG;
+    int n = 0;
+    const mflat::SearchTiming t = h->idx.timingSum(&n);
+    out->total_ms = t.total_ms;
+    out->screen_ms = t.screen_ms;
+    out->select_ms = t.select_ms;
+    out->screen_launches = t.screen_launches;
+    out->launches = t.launches;
+    out->fallback_queries = t.fallback_queries;
+    if (n_searches) *n_searches = n;
+    return MFLAT_OK;
 }
 
 MFLAT_API mflat_status_t mflat_flat_last_timing(const mflat_flat_index_t* h, mflat_timing_t* out) {

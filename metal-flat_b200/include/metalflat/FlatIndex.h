@@ -84,6 +84,8 @@ public:
                              void* stream);
     void setTiming(bool enable);
     SearchTiming lastTiming() const;
+    // Field-wise sums over every search since setTiming(true); *n = how many.
+    SearchTiming timingSum(int* n) const;
     // Row sharding: this index holds global rows [id_base, id_base + size());
     // search() becomes a collective over `world` ranks returning global ids.
     void setShard(int rank, int world, const uint8_t* comm_id, int64_t id_base);

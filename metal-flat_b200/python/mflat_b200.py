@@ -29,7 +29,7 @@ EXPORTS = [
     "mflat_flat_dim", "mflat_flat_add", "mflat_flat_reset", "mflat_flat_search",
     "mflat_flat_create_ex", "mflat_flat_storage", "mflat_flat_device",
     "mflat_flat_add_device", "mflat_flat_search_device", "mflat_flat_set_timing",
-    "mflat_flat_last_timing", "mflat_kmeans_assign", "mflat_kmeans_assign_device",
+    "mflat_flat_last_timing", "mflat_flat_timing_sum", "mflat_kmeans_assign", "mflat_kmeans_assign_device",
     "mflat_comm_unique_id", "mflat_flat_set_shard", "mflat_flat_search_noalloc",
     "mflat_flat_save", "mflat_flat_load",
     "mflat_coarse_create", "mflat_coarse_free", "mflat_coarse_train", "mflat_coarse_nlist",
@@ -89,6 +89,7 @@ def lib() -> ctypes.CDLL:
         "mflat_flat_search_noalloc": ([vp, vp, ci, ci, vp, vp, ctypes.POINTER(ci), vp], ci),
         "mflat_flat_set_timing": ([vp, ci], ci),
         "mflat_flat_last_timing": ([vp, ctypes.POINTER(Timing)], ci),
+        "mflat_flat_timing_sum": ([vp, ctypes.POINTER(Timing), ctypes.POINTER(ci)], ci),
         "mflat_kmeans_assign": ([f32p, ci, f32p, ci, ci, i32p, ci], ci),
         "mflat_kmeans_assign_device": ([vp, ci, vp, ci, ci, vp, ci, vp], ci),
         "mflat_comm_unique_id": ([ctypes.c_char_p], ci),
@@ -285,6 +286,14 @@ class FlatIndex:
         t = Timing()
         _check(self._lib.mflat_flat_last_timing(self._h, ctypes.byref(t)), "last_timing")
         return t
+
+    def timing_sum(self) -> tuple[Timing, int]:
+        """(field-wise sums, number of searches) since set_timing(True)."""
+        t = Timing()
+        n = ctypes.c_int(0)
+        _check(self._lib.mflat_flat_timing_sum(self._h, ctypes.byref(t), ctypes.byref(n)),
+               "timing_sum")
+        return t, n.value
 
     def set_shard(self, rank: int, world: int, comm_id: bytes | None, id_base: int) -> None:
         _check(self._lib.mflat_flat_set_shard(self._h, rank, world, comm_id, int(id_base)),

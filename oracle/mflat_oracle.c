@@ -207,3 +207,35 @@ void mfo_merge_shards(const int32_t* ids, const float* dist, int nshard,
         free(head);
     }
 }
+
+/* Exact fp64 scores of (query, row) pairs, the same evaluation as
+ * mfo_flat_search_f64: out[i] = score(q[qi[i]], rows[ri[i]]), larger = nearer
+ * (-sqL2 for metric 0, dot otherwise).  Used by the screened oracle at the
+ * benchmarked sizes (oracle/scale.py). */
+void mfo_score_pairs_f64(const float* rows, int dim, int metric, const float* q,
+                         const int64_t* qi, const int64_t* ri, int64_t npairs, double* out) {
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < npairs; ++i)
+        out[i] = score_f64(metric == MFO_L2 ? MFO_L2 : MFO_IP, q + qi[i] * (int64_t)dim,
+                           rows + ri[i] * (int64_t)dim, dim);
+}
+
+/* mfo_kmeans_assign_f32 restricted to a candidate list per point (ascending
+ * centroid ids, CSR cand_ptr[n+1] / cand_ids): the same sequential fp32 sqL2
+ * and strict '<' scan, so when every centroid that can reach the minimum is
+ * listed the result equals the full scan's. */
+void mfo_kmeans_assign_cand(const float* points, int64_t n, const float* cents, int dim,
+                            const int64_t* cand_ptr, const int32_t* cand_ids, int32_t* out) {
+#pragma omp parallel for schedule(dynamic, 64)
+    for (int64_t i = 0; i < n; ++i) {
+        const float* v = points + i * (int64_t)dim;
+        float best = INFINITY;
+        int bestC = 0;
+        for (int64_t j = cand_ptr[i]; j < cand_ptr[i + 1]; ++j) {
+            const int c = cand_ids[j];
+            const float dd = mfo_sq_l2_f32(v, cents + (int64_t)c * dim, dim);
+            if (dd < best) { best = dd; bestC = c; }
+        }
+        out[i] = bestC;
+    }
+}

@@ -86,6 +86,15 @@ void mfo_merge_shards(const int32_t* ids, const float* dist, int nshard,
                       int64_t m, int k, int metric,
                       int32_t* out_ids, float* out_dist);
 
+/* Exact fp64 scores of listed (query, row) pairs (score order of
+ * mfo_flat_search_f64; metric 2 = 1 on normalised inputs). */
+void mfo_score_pairs_f64(const float* rows, int dim, int metric, const float* q,
+                         const int64_t* qi, const int64_t* ri, int64_t npairs, double* out);
+
+/* mfo_kmeans_assign_f32 over a per-point candidate list (CSR, ascending ids). */
+void mfo_kmeans_assign_cand(const float* points, int64_t n, const float* cents, int dim,
+                            const int64_t* cand_ptr, const int32_t* cand_ids, int32_t* out);
+
 #ifdef __cplusplus
 }
 #endif

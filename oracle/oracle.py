@@ -54,6 +54,10 @@ def lib() -> ctypes.CDLL:
                                                   np.ctypeslib.ndpointer(np.int64, flags="C_CONTIGUOUS"),
                                                   f32p, i32p, i32p, i32p]
         _lib.mfo_kmeans_train_sharded.restype = ci
+        i64p = np.ctypeslib.ndpointer(np.int64, flags="C_CONTIGUOUS")
+        f64p = np.ctypeslib.ndpointer(np.float64, flags="C_CONTIGUOUS")
+        _lib.mfo_score_pairs_f64.argtypes = [f32p, ci, ci, f32p, i64p, i64p, i64, f64p]
+        _lib.mfo_kmeans_assign_cand.argtypes = [f32p, i64, f32p, ci, i64p, i32p, i32p]
     return _lib
 
 

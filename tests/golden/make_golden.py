@@ -1,8 +1,8 @@
 """Generate the golden fixtures in tests/golden/ from the reference itself.
 
-Run in the build container (where the reference tree is mounted):
+Run where a source checkout of the reference (metal-flat) is available:
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py <path to the metal-flat checkout>
 
 It compiles oracle/_ref/libref_golden.so from the reference's own
 src/Distance.h and src/Log.cpp (recipe: oracle/Makefile) and records, for
@@ -30,8 +30,8 @@ ROOT = os.path.dirname(os.path.dirname(HERE))
 ORACLE = os.path.join(ROOT, "oracle")
 
 
-def load_ref():
-    subprocess.run(["make", "-s", "-C", ORACLE], check=True)
+def load_ref(ref_dir):
+    subprocess.run(["make", "-s", "-C", ORACLE, f"REF={ref_dir}"], check=True)
     path = os.path.join(ORACLE, "_ref", "libref_golden.so")
     if not os.path.exists(path):
         sys.exit("reference tree not available: cannot build libref_golden.so")
@@ -89,7 +89,9 @@ def cpu_search(L, db, q, k, metric):
 
 
 def main():
-    L = load_ref()
+    if len(sys.argv) != 2:
+        sys.exit("usage: make_golden.py <path to the metal-flat checkout>")
+    L = load_ref(os.path.abspath(sys.argv[1]))
     rng = np.random.default_rng(20261201)
     out = {}
     for n, dim in ((37, 19), (64, 128), (9, 1)):

@@ -71,6 +71,13 @@ def test_argument_checks_without_device(built_lib):
         # m == 0 is valid and produces nothing
         assert L.mflat_flat_search(h, fp, 0, 5, None, None, ctypes.byref(used)) == 0
         assert used.value == 0
+        # the allocation-free entry takes a null query pointer when m == 0,
+        # like the device layer, and still rejects it for m > 0
+        used.value = -1
+        assert L.mflat_flat_search_noalloc(h, None, 0, 5, None, None, ctypes.byref(used), None) == 0
+        assert used.value == 0
+        assert L.mflat_flat_search_noalloc(h, None, 1, 5, None, None, None, None) == 1
+        assert L.mflat_flat_search_noalloc(None, None, 0, 5, None, None, None, None) == 1
         assert L.mflat_flat_set_shard(h, 2, 2, None, 0) == 2
     finally:
         L.mflat_flat_free(h)
