@@ -61,7 +61,7 @@ typedef enum {                      /* c/include/mflat.h:42-49, value-stable */
 
 /* ADDITIVE: storage precision of the database rows on the device. */
 typedef enum {
-    MFLAT_STORAGE_FP32 = 0,         /* exact path: 3xTF32 screen + fp64 re-rank */
+    MFLAT_STORAGE_FP32 = 0,         /* exact path: 3 x bf16 screen + fp64 re-rank */
     MFLAT_STORAGE_FP16 = 1,         /* kind::f16 tensor cores, recall path      */
     MFLAT_STORAGE_BF16 = 2
 } mflat_storage_t;

@@ -95,23 +95,6 @@ bool get_encoder() {
     return g_encode != nullptr;
 }
 
-// Row-major fp32 matrix [rows][inner] -> 2-D tensor map with a
-// [box_rows][32 floats] box and 128-byte swizzle (the UMMA K-major SW128
-// layout).  Rows past `rows` read as zero.
-bool make_map_f32(CUtensorMap* map, const float* base, uint64_t inner, uint64_t rows,
-                  uint32_t box_rows) {
-    if (!get_encoder()) return false;
-    cuuint64_t dims[2] = {inner, rows};
-    cuuint64_t strides[1] = {inner * sizeof(float)};
-    cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), box_rows};
-    cuuint32_t estr[2] = {1, 1};
-    CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims,
-                          strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    return r == CUDA_SUCCESS;
-}
-
 // 16-bit rows [rows][inner] (fp16 / bf16 bits): box [box_rows][64 halves].
 bool make_map_u16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows,
                   uint32_t box_rows) {
@@ -187,16 +170,14 @@ __global__ void ingest_rows_bits_kernel(const uint16_t* __restrict__ src, int64_
 }
 
 // Stored rows [row0, row0 + n) in storage precision without padding: fp32
-// rows as hi + lo (exactly the ingested value), 16-bit rows bit for bit.
-__global__ void export_rows_f32_kernel(const float* __restrict__ db_hi, const float* __restrict__ db_lo,
-                                       int64_t row0, int64_t n, int dim, int d_pad,
-                                       float* __restrict__ out) {
+// rows as ingested, 16-bit rows bit for bit.
+__global__ void export_rows_f32_kernel(const float* __restrict__ db_x, int64_t row0, int64_t n,
+                                       int dim, int d_pad, float* __restrict__ out) {
     const int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (e >= n * dim) return;
     const int64_t r = e / dim;
     const int c = static_cast<int>(e - r * dim);
-    const int64_t o = (row0 + r) * d_pad + c;
-    out[e] = db_hi[o] + db_lo[o];
+    out[e] = db_x[(row0 + r) * d_pad + c];
 }
 
 __global__ void export_rows_bits_kernel(const uint16_t* __restrict__ db, int64_t row0, int64_t n,
@@ -238,24 +219,30 @@ __global__ void prep_queries_half_kernel(const float* __restrict__ src, int m, i
     qsq[i] = static_cast<float>(s2);
 }
 
-__device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
-    hi = __uint_as_float(f32_to_tf32_rna(x));
-    lo = x - hi;   // exact: lo = x - tf32(x) has at most 13 significant bits
+// x ~ h + l: h = bf16(x), l = bf16(x - h), both round to nearest (x - h is
+// exact in fp32); |x - h - l| <= 2^-8 |x - h| <= 2^-16 |x|.
+__device__ __forceinline__ void split_bf16(float x, uint16_t& h, uint16_t& l) {
+    const __nv_bfloat16 hb = __float2bfloat16_rn(x);
+    h = __bfloat16_as_ushort(hb);
+    l = __bfloat16_as_ushort(__float2bfloat16_rn(x - __bfloat162float(hb)));
 }
 
 // One thread per row: optional Cosine normalisation (src/Distance.h:50-60),
-// squared norm with double accumulation (Distance.h:40-47), tf32 split,
-// zero padding to d_pad, score bias and running max row norm.
-// `normalize` = 0 for rows that are already stored values (a reloaded index).
+// squared norm with double accumulation (Distance.h:40-47), the stored fp32
+// row and its bf16 split planes, zero padding to d_pad, score bias and running
+// max row norm.  `normalize` = 0 for rows that are already stored values (a
+// reloaded index).
 __global__ void ingest_rows_kernel(const float* __restrict__ src, int64_t n, int dim, int d_pad,
-                                   int metric, int normalize, int64_t row0, float* __restrict__ db_hi,
-                                   float* __restrict__ db_lo, float* __restrict__ colbias,
-                                   float* __restrict__ dnorm, unsigned* xmax_bits) {
+                                   int metric, int normalize, int64_t row0, float* __restrict__ db_x,
+                                   uint16_t* __restrict__ db_h, uint16_t* __restrict__ db_l,
+                                   float* __restrict__ colbias, float* __restrict__ dnorm,
+                                   unsigned* xmax_bits) {
     const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (i >= n) return;
     const float* row = src + i * dim;
-    float* oh = db_hi + (row0 + i) * d_pad;
-    float* ol = db_lo + (row0 + i) * d_pad;
+    float* ox = db_x + (row0 + i) * d_pad;
+    uint16_t* oh = db_h + (row0 + i) * d_pad;
+    uint16_t* ol = db_l + (row0 + i) * d_pad;
     float inv = 1.0f;
     bool scale = false;
     if (metric == kCosine && normalize) {
@@ -267,12 +254,13 @@ __global__ void ingest_rows_kernel(const float* __restrict__ src, int64_t n, int
     for (int c = 0; c < dim; ++c) {
         const float x = scale ? row[c] * inv : row[c];
         s2 += static_cast<double>(x) * x;
-        float h, l;
-        split_tf32(x, h, l);
+        uint16_t h, l;
+        split_bf16(x, h, l);
+        ox[c] = x;
         oh[c] = h;
         ol[c] = l;
     }
-    for (int c = dim; c < d_pad; ++c) { oh[c] = 0.0f; ol[c] = 0.0f; }
+    for (int c = dim; c < d_pad; ++c) { ox[c] = 0.0f; oh[c] = 0; ol[c] = 0; }
     const float dn = static_cast<float>(s2);
     dnorm[row0 + i] = dn;
     colbias[row0 + i] = metric == kL2 ? -dn : 0.0f;
@@ -280,17 +268,19 @@ __global__ void ingest_rows_kernel(const float* __restrict__ src, int64_t n, int
     atomicMax(xmax_bits, __float_as_uint(nrm));
 }
 
-// One thread per padded query row: Cosine normalisation, tf32 split, ||q||
-// (rounded up) for the error bound.  Rows >= m are zero.
+// One thread per padded query row: Cosine normalisation, the fp32 query and
+// its bf16 split, ||q|| (rounded up) for the error bound.  Rows >= m are zero.
 __global__ void prep_queries_kernel(const float* __restrict__ src, int m, int m_pad, int dim,
-                                    int d_pad, int metric, float* __restrict__ q_hi,
-                                    float* __restrict__ q_lo, float* __restrict__ qnorm) {
+                                    int d_pad, int metric, float* __restrict__ q_x,
+                                    uint16_t* __restrict__ q_h, uint16_t* __restrict__ q_l,
+                                    float* __restrict__ qnorm) {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= m_pad) return;
-    float* oh = q_hi + static_cast<int64_t>(i) * d_pad;
-    float* ol = q_lo + static_cast<int64_t>(i) * d_pad;
+    float* ox = q_x + static_cast<int64_t>(i) * d_pad;
+    uint16_t* oh = q_h + static_cast<int64_t>(i) * d_pad;
+    uint16_t* ol = q_l + static_cast<int64_t>(i) * d_pad;
     if (i >= m) {
-        for (int c = 0; c < d_pad; ++c) { oh[c] = 0.0f; ol[c] = 0.0f; }
+        for (int c = 0; c < d_pad; ++c) { ox[c] = 0.0f; oh[c] = 0; ol[c] = 0; }
         qnorm[i] = 0.0f;
         return;
     }
@@ -306,12 +296,13 @@ __global__ void prep_queries_kernel(const float* __restrict__ src, int m, int m_
     for (int c = 0; c < dim; ++c) {
         const float x = scale ? row[c] * inv : row[c];
         s2 += static_cast<double>(x) * x;
-        float h, l;
-        split_tf32(x, h, l);
+        uint16_t h, l;
+        split_bf16(x, h, l);
+        ox[c] = x;
         oh[c] = h;
         ol[c] = l;
     }
-    for (int c = dim; c < d_pad; ++c) { oh[c] = 0.0f; ol[c] = 0.0f; }
+    for (int c = dim; c < d_pad; ++c) { ox[c] = 0.0f; oh[c] = 0; ol[c] = 0; }
     qnorm[i] = static_cast<float>(sqrt(s2) * (1.0 + 1e-7));
 }
 
@@ -330,34 +321,49 @@ cudaError_t grow(mflat_cu_index* ix, int64_t need) {
     cudaStream_t st = ix->stream;
     int64_t cap = std::max<int64_t>(need, ix->cap + ix->cap / 2);
     cap = (cap + kBN - 1) / kBN * kBN;
-    float *h = nullptr, *l = nullptr, *cb = nullptr, *dn = nullptr;
+    // fp32 storage: x (4 B) + h, l (2 B each) per element; 16-bit: one plane
+    void *x = nullptr, *h = nullptr, *l = nullptr;
+    float *cb = nullptr, *dn = nullptr;
     const bool half = ix->storage != 0;
-    const size_t rowb = static_cast<size_t>(ix->d_pad) * (half ? 2 : sizeof(float));
+    const size_t row16 = static_cast<size_t>(ix->d_pad) * 2;
+    const size_t row32 = static_cast<size_t>(ix->d_pad) * sizeof(float);
     cudaError_t e;
-    if ((e = cudaMalloc(&h, cap * rowb)) != cudaSuccess) goto bad;
-    if (!half && (e = cudaMalloc(&l, cap * rowb)) != cudaSuccess) goto bad;
+    if ((e = cudaMalloc(&h, cap * row16)) != cudaSuccess) goto bad;
+    if (!half && (e = cudaMalloc(&l, cap * row16)) != cudaSuccess) goto bad;
+    if (!half && (e = cudaMalloc(&x, cap * row32)) != cudaSuccess) goto bad;
     if ((e = cudaMalloc(&cb, cap * sizeof(float))) != cudaSuccess) goto bad;
     if ((e = cudaMalloc(&dn, cap * sizeof(float))) != cudaSuccess) goto bad;
     if (ix->n > 0) {
-        cudaMemcpyAsync(h, half ? ix->db16 : static_cast<void*>(ix->db_hi), ix->n * rowb,
+        cudaMemcpyAsync(h, half ? ix->db16 : static_cast<void*>(ix->db_h), ix->n * row16,
                         cudaMemcpyDeviceToDevice, st);
-        if (!half) cudaMemcpyAsync(l, ix->db_lo, ix->n * rowb, cudaMemcpyDeviceToDevice, st);
+        if (!half) {
+            cudaMemcpyAsync(l, ix->db_l, ix->n * row16, cudaMemcpyDeviceToDevice, st);
+            cudaMemcpyAsync(x, ix->db_x, ix->n * row32, cudaMemcpyDeviceToDevice, st);
+        }
         cudaMemcpyAsync(cb, ix->colbias, ix->n * sizeof(float), cudaMemcpyDeviceToDevice, st);
         cudaMemcpyAsync(dn, ix->dnorm, ix->n * sizeof(float), cudaMemcpyDeviceToDevice, st);
     }
     fill_f32_kernel<<<blocks_for(cap - ix->n, 256), 256, 0, st>>>(cb + ix->n, cap - ix->n, -kInf);
     if ((e = cudaStreamSynchronize(st)) != cudaSuccess) goto bad;
-    cudaFree(half ? ix->db16 : static_cast<void*>(ix->db_hi));
-    cudaFree(ix->db_lo);
+    cudaFree(ix->db16);
+    cudaFree(ix->db_h);
+    cudaFree(ix->db_l);
+    cudaFree(ix->db_x);
     cudaFree(ix->colbias);
     cudaFree(ix->dnorm);
-    if (half) ix->db16 = h; else ix->db_hi = h;
-    ix->db_lo = l;
+    if (half) {
+        ix->db16 = h;
+    } else {
+        ix->db_h = static_cast<uint16_t*>(h);
+        ix->db_l = static_cast<uint16_t*>(l);
+        ix->db_x = static_cast<float*>(x);
+    }
     ix->colbias = cb;
     ix->dnorm = dn;
     ix->cap = cap;
     return cudaSuccess;
 bad:
+    cudaFree(x);
     cudaFree(h);
     cudaFree(l);
     cudaFree(cb);
@@ -382,21 +388,22 @@ int kp_for(int k) { return k <= 21 ? 32 : 0; }
 
 // Bytes of one 256-row database tile as the screens read it.
 size_t tile_bytes(const mflat_cu_index* ix) {
-    return static_cast<size_t>(kBN) * ix->d_pad * (ix->storage != 0 ? 2 : 8);
+    return static_cast<size_t>(kBN) * ix->d_pad * (ix->storage != 0 ? 2 : 4);
 }
 
 }  // namespace
 
 // Entry points for other translation units of this library (noalloc.cu).
-bool encode_map_f32(CUtensorMap* map, const float* base, uint64_t inner, uint64_t rows,
-                    uint32_t box_rows) {
-    return make_map_f32(map, base, inner, rows, box_rows);
+bool encode_map_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows,
+                     uint32_t box_rows) {
+    return make_map_u16(map, base, inner, rows, box_rows);
 }
 
 cudaError_t launch_prep_queries(const float* src, int m, int m_pad, int dim, int d_pad, int metric,
-                                float* q_hi, float* q_lo, float* qnorm, cudaStream_t st) {
+                                float* q_x, uint16_t* q_h, uint16_t* q_l, float* qnorm,
+                                cudaStream_t st) {
     prep_queries_kernel<<<blocks_for(m_pad, 128), 128, 0, st>>>(src, m, m_pad, dim, d_pad, metric,
-                                                                q_hi, q_lo, qnorm);
+                                                                q_x, q_h, q_l, qnorm);
     return cudaGetLastError();
 }
 
@@ -424,6 +431,21 @@ int check_device_error(mflat_cu_index* ix, cudaStream_t st) {
     return ST_OK;
 }
 
+// The fp32-storage screen over sp's query batch (bf16 planes in ix->q_h /
+// ix->q_l, rows in ix->db_h / ix->db_l), or the CUDA-core cross-check.
+cudaError_t launch_fp32_screen(mflat_cu_index* ix, const ScreenParams& sp, int kp, cudaStream_t st) {
+    if (ix->force_simt) return launch_screen_simt(kp, sp, st);
+    CUtensorMap ta_h, ta_l, tb_h, tb_l;
+    if (!make_map_u16(&ta_h, ix->q_h.p, sp.d_pad, sp.m_pad, kBM) ||
+        !make_map_u16(&ta_l, ix->q_l.p, sp.d_pad, sp.m_pad, kBM) ||
+        !make_map_u16(&tb_h, ix->db_h, sp.d_pad, ix->n, kBN) ||
+        !make_map_u16(&tb_l, ix->db_l, sp.d_pad, ix->n, kBN))
+        return cudaErrorInvalidValue;
+    const int64_t units = static_cast<int64_t>(sp.n_qtiles) * sp.n_chunks;
+    const int grid = static_cast<int>(std::min<int64_t>(units, ix->num_sms));
+    return launch_screen_bf16x3(kp, ta_h, ta_l, tb_h, tb_l, sp, grid, st);
+}
+
 int run_screen(mflat_cu_index* ix, const float* queries, int m, int kp, int on_device,
                cudaStream_t st, ScreenRun& out, int max_chunks) {
     const int m_pad = (m + kBM - 1) / kBM * kBM;
@@ -441,8 +463,9 @@ int run_screen(mflat_cu_index* ix, const float* queries, int m, int kp, int on_d
                "query upload");
         qsrc = ix->q_in.as<float>();
     }
-    CU_TRY(ix->q_hi.ensure(static_cast<size_t>(m_pad) * d_pad * sizeof(float)), "query split");
-    CU_TRY(ix->q_lo.ensure(static_cast<size_t>(m_pad) * d_pad * sizeof(float)), "query split");
+    CU_TRY(ix->q_x.ensure(static_cast<size_t>(m_pad) * d_pad * sizeof(float)), "query buffer");
+    CU_TRY(ix->q_h.ensure(static_cast<size_t>(m_pad) * d_pad * 2), "query split");
+    CU_TRY(ix->q_l.ensure(static_cast<size_t>(m_pad) * d_pad * 2), "query split");
     CU_TRY(ix->qnorm.ensure(static_cast<size_t>(m_pad) * sizeof(float)), "query norms");
     const size_t parts = static_cast<size_t>(n_chunks) * m_pad * kp;
     CU_TRY(ix->part_s.ensure(parts * sizeof(float)), "candidate lists");
@@ -451,10 +474,9 @@ int run_screen(mflat_cu_index* ix, const float* queries, int m, int kp, int on_d
     CU_TRY(cudaMemsetAsync(ix->thr.p, 0, static_cast<size_t>(m_pad) * sizeof(uint32_t), st), "floors");
 
     if (ix->timing) cudaEventRecord(ix->ev[0], st);
-    prep_queries_kernel<<<blocks_for(m_pad, 128), 128, 0, st>>>(
-        qsrc, m, m_pad, ix->dim, d_pad, ix->metric, ix->q_hi.as<float>(), ix->q_lo.as<float>(),
-        ix->qnorm.as<float>());
-    CU_TRY(cudaGetLastError(), "query prep launch");
+    CU_TRY(launch_prep_queries(qsrc, m, m_pad, ix->dim, d_pad, ix->metric, ix->q_x.as<float>(),
+                               ix->q_h.as<uint16_t>(), ix->q_l.as<uint16_t>(), ix->qnorm.as<float>(), st),
+           "query prep launch");
 
     ScreenParams sp{};
     sp.m = m;
@@ -473,35 +495,18 @@ int run_screen(mflat_cu_index* ix, const float* queries, int m, int kp, int on_d
     sp.thr = ix->thr.as<uint32_t>();
     sp.tile_stride = 1;
     sp.use_floor = 1;
-    sp.q_hi = ix->q_hi.as<float>();
-    sp.q_lo = ix->q_lo.as<float>();
-    sp.db_hi = ix->db_hi;
-    sp.db_lo = ix->db_lo;
+    sp.q_x = ix->q_x.as<float>();
+    sp.db_x = ix->db_x;
 
     if (ix->timing) cudaEventRecord(ix->ev[1], st);
-    cudaError_t le;
-    if (ix->force_simt) {
-        le = launch_screen_simt(kp, sp, st);
-    } else {
-        CUtensorMap ta_hi, ta_lo, tb_hi, tb_lo;
-        if (!make_map_f32(&ta_hi, sp.q_hi, d_pad, m_pad, kBM) ||
-            !make_map_f32(&ta_lo, sp.q_lo, d_pad, m_pad, kBM) ||
-            !make_map_f32(&tb_hi, ix->db_hi, d_pad, ix->n, kBN) ||
-            !make_map_f32(&tb_lo, ix->db_lo, d_pad, ix->n, kBN))
-            return fail(ST_DEVICE, "tensor map encoding failed");
-        const int64_t units = static_cast<int64_t>(n_qtiles) * n_chunks;
-        const int grid = static_cast<int>(std::min<int64_t>(units, ix->num_sms));
-        le = launch_screen_tf32x3(kp, ta_hi, ta_lo, tb_hi, tb_lo, sp, grid, st);
-    }
-    CU_TRY(le, "screen launch");
+    CU_TRY(launch_fp32_screen(ix, sp, kp, st), "screen launch");
     if (ix->timing) cudaEventRecord(ix->ev[2], st);
 
     out.kp = kp;
     out.m = m;
     out.m_pad = m_pad;
     out.n_chunks = n_chunks;
-    out.q_hi = sp.q_hi;
-    out.q_lo = sp.q_lo;
+    out.q_x = sp.q_x;
     out.qnorm = ix->qnorm.as<float>();
     out.part_s = sp.part_score;
     out.part_i = sp.part_id;
@@ -578,16 +583,7 @@ int estimate_floor(mflat_cu_index* ix, const LargePlan& P, const ScreenParams& b
 }
 
 cudaError_t launch_pass(mflat_cu_index* ix, const ScreenParams& sp, int kp, cudaStream_t st) {
-    if (ix->force_simt) return launch_screen_simt(kp, sp, st);
-    CUtensorMap ta_hi, ta_lo, tb_hi, tb_lo;
-    if (!make_map_f32(&ta_hi, sp.q_hi, sp.d_pad, sp.m_pad, kBM) ||
-        !make_map_f32(&ta_lo, sp.q_lo, sp.d_pad, sp.m_pad, kBM) ||
-        !make_map_f32(&tb_hi, ix->db_hi, sp.d_pad, ix->n, kBN) ||
-        !make_map_f32(&tb_lo, ix->db_lo, sp.d_pad, ix->n, kBN))
-        return cudaErrorInvalidValue;
-    const int64_t units = static_cast<int64_t>(sp.n_qtiles) * sp.n_chunks;
-    const int grid = static_cast<int>(std::min<int64_t>(units, ix->num_sms));
-    return launch_screen_tf32x3(kp, ta_hi, ta_lo, tb_hi, tb_lo, sp, grid, st);
+    return launch_fp32_screen(ix, sp, kp, st);
 }
 
 }  // namespace
@@ -607,8 +603,9 @@ int search_large(mflat_cu_index* ix, const float* queries, int m, int k_out, int
         qsrc = ix->q_in.as<float>();
     }
     const int bm_pad = (P.batch + kBM - 1) / kBM * kBM;
-    CU_TRY(ix->q_hi.ensure(static_cast<size_t>(bm_pad) * d_pad * sizeof(float)), "query split");
-    CU_TRY(ix->q_lo.ensure(static_cast<size_t>(bm_pad) * d_pad * sizeof(float)), "query split");
+    CU_TRY(ix->q_x.ensure(static_cast<size_t>(bm_pad) * d_pad * sizeof(float)), "query buffer");
+    CU_TRY(ix->q_h.ensure(static_cast<size_t>(bm_pad) * d_pad * 2), "query split");
+    CU_TRY(ix->q_l.ensure(static_cast<size_t>(bm_pad) * d_pad * 2), "query split");
     CU_TRY(ix->qnorm.ensure(static_cast<size_t>(bm_pad) * sizeof(float)), "query norms");
     CU_TRY(ix->thr.ensure(static_cast<size_t>(bm_pad) * sizeof(uint32_t)), "floors");
     CU_TRY(ix->buf_cnt.ensure(static_cast<size_t>(bm_pad) * sizeof(uint32_t)), "buffer counts");
@@ -635,8 +632,8 @@ int search_large(mflat_cu_index* ix, const float* queries, int m, int k_out, int
         const int mb = std::min(P.batch, m - b0);
         const int mb_pad = (mb + kBM - 1) / kBM * kBM;
         CU_TRY(launch_prep_queries(qsrc + static_cast<int64_t>(b0) * ix->dim, mb, mb_pad, ix->dim,
-                                   d_pad, ix->metric, ix->q_hi.as<float>(), ix->q_lo.as<float>(),
-                                   ix->qnorm.as<float>(), st),
+                                   d_pad, ix->metric, ix->q_x.as<float>(), ix->q_h.as<uint16_t>(),
+                                   ix->q_l.as<uint16_t>(), ix->qnorm.as<float>(), st),
                "query prep launch");
         CU_TRY(cudaMemsetAsync(ix->thr.p, 0, static_cast<size_t>(mb_pad) * sizeof(uint32_t), st), "floors");
         CU_TRY(cudaMemsetAsync(ix->buf_cnt.p, 0, static_cast<size_t>(mb_pad) * sizeof(uint32_t), st), "counts");
@@ -653,10 +650,8 @@ int search_large(mflat_cu_index* ix, const float* queries, int m, int k_out, int
         sp.colbias = ix->colbias;
         sp.err = ix->err;
         sp.thr = ix->thr.as<uint32_t>();
-        sp.q_hi = ix->q_hi.as<float>();
-        sp.q_lo = ix->q_lo.as<float>();
-        sp.db_hi = ix->db_hi;
-        sp.db_lo = ix->db_lo;
+        sp.q_x = ix->q_x.as<float>();
+        sp.db_x = ix->db_x;
         sp.buf_cnt = ix->buf_cnt.as<uint32_t>();
         sp.buf_s = ix->buf_s.as<float>();
         sp.buf_i = ix->buf_i.as<int32_t>();
@@ -691,11 +686,9 @@ int search_large(mflat_cu_index* ix, const float* queries, int m, int k_out, int
         ls.buf_i = sp.buf_i;
         ls.cap = P.cap;
         ls.exact = 1;
-        ls.q_hi = sp.q_hi;
-        ls.q_lo = sp.q_lo;
+        ls.q_x = sp.q_x;
         ls.qnorm = ix->qnorm.as<float>();
-        ls.db_hi = ix->db_hi;
-        ls.db_lo = ix->db_lo;
+        ls.db_x = ix->db_x;
         ls.xmax_bits = ix->xmax_bits;
         ls.gamma = screen_gamma(d_pad);
         ls.id_base = ix->world > 1 ? ix->id_base : 0;
@@ -963,7 +956,7 @@ int index_add(mflat_cu_index_t* ix, const void* vectors, int64_t n, int on_devic
         else
             ingest_rows_kernel<<<blocks_for(cnt, 128), 128, 0, ix->stream>>>(
                 static_cast<const float*>(src), cnt, ix->dim, ix->d_pad, ix->metric, raw ? 0 : 1,
-                ix->n + off, ix->db_hi, ix->db_lo, ix->colbias, ix->dnorm, ix->xmax_bits);
+                ix->n + off, ix->db_x, ix->db_h, ix->db_l, ix->colbias, ix->dnorm, ix->xmax_bits);
         CU_TRY(cudaGetLastError(), "ingest launch");
         if (!on_device) CU_TRY(cudaStreamSynchronize(ix->stream), "ingest");
     }
@@ -1002,11 +995,9 @@ int search_list_exact(mflat_cu_index* ix, const float* queries, int m, int k_out
     sel.n = ix->n;
     sel.part_score = run.part_s;
     sel.part_id = run.part_i;
-    sel.q_hi = run.q_hi;
-    sel.q_lo = run.q_lo;
+    sel.q_x = run.q_x;
     sel.qnorm = run.qnorm;
-    sel.db_hi = ix->db_hi;
-    sel.db_lo = ix->db_lo;
+    sel.db_x = ix->db_x;
     sel.xmax_bits = ix->xmax_bits;
     sel.gamma = screen_gamma(ix->d_pad);
     sel.id_base = ix->world > 1 ? ix->id_base : 0;
@@ -1113,8 +1104,9 @@ int mflat_cu_index_create(int device, int dim, int metric, int storage, mflat_cu
     if (!ix) return fail(ST_ALLOC, "host allocation failed");
     ix->device = device;
     ix->dim = dim;
-    // one 128-byte k-block = 32 fp32 or 64 16-bit elements
-    ix->d_pad = storage == 0 ? (dim + kBK - 1) / kBK * kBK : (dim + 63) / 64 * 64;
+    // one 128-byte k-block = 64 16-bit elements (the fp32 storage's screen
+    // planes are bf16 too)
+    ix->d_pad = (dim + kBK - 1) / kBK * kBK;
     ix->metric = (metric == kIP || metric == kCosine) ? metric : kL2;
     ix->storage = storage;
     cudaDeviceGetAttribute(&ix->num_sms, cudaDevAttrMultiProcessorCount, device);
@@ -1146,15 +1138,16 @@ void mflat_cu_index_destroy(mflat_cu_index_t* ix) {
     if (ix->stream) cudaStreamSynchronize(ix->stream);
     comm_release(ix);
     cudaFree(ix->db16);
-    cudaFree(ix->db_hi);
-    cudaFree(ix->db_lo);
+    cudaFree(ix->db_x);
+    cudaFree(ix->db_h);
+    cudaFree(ix->db_l);
     cudaFree(ix->colbias);
     cudaFree(ix->dnorm);
     cudaFree(ix->xmax_bits);
     cudaFree(ix->err);
     cudaFree(ix->flag_count);
     if (ix->host_words) cudaFreeHost(ix->host_words);
-    for (DevBuf* b : {&ix->stage_in, &ix->q_in, &ix->q_hi, &ix->q_lo, &ix->qnorm, &ix->part_s,
+    for (DevBuf* b : {&ix->stage_in, &ix->q_in, &ix->q_x, &ix->q_h, &ix->q_l, &ix->qnorm, &ix->part_s,
                       &ix->part_i, &ix->flag_list, &ix->out_ids, &ix->out_dist, &ix->gather_ids,
                       &ix->gather_dist, &ix->merge_tmp_ids, &ix->merge_tmp_dist, &ix->thr, &ix->thr_stat, &ix->fb_s,
                       &ix->fb_i, &ix->buf_cnt, &ix->buf_s, &ix->buf_i, &ix->lk_words,
@@ -1196,7 +1189,7 @@ int mflat_cu_index_export_rows(mflat_cu_index_t* ix, int64_t start, int64_t coun
                 ix->stage_in.as<uint16_t>());
         else
             export_rows_f32_kernel<<<blocks_for(elems, 256), 256, 0, ix->stream>>>(
-                ix->db_hi, ix->db_lo, start + off, cnt, ix->dim, ix->d_pad, ix->stage_in.as<float>());
+                ix->db_x, start + off, cnt, ix->dim, ix->d_pad, ix->stage_in.as<float>());
         CU_TRY(cudaGetLastError(), "export launch");
         CU_TRY(cudaMemcpyAsync(static_cast<uint8_t*>(host_out) + off * ix->dim * elem, ix->stage_in.p,
                                static_cast<size_t>(elems) * elem, cudaMemcpyDeviceToHost, ix->stream),

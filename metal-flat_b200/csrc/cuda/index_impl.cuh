@@ -59,8 +59,7 @@ inline unsigned blocks_for(int64_t n, int t) { return static_cast<unsigned>((n +
 // Result of the screen stage of one search (per (query, chunk) top-KP lists).
 struct ScreenRun {
     int kp = 0, m = 0, m_pad = 0, n_chunks = 0;
-    const float* q_hi = nullptr;
-    const float* q_lo = nullptr;
+    const float* q_x = nullptr;       // fp32 queries [m_pad][d_pad] (exact re-rank)
     const float* qnorm = nullptr;
     const float* part_s = nullptr;
     const int32_t* part_i = nullptr;
@@ -76,8 +75,9 @@ struct mflat_cu_index {
     cudaStream_t stream = nullptr;
     int64_t n = 0, cap = 0;
     void* db16 = nullptr;         // fp16 / bf16 storage: [cap][d_pad] 16-bit
-    float* db_hi = nullptr;       // [cap][d_pad]
-    float* db_lo = nullptr;
+    float* db_x = nullptr;        // fp32 storage: the rows [cap][d_pad]
+    uint16_t* db_h = nullptr;     // fp32 storage: bf16 screen planes [cap][d_pad]
+    uint16_t* db_l = nullptr;
     float* colbias = nullptr;     // [cap], -inf past n
     float* dnorm = nullptr;       // [cap]
     unsigned* xmax_bits = nullptr;
@@ -85,7 +85,7 @@ struct mflat_cu_index {
     int* flag_count = nullptr;    // queries routed to the exact full scan
     int* host_words = nullptr;    // pinned: [0] err, [4..7] status words, [8 + slot] fallback
                                   // query count of timing slot `slot`
-    mflat_cu::DevBuf stage_in, q_in, q_hi, q_lo, qnorm, part_s, part_i, flag_list, out_ids, out_dist;
+    mflat_cu::DevBuf stage_in, q_in, q_x, q_h, q_l, qnorm, part_s, part_i, flag_list, out_ids, out_dist;
     mflat_cu::DevBuf thr, thr_stat, fb_s, fb_i;
     mflat_cu::DevBuf buf_cnt, buf_s, buf_i, lk_words;   // large-k candidate buffers
     mflat_cu::DevBuf q16, qsq;                          // 16-bit queries, ||q||^2
@@ -140,10 +140,11 @@ cudaError_t launch_merge_ranks(const int32_t* gids, const float* gdist, int worl
 // Synchronise `st`; with a communicator attached, watch it for peer failure.
 int wait_stream_checked(mflat_cu_index* ix, cudaStream_t st);
 const char* last_error_message();
-bool encode_map_f32(CUtensorMap* map, const float* base, uint64_t inner, uint64_t rows,
-                    uint32_t box_rows);
 cudaError_t launch_prep_queries(const float* src, int m, int m_pad, int dim, int d_pad, int metric,
-                                float* q_hi, float* q_lo, float* qnorm, cudaStream_t st);
+                                float* q_x, uint16_t* q_h, uint16_t* q_l, float* qnorm,
+                                cudaStream_t st);
+bool encode_map_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows,
+                     uint32_t box_rows);
 cudaError_t launch_fill_empty(int32_t* ids, float* dist, int64_t n, float v, cudaStream_t st);
 void plan_screen_chunks(int n_qtiles, int n_tiles, int num_sms, int max_chunks, int& n_chunks,
                         int& tiles_per_chunk);

@@ -1,20 +1,23 @@
 // kernels.cuh -- shared layouts, parameter blocks and device helpers of the
 // flat-search kernels.
 //
-// Data layout in HBM (one index on one device):
-//   db_hi, db_lo : float [cap][d_pad]  rows split as x = hi + lo exactly, with
-//                  hi = tf32(x) (round-to-nearest) and lo = x - hi; d_pad is
-//                  dim rounded up to 32 (one 128-byte TMA/UMMA k-block), the
-//                  padding is zero.  hi + lo reproduces the stored fp32 row
-//                  bit-for-bit for the exact fp64 re-rank.
+// Data layout in HBM (one index on one device), fp32 storage:
+//   db_x         : float [cap][d_pad]     the stored rows (exact fp32; Cosine
+//                  rows normalised), read by the exact fp64 re-rank;
+//   db_h, db_l   : bf16  [cap][d_pad]     screen planes, x = h + l + r with
+//                  h = bf16(x), l = bf16(x - h) (round to nearest) and
+//                  |r| <= 2^-16 |x|; d_pad is dim rounded up to 64 (one
+//                  128-byte TMA/UMMA k-block of 16-bit elements), the padding
+//                  is zero.
 //   colbias      : float [cap]        per-row additive term of the screen
 //                  score: -||x||^2 (L2) or 0 (IP / Cosine); -inf past n, so a
 //                  ragged last tile can never enter a top-k list.
 //   xmax_bits    : uint  [1]          bits of max_i ||x_i|| (error bound).
-//   q_hi, q_lo   : float [m_pad][d_pad] split queries (same rule), zero rows
-//                  past m; qnorm: float [m] = ||q|| (for the error bound).
+//   q_x, q_h, q_l: the queries in the same three forms ([m_pad][d_pad], zero
+//                  rows past m); qnorm: float [m] = ||q|| (error bound).
 //   part_score/part_id : [n_chunks][m_pad][KP] per (query, db chunk) top-KP
 //                  lists of the screen, sorted by (score desc, id asc).
+// fp16 / bf16 storage keeps one 16-bit plane (db16, q16) instead.
 //
 // Screen score (larger = nearer, reference src/Distance.h:65-69):
 //   L2 : s = 2 q.x - ||x||^2      (= ||q||^2 - ||q - x||^2, ||q||^2 dropped)
@@ -29,25 +32,30 @@
 
 namespace mflat_cu {
 
-constexpr int kBK = 32;           // fp32 elements per k-block (128 bytes)
-constexpr int kMaxDPadResident = 128;   // A (queries) kept resident in smem up to this
+constexpr int kBK = 64;           // 16-bit elements per k-block (128 bytes)
+constexpr int kMaxDPadResident = 256;   // A (queries) kept resident in smem up to this
 constexpr int kSelectMaxThreads = 256;   // one select thread per list
 constexpr int kFbChunks = 64;     // database chunks of the exact fallback scan
 
 enum Metric : int { kL2 = 0, kIP = 1, kCosine = 2 };
 
-// Relative error bound gamma of a screen dot product over d_pad elements:
-// |dot' - q.x| <= gamma * ||q|| * ||x||.  3xTF32: split error 2.5 * 2^-21 per
-// product plus fp32 accumulation of 3 * d_pad products, with an 8x safety
-// factor on the latter.
+// Relative error bound gamma of the fp32-storage screen dot product over d_pad
+// elements: |dot' - q.x| <= gamma * ||q|| * ||x||.  The screen sums
+// q_h x_h + q_l x_h + q_h x_l (3 x bf16, each product exact in fp32); what
+// the split leaves out of q_i x_i (the dropped q_l x_l and the residues r of
+// both operands) is about 3 * 2^-16 |q_i x_i|, bounded here by 4 * 2^-16, and
+// the fp32 accumulation of 3 * d_pad products adds (3 * d_pad + 16) * 2^-24,
+// taken with an 8x safety factor since the tensor core's summation order
+// and rounding are not specified.  Sum |q_i x_i| <= ||q|| ||x|| (Cauchy-Schwarz).
 inline float screen_gamma(int d_pad) {
-    return static_cast<float>((3.0 * d_pad + 16.0) * 4.76837158203125e-07);   // 2^-21
+    return static_cast<float>(4.0 * 1.52587890625e-05 +                 // 4 * 2^-16
+                              (3.0 * d_pad + 16.0) * 4.76837158203125e-07);   // 8 * 2^-24
 }
 
 struct ScreenParams {
     int m;                 // queries
     int m_pad;             // multiple of kBM
-    int d_pad;             // multiple of kBK
+    int d_pad;             // multiple of kBK (64)
     int64_t n;             // database rows
     int n_tiles;           // ceil(n / kBN)
     int n_qtiles;          // m_pad / kBM
@@ -70,9 +78,9 @@ struct ScreenParams {
     float* buf_s;
     int32_t* buf_i;
     uint32_t cap;
-    // SIMT path only
-    const float* q_hi; const float* q_lo;
-    const float* db_hi; const float* db_lo;
+    // SIMT path only: the fp32 queries and rows
+    const float* q_x;
+    const float* db_x;
 };
 
 struct SelectParams {
@@ -80,8 +88,8 @@ struct SelectParams {
     int m, m_pad, dim, d_pad, k_out, n_chunks, metric;
     int64_t n;
     const float* part_score; const int32_t* part_id;
-    const float* q_hi; const float* q_lo; const float* qnorm;
-    const float* db_hi; const float* db_lo;
+    const float* q_x; const float* qnorm;     // fp32 queries [m_pad][d_pad], ||q||
+    const float* db_x;                        // fp32 rows [n][d_pad]
     const unsigned* xmax_bits;
     float gamma;           // relative dot-product error bound of the screen
     int64_t id_base;       // added to every returned id (row sharding)
@@ -96,8 +104,8 @@ struct LargeSelectParams {
     const uint32_t* cnt; const float* buf_s; const int32_t* buf_i; uint32_t cap;
     const uint32_t* thr;                  // floor keys used by the screen
     int exact;                            // 1: fp64 re-rank of the proven window
-    const float* q_hi; const float* q_lo; const float* qnorm;
-    const float* db_hi; const float* db_lo;
+    const float* q_x; const float* qnorm;
+    const float* db_x;
     const unsigned* xmax_bits; float gamma;
     const float* qsq;                     // recall path: ||q||^2 for L2 distances
     int64_t id_base;
@@ -144,8 +152,9 @@ __device__ __forceinline__ bool cand_better(float sa, int ia, float sb, int ib) 
 // ------------------------------------------------------------- launchers
 // All launchers enqueue on `stream` and return the launch status.
 // kp = 0 selects buffer mode (append every score above the floor).
-cudaError_t launch_screen_tf32x3(int kp, const CUtensorMap& a_hi, const CUtensorMap& a_lo,
-                                 const CUtensorMap& b_hi, const CUtensorMap& b_lo,
+// fp32 storage: bf16 planes (a_h / a_l: queries, b_h / b_l: rows), 3 x bf16.
+cudaError_t launch_screen_bf16x3(int kp, const CUtensorMap& a_h, const CUtensorMap& a_l,
+                                 const CUtensorMap& b_h, const CUtensorMap& b_l,
                                  const ScreenParams& p, int grid, cudaStream_t stream);
 cudaError_t launch_screen_simt(int kp, const ScreenParams& p, cudaStream_t stream);
 // fp16 / bf16 storage (q and db in 16-bit, d_pad a multiple of 64); kp 0 =
@@ -155,7 +164,7 @@ cudaError_t launch_screen_f16(int kp, bool bf16, const CUtensorMap& a, const CUt
 int screen_f16_smem_bytes(int d_pad);
 cudaError_t launch_select_exact(int kp, const SelectParams& p, cudaStream_t stream);
 cudaError_t launch_fallback_exact(const SelectParams& p, int grid, cudaStream_t stream);
-int screen_tf32x3_smem_bytes(int d_pad);
+int screen_bf16x3_smem_bytes(int d_pad);
 cudaError_t launch_select_large(const LargeSelectParams& p, cudaStream_t stream);
 // Recall path, list mode: merge n_lists lists per query, write the top k_out
 // with screen distances (L2: max(0, ||q||^2 - s); IP / Cosine: s).

@@ -77,11 +77,9 @@ extern "C" int mflat_cu_kmeans_assign(const float* points, int64_t n, const floa
     sel.n = ix->n;
     sel.part_score = run.part_s;
     sel.part_id = run.part_i;
-    sel.q_hi = run.q_hi;
-    sel.q_lo = run.q_lo;
+    sel.q_x = run.q_x;
     sel.qnorm = run.qnorm;
-    sel.db_hi = ix->db_hi;
-    sel.db_lo = ix->db_lo;
+    sel.db_x = ix->db_x;
     sel.xmax_bits = ix->xmax_bits;
     sel.gamma = screen_gamma(ix->d_pad);
     sel.flag_count = ix->flag_count;

@@ -38,7 +38,7 @@ namespace mflat_cu {
 namespace {
 
 constexpr int kNaMaxQueries = 128;                   // one query tile
-constexpr int kNaMaxDim = kMaxDPadResident;          // 128
+constexpr int kNaMaxDim = 128;
 constexpr int kNaMaxK = 21;
 constexpr int kNaKP = 32;
 constexpr int kNaMaxChunks = 32;
@@ -48,10 +48,13 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kNaScratchBytes
 
 constexpr size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
-// Byte offsets of the per-call buffers inside g_noalloc_scratch.
-constexpr size_t kOffQHi = 0;
-constexpr size_t kOffQLo = kOffQHi + align256(size_t(kNaMaxQueries) * kNaMaxDim * 4);
-constexpr size_t kOffQNorm = kOffQLo + align256(size_t(kNaMaxQueries) * kNaMaxDim * 4);
+// Byte offsets of the per-call buffers inside g_noalloc_scratch: the fp32
+// queries and their bf16 split planes, norms, candidate lists, floors and the
+// exact fallback's lists.
+constexpr size_t kOffQX = 0;
+constexpr size_t kOffQH = kOffQX + align256(size_t(kNaMaxQueries) * kNaMaxDim * 4);
+constexpr size_t kOffQL = kOffQH + align256(size_t(kNaMaxQueries) * kNaMaxDim * 2);
+constexpr size_t kOffQNorm = kOffQL + align256(size_t(kNaMaxQueries) * kNaMaxDim * 2);
 constexpr size_t kOffPartS = kOffQNorm + align256(size_t(kNaMaxQueries) * 4);
 constexpr size_t kOffPartI = kOffPartS + align256(size_t(kNaMaxChunks) * kNaMaxQueries * kNaKP * 4);
 constexpr size_t kOffThr = kOffPartI + align256(size_t(kNaMaxChunks) * kNaMaxQueries * kNaKP * 4);
@@ -125,8 +128,9 @@ extern "C" int mflat_cu_index_search_noalloc(mflat_cu_index_t* ix, const float* 
     int n_chunks = 1, tpc = n_tiles;
     plan_screen_chunks(1, n_tiles, ix->num_sms, kNaMaxChunks, n_chunks, tpc);
 
-    float* q_hi = reinterpret_cast<float*>(base + kOffQHi);
-    float* q_lo = reinterpret_cast<float*>(base + kOffQLo);
+    float* q_x = reinterpret_cast<float*>(base + kOffQX);
+    uint16_t* q_h = reinterpret_cast<uint16_t*>(base + kOffQH);
+    uint16_t* q_l = reinterpret_cast<uint16_t*>(base + kOffQL);
     float* qnorm = reinterpret_cast<float*>(base + kOffQNorm);
     float* part_s = reinterpret_cast<float*>(base + kOffPartS);
     int32_t* part_i = reinterpret_cast<int32_t*>(base + kOffPartI);
@@ -135,7 +139,7 @@ extern "C" int mflat_cu_index_search_noalloc(mflat_cu_index_t* ix, const float* 
     double* fb_s = reinterpret_cast<double*>(base + kOffFbS);
     int32_t* fb_i = reinterpret_cast<int32_t*>(base + kOffFbI);
 
-    CU_TRY(launch_prep_queries(d_queries, m, m_pad, ix->dim, d_pad, ix->metric, q_hi, q_lo, qnorm, st),
+    CU_TRY(launch_prep_queries(d_queries, m, m_pad, ix->dim, d_pad, ix->metric, q_x, q_h, q_l, qnorm, st),
            "query prep launch");
     CU_TRY(cudaMemsetAsync(thr, 0, static_cast<size_t>(m_pad) * sizeof(uint32_t), st), "floors");
     CU_TRY(cudaMemsetAsync(ix->flag_count, 0, sizeof(int), st), "fallback count");
@@ -157,14 +161,14 @@ extern "C" int mflat_cu_index_search_noalloc(mflat_cu_index_t* ix, const float* 
     sp.thr = thr;
     sp.tile_stride = 1;
     sp.use_floor = 1;
-    CUtensorMap ta_hi, ta_lo, tb_hi, tb_lo;
-    if (!encode_map_f32(&ta_hi, q_hi, d_pad, m_pad, kBM) ||
-        !encode_map_f32(&ta_lo, q_lo, d_pad, m_pad, kBM) ||
-        !encode_map_f32(&tb_hi, ix->db_hi, d_pad, ix->n, kBN) ||
-        !encode_map_f32(&tb_lo, ix->db_lo, d_pad, ix->n, kBN))
+    CUtensorMap ta_h, ta_l, tb_h, tb_l;
+    if (!encode_map_bf16(&ta_h, q_h, d_pad, m_pad, kBM) ||
+        !encode_map_bf16(&ta_l, q_l, d_pad, m_pad, kBM) ||
+        !encode_map_bf16(&tb_h, ix->db_h, d_pad, ix->n, kBN) ||
+        !encode_map_bf16(&tb_l, ix->db_l, d_pad, ix->n, kBN))
         return fail(ST_DEVICE, "tensor map encoding failed");
     const int grid = n_chunks < ix->num_sms ? n_chunks : ix->num_sms;
-    CU_TRY(launch_screen_tf32x3(kNaKP, ta_hi, ta_lo, tb_hi, tb_lo, sp, grid, st), "screen launch");
+    CU_TRY(launch_screen_bf16x3(kNaKP, ta_h, ta_l, tb_h, tb_l, sp, grid, st), "screen launch");
 
     SelectParams sel{};
     sel.m = m;
@@ -177,11 +181,9 @@ extern "C" int mflat_cu_index_search_noalloc(mflat_cu_index_t* ix, const float* 
     sel.n = ix->n;
     sel.part_score = part_s;
     sel.part_id = part_i;
-    sel.q_hi = q_hi;
-    sel.q_lo = q_lo;
+    sel.q_x = q_x;
     sel.qnorm = qnorm;
-    sel.db_hi = ix->db_hi;
-    sel.db_lo = ix->db_lo;
+    sel.db_x = ix->db_x;
     sel.xmax_bits = ix->xmax_bits;
     sel.gamma = screen_gamma(d_pad);
     sel.out_ids = d_ids;

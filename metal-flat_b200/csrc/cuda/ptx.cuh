@@ -143,18 +143,8 @@ __device__ __forceinline__ void tc_fence_after() {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
 
-// D[tmem] (+)= A[smem desc] * B[smem desc]^T, kind::tf32, issued by one thread.
-__device__ __forceinline__ void tc_mma_tf32(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
-                                            uint32_t idesc, uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-        : "memory");
-}
-
-// Same for kind::f16 (A and B both f16 or both bf16, fp32 accumulation).
+// D[tmem] (+)= A[smem desc] * B[smem desc]^T, kind::f16 (A and B both f16
+// or both bf16, fp32 accumulation), issued by one thread.
 __device__ __forceinline__ void tc_mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
                                            uint32_t idesc, uint32_t accumulate) {
     asm volatile(
@@ -246,10 +236,6 @@ __host__ __device__ constexpr uint32_t make_idesc(uint32_t ab_format, uint32_t M
     return (1u << 4) | (ab_format << 7) | (ab_format << 10) | ((N >> 3) << 17) | ((M >> 4) << 24);
 }
 
-__device__ __forceinline__ uint32_t f32_to_tf32_rna(float x) {
-    uint32_t r;
-    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-    return r;
-}
+
 
 }  // namespace mflat_cu

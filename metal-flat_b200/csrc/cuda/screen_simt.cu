@@ -2,7 +2,7 @@
 // the tcgen05 kernel (per (query, chunk) top-KP lists).  It is the
 // independent GPU cross-check of screen_tc.cu, selected with
 // MFLAT_SCREEN=simt; the fp32 dot product here is computed directly from the
-// reconstructed rows (hi + lo), in index order.
+// stored fp32 rows, in index order.
 #include "kernels.cuh"
 #include "ptx.cuh"
 
@@ -19,16 +19,14 @@ __global__ void __launch_bounds__(128) screen_simt_kernel(const ScreenParams p) 
     TopList<KP> L;
     L.init();
     if (row < p.m) {
-        const float* qh = p.q_hi + static_cast<int64_t>(row) * p.d_pad;
-        const float* ql = p.q_lo + static_cast<int64_t>(row) * p.d_pad;
+        const float* qx = p.q_x + static_cast<int64_t>(row) * p.d_pad;
         for (int64_t t = t0; t < t1; ++t) {
             const int64_t j0 = t * p.tile_stride * kBN;
             const int64_t j1 = min(j0 + kBN, p.n);
             for (int64_t j = j0; j < j1; ++j) {
-                const float* xh = p.db_hi + j * p.d_pad;
-                const float* xl = p.db_lo + j * p.d_pad;
+                const float* x = p.db_x + j * p.d_pad;
                 float acc = 0.0f;
-                for (int c = 0; c < p.d_pad; ++c) acc = fmaf(qh[c] + ql[c], xh[c] + xl[c], acc);
+                for (int c = 0; c < p.d_pad; ++c) acc = fmaf(qx[c], x[c], acc);
                 const float s = fmaf(p.alpha, acc, p.colbias[j]);
                 if (s > L.worst()) L.insert(s, static_cast<int>(j));
             }
@@ -50,16 +48,14 @@ __global__ void __launch_bounds__(128) screen_simt_buffer_kernel(const ScreenPar
     const int64_t t0 = static_cast<int64_t>(ch) * p.tiles_per_chunk;
     const int64_t t1 = min(t0 + p.tiles_per_chunk, static_cast<int64_t>(p.n_tiles));
     const float floor_adj = floor_below(p.thr[row]);
-    const float* qh = p.q_hi + static_cast<int64_t>(row) * p.d_pad;
-    const float* ql = p.q_lo + static_cast<int64_t>(row) * p.d_pad;
+    const float* qx = p.q_x + static_cast<int64_t>(row) * p.d_pad;
     for (int64_t t = t0; t < t1; ++t) {
         const int64_t j0 = t * p.tile_stride * kBN;
         const int64_t j1 = min(j0 + kBN, p.n);
         for (int64_t j = j0; j < j1; ++j) {
-            const float* xh = p.db_hi + j * p.d_pad;
-            const float* xl = p.db_lo + j * p.d_pad;
+            const float* x = p.db_x + j * p.d_pad;
             float acc = 0.0f;
-            for (int c = 0; c < p.d_pad; ++c) acc = fmaf(qh[c] + ql[c], xh[c] + xl[c], acc);
+            for (int c = 0; c < p.d_pad; ++c) acc = fmaf(qx[c], x[c], acc);
             const float s = fmaf(p.alpha, acc, p.colbias[j]);
             if (s > floor_adj) {
                 const uint32_t slot = atomicAdd(p.buf_cnt + row, 1u);

@@ -4,12 +4,16 @@
 // src/FlatIndex.mm:63-107, which round-tripped an m x tileW score matrix
 // through device memory; here no score matrix is ever written).
 //
-// fp32 exactness: each operand is split x = hi + lo with hi = tf32(x); the
-// kernel accumulates A_hi.B_hi + A_lo.B_hi + A_hi.B_lo (3xTF32) in a TMEM
-// fp32 accumulator.  The result is a *screen*: the top-KP candidates per
-// (query, database chunk) by screen score, KP > k, which the select kernel
-// re-ranks exactly in fp64 after proving (with an a-priori error bound) that
-// the true top-k is inside the candidate set.
+// fp32 storage: each operand is held as two bf16 planes, x ~ h + l with
+// h = bf16(x) and l = bf16(x - h); the kernel accumulates
+// A_h.B_h + A_l.B_h + A_h.B_l (3 x bf16, kind::f16 at twice the kind::tf32
+// rate) in a TMEM fp32 accumulator.  Each product of bf16 values is exact in
+// fp32; what the split drops is ~3 * 2^-16 of |q_i x_i|, inside the error
+// bound the select kernel works with (screen_gamma).  The result is a
+// *screen*: the top-KP candidates per (query, database chunk) by screen
+// score, KP > k, which the select kernel re-ranks exactly in fp64 from the
+// stored fp32 rows after proving (with that a-priori bound) that the true
+// top-k is inside the candidate set.
 //
 // Work unit = (query tile of 128 rows, database chunk of whole 256-row tiles).
 // Persistent CTAs (one per SM) walk units chunk-major so that the CTAs
@@ -19,13 +23,13 @@
 //   warps 0-3  epilogue: thread t owns query row t of the tile = TMEM lane t;
 //              reads 32 fp32 columns at a time with tcgen05.ld, forms the
 //              score s = alpha*dot + colbias[row] and keeps a register top-KP.
-//   warp 4     TMA producer: for d_pad <= 128 the query tile (A, hi and lo
+//   warp 4     TMA producer: for d_pad <= 256 the query tile (A, h and l
 //              planes, all k-blocks) stays resident in shared memory for the
 //              unit and the database tile is streamed one (k-block, plane) of
 //              32 KB per ring stage; for larger d_pad each stage carries that
-//              k-block's query plane too (16 + 32 KB), and a k-block's hi and
-//              lo stages are consumed together.
-//   warp 5     TMEM allocator + MMA issuer (one thread), M=128 N=256 K=8,
+//              k-block's query plane too (16 + 32 KB), and a k-block's h and
+//              l stages are consumed together.
+//   warp 5     TMEM allocator + MMA issuer (one thread), M=128 N=256 K=16,
 //              double-buffered accumulators (2 x 256 TMEM columns).
 #include "epilogue.cuh"
 #include "kernels.cuh"
@@ -38,13 +42,13 @@ constexpr int kThreads = 192;
 constexpr int kEpiWarps = 4;
 constexpr int kProducerWarp = 4;
 constexpr int kMmaWarp = 5;
-constexpr int kATileBytes = kBM * kBK * 4;        // 16 KB: 128 rows x 128 B
-constexpr int kStageBytes = kBN * kBK * 4;        // 32 KB: 256 rows x 128 B
+constexpr int kATileBytes = kBM * kBK * 2;        // 16 KB: 128 rows x 128 B
+constexpr int kStageBytes = kBN * kBK * 2;        // 32 KB: 256 rows x 128 B
 constexpr int kMaxStages = 6;
 constexpr int kSmemBudget = 7 * kStageBytes;      // A + ring <= 224 KB
-constexpr uint32_t kIdescTF32 = make_idesc(2u, kBM, kBN);
+constexpr uint32_t kIdescBF16 = make_idesc(1u, kBM, kBN);   // bf16 x bf16 -> fp32
 
-// Query tile resident up to d_pad = 128 (4 k-blocks, 128 KB for both planes);
+// Query tile resident up to d_pad = 256 (4 k-blocks, 128 KB for both planes);
 // above, streamed with the database tile.
 __host__ __device__ inline bool a_streamed(int kb) { return kb * kBK > kMaxDPadResident; }
 __host__ __device__ inline int stage_bytes_for(int kb) {
@@ -54,7 +58,7 @@ __host__ __device__ inline int n_stages_for(int kb) {
     const int a = a_streamed(kb) ? 0 : kb * 2 * kATileBytes;
     int s = (kSmemBudget - a) / stage_bytes_for(kb);
     if (s > kMaxStages) s = kMaxStages;
-    if (a_streamed(kb)) s &= ~1;   // a k-block's hi and lo stages are used as a pair
+    if (a_streamed(kb)) s &= ~1;   // a k-block's h and l stages are used as a pair
     return s;
 }
 
@@ -91,10 +95,10 @@ __device__ inline SmemLayout carve(uint8_t* base, int kb, int stages) {
 
 template <int KP, bool kBuf>
 __global__ void __launch_bounds__(kThreads, 1)
-screen_tf32x3_kernel(const __grid_constant__ CUtensorMap tm_a_hi,
-                     const __grid_constant__ CUtensorMap tm_a_lo,
-                     const __grid_constant__ CUtensorMap tm_b_hi,
-                     const __grid_constant__ CUtensorMap tm_b_lo, const ScreenParams p) {
+screen_bf16x3_kernel(const __grid_constant__ CUtensorMap tm_a_h,
+                     const __grid_constant__ CUtensorMap tm_a_l,
+                     const __grid_constant__ CUtensorMap tm_b_h,
+                     const __grid_constant__ CUtensorMap tm_b_l, const ScreenParams p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -131,10 +135,10 @@ screen_tf32x3_kernel(const __grid_constant__ CUtensorMap tm_a_hi,
         tmem_relinquish();
     }
     if (warp == kProducerWarp && lane == 0) {
-        tma_prefetch_desc(&tm_a_hi);
-        tma_prefetch_desc(&tm_a_lo);
-        tma_prefetch_desc(&tm_b_hi);
-        tma_prefetch_desc(&tm_b_lo);
+        tma_prefetch_desc(&tm_a_h);
+        tma_prefetch_desc(&tm_a_l);
+        tma_prefetch_desc(&tm_b_h);
+        tma_prefetch_desc(&tm_b_l);
     }
     tc_fence_before();
     __syncthreads();
@@ -161,8 +165,8 @@ screen_tf32x3_kernel(const __grid_constant__ CUtensorMap tm_a_hi,
                     if (!mbar_wait(S.a_empty, a_phase ^ 1u, abort_flag)) { ok = false; break; }
                     mbar_arrive_expect_tx(S.a_full, static_cast<uint32_t>(kb_count * 2 * kATileBytes));
                     for (int kb = 0; kb < kb_count; ++kb) {
-                        tma_load_2d(&tm_a_hi, S.a_full, S.a + kb * kATileBytes, kb * kBK, qt * kBM);
-                        tma_load_2d(&tm_a_lo, S.a_full, S.a + (kb_count + kb) * kATileBytes, kb * kBK,
+                        tma_load_2d(&tm_a_h, S.a_full, S.a + kb * kATileBytes, kb * kBK, qt * kBM);
+                        tma_load_2d(&tm_a_l, S.a_full, S.a + (kb_count + kb) * kATileBytes, kb * kBK,
                                     qt * kBM);
                     }
                     a_issued = true;
@@ -176,11 +180,11 @@ screen_tf32x3_kernel(const __grid_constant__ CUtensorMap tm_a_hi,
                             uint8_t* dst = S.b + stage * sbytes;
                             mbar_arrive_expect_tx(&S.full[stage], static_cast<uint32_t>(sbytes));
                             if (stream_a) {
-                                tma_load_2d(plane ? &tm_a_lo : &tm_a_hi, &S.full[stage], dst, kb * kBK,
+                                tma_load_2d(plane ? &tm_a_l : &tm_a_h, &S.full[stage], dst, kb * kBK,
                                             qt * kBM);
                                 dst += kATileBytes;
                             }
-                            tma_load_2d(plane ? &tm_b_lo : &tm_b_hi, &S.full[stage], dst, kb * kBK,
+                            tma_load_2d(plane ? &tm_b_l : &tm_b_h, &S.full[stage], dst, kb * kBK,
                                         t * p.tile_stride * kBN);
                             issued_mask |= 1u << stage;
                             issued_phase = (issued_phase & ~(1u << stage)) | (sphase << stage);
@@ -221,60 +225,60 @@ screen_tf32x3_kernel(const __grid_constant__ CUtensorMap tm_a_hi,
                     tc_fence_after();
                     const uint32_t d_tmem = tmem_base + b * kBN;
                     for (int kb = 0; kb < kb_count && ok && stream_a; ++kb) {
-                        // the k-block's hi stage [A_hi | B_hi] and lo stage [A_lo | B_lo]
-                        const int s_hi = stage;
-                        const uint32_t ph_hi = sphase;
+                        // the k-block's h stage [A_h | B_h] and l stage [A_l | B_l]
+                        const int s_h = stage;
+                        const uint32_t ph_h = sphase;
                         if (++stage == stages) { stage = 0; sphase ^= 1u; }
-                        const int s_lo = stage;
-                        const uint32_t ph_lo = sphase;
+                        const int s_l = stage;
+                        const uint32_t ph_l = sphase;
                         if (++stage == stages) { stage = 0; sphase ^= 1u; }
-                        if (!mbar_wait(&S.full[s_hi], ph_hi, abort_flag) ||
-                            !mbar_wait(&S.full[s_lo], ph_lo, abort_flag)) { ok = false; break; }
+                        if (!mbar_wait(&S.full[s_h], ph_h, abort_flag) ||
+                            !mbar_wait(&S.full[s_l], ph_l, abort_flag)) { ok = false; break; }
                         tc_fence_after();
-                        const uint32_t base_hi = smem_u32(S.b + s_hi * sbytes);
-                        const uint32_t base_lo = smem_u32(S.b + s_lo * sbytes);
-                        const uint64_t a_hi = smem_desc_k_sw128(base_hi);
-                        const uint64_t b_hi = smem_desc_k_sw128(base_hi + kATileBytes);
-                        const uint64_t a_lo = smem_desc_k_sw128(base_lo);
-                        const uint64_t b_lo = smem_desc_k_sw128(base_lo + kATileBytes);
+                        const uint32_t base_h = smem_u32(S.b + s_h * sbytes);
+                        const uint32_t base_l = smem_u32(S.b + s_l * sbytes);
+                        const uint64_t a_h = smem_desc_k_sw128(base_h);
+                        const uint64_t b_h = smem_desc_k_sw128(base_h + kATileBytes);
+                        const uint64_t a_l = smem_desc_k_sw128(base_l);
+                        const uint64_t b_l = smem_desc_k_sw128(base_l + kATileBytes);
 #pragma unroll
-                        for (int ks = 0; ks < kBK / 8; ++ks) {
+                        for (int ks = 0; ks < kBK / 16; ++ks) {
                             const uint64_t o = static_cast<uint64_t>(ks * 2);   // 32 B >> 4
-                            tc_mma_tf32(d_tmem, a_hi + o, b_hi + o, kIdescTF32,
+                            tc_mma_f16(d_tmem, a_h + o, b_h + o, kIdescBF16,
                                         (kb | ks) != 0 ? 1u : 0u);
-                            tc_mma_tf32(d_tmem, a_lo + o, b_hi + o, kIdescTF32, 1u);
-                            tc_mma_tf32(d_tmem, a_hi + o, b_lo + o, kIdescTF32, 1u);
+                            tc_mma_f16(d_tmem, a_l + o, b_h + o, kIdescBF16, 1u);
+                            tc_mma_f16(d_tmem, a_h + o, b_l + o, kIdescBF16, 1u);
                         }
                         issued_any = true;
-                        tc_commit(&S.empty[s_hi]);
-                        tc_commit(&S.empty[s_lo]);
+                        tc_commit(&S.empty[s_h]);
+                        tc_commit(&S.empty[s_l]);
                     }
                     for (int kb = 0; kb < kb_count && ok && !stream_a; ++kb) {
-                        const uint64_t a_hi = smem_desc_k_sw128(a_addr + kb * kATileBytes);
-                        const uint64_t a_lo =
+                        const uint64_t a_h = smem_desc_k_sw128(a_addr + kb * kATileBytes);
+                        const uint64_t a_l =
                             smem_desc_k_sw128(a_addr + (kb_count + kb) * kATileBytes);
-                        // stage holding B_hi of this k-block
+                        // stage holding B_h of this k-block
                         if (!mbar_wait(&S.full[stage], sphase, abort_flag)) { ok = false; break; }
                         tc_fence_after();
                         uint64_t bd = smem_desc_k_sw128(smem_u32(S.b + stage * kStageBytes));
 #pragma unroll
-                        for (int ks = 0; ks < kBK / 8; ++ks) {
+                        for (int ks = 0; ks < kBK / 16; ++ks) {
                             const uint64_t o = static_cast<uint64_t>(ks * 2);   // 32 B >> 4
-                            tc_mma_tf32(d_tmem, a_hi + o, bd + o, kIdescTF32,
+                            tc_mma_f16(d_tmem, a_h + o, bd + o, kIdescBF16,
                                         (kb | ks) != 0 ? 1u : 0u);
-                            tc_mma_tf32(d_tmem, a_lo + o, bd + o, kIdescTF32, 1u);
+                            tc_mma_f16(d_tmem, a_l + o, bd + o, kIdescBF16, 1u);
                         }
                         issued_any = true;
                         tc_commit(&S.empty[stage]);
                         if (++stage == stages) { stage = 0; sphase ^= 1u; }
-                        // stage holding B_lo of this k-block
+                        // stage holding B_l of this k-block
                         if (!mbar_wait(&S.full[stage], sphase, abort_flag)) { ok = false; break; }
                         tc_fence_after();
                         bd = smem_desc_k_sw128(smem_u32(S.b + stage * kStageBytes));
 #pragma unroll
-                        for (int ks = 0; ks < kBK / 8; ++ks) {
+                        for (int ks = 0; ks < kBK / 16; ++ks) {
                             const uint64_t o = static_cast<uint64_t>(ks * 2);
-                            tc_mma_tf32(d_tmem, a_hi + o, bd + o, kIdescTF32, 1u);
+                            tc_mma_f16(d_tmem, a_h + o, bd + o, kIdescBF16, 1u);
                         }
                         tc_commit(&S.empty[stage]);
                         if (++stage == stages) { stage = 0; sphase ^= 1u; }
@@ -389,35 +393,35 @@ screen_tf32x3_kernel(const __grid_constant__ CUtensorMap tm_a_hi,
 }
 
 template <int KP, bool kBuf = false>
-cudaError_t launch_kp(const CUtensorMap& a_hi, const CUtensorMap& a_lo, const CUtensorMap& b_hi,
-                      const CUtensorMap& b_lo, const ScreenParams& p, int grid,
+cudaError_t launch_kp(const CUtensorMap& a_h, const CUtensorMap& a_l, const CUtensorMap& b_h,
+                      const CUtensorMap& b_l, const ScreenParams& p, int grid,
                       cudaStream_t stream) {
-    const int smem = screen_tf32x3_smem_bytes(p.d_pad);
-    cudaError_t e = cudaFuncSetAttribute(screen_tf32x3_kernel<KP, kBuf>,
+    const int smem = screen_bf16x3_smem_bytes(p.d_pad);
+    cudaError_t e = cudaFuncSetAttribute(screen_bf16x3_kernel<KP, kBuf>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
-    screen_tf32x3_kernel<KP, kBuf><<<grid, kThreads, smem, stream>>>(a_hi, a_lo, b_hi, b_lo, p);
+    screen_bf16x3_kernel<KP, kBuf><<<grid, kThreads, smem, stream>>>(a_h, a_l, b_h, b_l, p);
     return cudaGetLastError();
 }
 
 }  // namespace
 
-int screen_tf32x3_smem_bytes(int d_pad) {
+int screen_bf16x3_smem_bytes(int d_pad) {
     const int kb = d_pad / kBK;
     const int a = a_streamed(kb) ? 0 : kb * 2 * kATileBytes;
     return 1024 + a + n_stages_for(kb) * stage_bytes_for(kb) + 256;
 }
 
-cudaError_t launch_screen_tf32x3(int kp, const CUtensorMap& a_hi, const CUtensorMap& a_lo,
-                                 const CUtensorMap& b_hi, const CUtensorMap& b_lo,
+cudaError_t launch_screen_bf16x3(int kp, const CUtensorMap& a_h, const CUtensorMap& a_l,
+                                 const CUtensorMap& b_h, const CUtensorMap& b_l,
                                  const ScreenParams& p, int grid, cudaStream_t stream) {
     if (p.d_pad % kBK != 0 || p.d_pad < kBK) return cudaErrorInvalidValue;
     switch (kp) {
-        case 0: return launch_kp<4, true>(a_hi, a_lo, b_hi, b_lo, p, grid, stream);
-        case 4: return launch_kp<4>(a_hi, a_lo, b_hi, b_lo, p, grid, stream);
-        case 8: return launch_kp<8>(a_hi, a_lo, b_hi, b_lo, p, grid, stream);
-        case 16: return launch_kp<16>(a_hi, a_lo, b_hi, b_lo, p, grid, stream);
-        case 32: return launch_kp<32>(a_hi, a_lo, b_hi, b_lo, p, grid, stream);
+        case 0: return launch_kp<4, true>(a_h, a_l, b_h, b_l, p, grid, stream);
+        case 4: return launch_kp<4>(a_h, a_l, b_h, b_l, p, grid, stream);
+        case 8: return launch_kp<8>(a_h, a_l, b_h, b_l, p, grid, stream);
+        case 16: return launch_kp<16>(a_h, a_l, b_h, b_l, p, grid, stream);
+        case 32: return launch_kp<32>(a_h, a_l, b_h, b_l, p, grid, stream);
         default: return cudaErrorInvalidValue;
     }
 }

@@ -1,14 +1,14 @@
 // select.cu -- candidate merge, exactness proof and exact re-rank.
 //
 // The screen (screen_tc.cu) leaves, per query and database chunk, the top-KP
-// rows by the fp32 screen score s' (3xTF32 dot + norm term).  Every screen
+// rows by the fp32 screen score s' (3 x bf16 dot + norm term).  Every screen
 // score is within E of the exact score s (a-priori bound, see error_bound()).
 // If the KP-th best merged screen score is below (k-th best) - 2E, every row
 // of the true top-k is among the KP candidates (standard argument: the k rows
 // of the true top-k all have s' >= s_(k) - E, hence s'_(k) >= s_(k) - E, and
 // s'_(k) <= s_(k) + E; a true top-k row therefore has s' >= s'_(k) - 2E).
 // The candidates are then re-scored exactly in fp64 from the stored fp32 rows
-// (hi + lo) and ordered by (distance, id), which is the fp64 brute-force
+// and ordered by (distance, id), which is the fp64 brute-force
 // oracle's order (reference semantics: src/Distance.h:26-81, ties to the
 // lowest id as in src/FlatIndex.mm:272-281).  Queries whose proof fails
 // (many near-equal scores, e.g. duplicated rows) are re-done by an exact
@@ -74,18 +74,18 @@ __device__ __forceinline__ double error_bound(int metric, double qn, double xmax
     return gamma * qn * xmax + 1e-30;
 }
 
-__device__ __forceinline__ double exact_score(int metric, const float* qh, const float* ql,
-                                              const float* xh, const float* xl, int dim) {
+// fp64 score of the stored fp32 query and row, index order (the fp64 oracle's
+// evaluation): -sum (q - x)^2 for L2, sum q x otherwise.
+__device__ __forceinline__ double exact_score(int metric, const float* q, const float* x, int dim) {
     double acc = 0.0;
     if (metric == kL2) {
         for (int c = 0; c < dim; ++c) {
-            const double e = static_cast<double>(qh[c] + ql[c]) - static_cast<double>(xh[c] + xl[c]);
+            const double e = static_cast<double>(q[c]) - static_cast<double>(x[c]);
             acc += e * e;
         }
         return -acc;
     }
-    for (int c = 0; c < dim; ++c)
-        acc += static_cast<double>(qh[c] + ql[c]) * static_cast<double>(xh[c] + xl[c]);
+    for (int c = 0; c < dim; ++c) acc += static_cast<double>(q[c]) * static_cast<double>(x[c]);
     return acc;
 }
 
@@ -208,10 +208,8 @@ __global__ void __launch_bounds__(128) select_exact_kernel(const SelectParams p)
     // exact fp64 re-score (lane = candidate), then (distance, id) order
     double ex = -DBL_MAX;
     if (id >= 0) {
-        const float* qh = p.q_hi + static_cast<int64_t>(qi) * p.d_pad;
-        const float* ql = p.q_lo + static_cast<int64_t>(qi) * p.d_pad;
         const int64_t r = id;
-        ex = exact_score(p.metric, qh, ql, p.db_hi + r * p.d_pad, p.db_lo + r * p.d_pad, p.dim);
+        ex = exact_score(p.metric, p.q_x + static_cast<int64_t>(qi) * p.d_pad, p.db_x + r * p.d_pad, p.dim);
     }
     int rid = id;
     warp_sort_better_first(ex, rid, lane);
@@ -245,16 +243,14 @@ __global__ void __launch_bounds__(kFbThreads) fallback_scan_kernel(const SelectP
         const int c = pair / nflag;
         const int f = pair % nflag;
         const int qi = p.flag_list[f];
-        const float* qh = p.q_hi + static_cast<int64_t>(qi) * p.d_pad;
-        const float* ql = p.q_lo + static_cast<int64_t>(qi) * p.d_pad;
+        const float* qx = p.q_x + static_cast<int64_t>(qi) * p.d_pad;
         const int64_t r0 = c * per;
         const int64_t r1 = min(p.n, r0 + per);
         double bs[kFbMaxK];
         int bi[kFbMaxK];
         for (int i = 0; i < k; ++i) { bs[i] = -DBL_MAX; bi[i] = -1; }   // sorted desc
         for (int64_t j = r0 + threadIdx.x; j < r1; j += blockDim.x) {
-            const double s = exact_score(p.metric, qh, ql, p.db_hi + j * p.d_pad,
-                                         p.db_lo + j * p.d_pad, p.dim);
+            const double s = exact_score(p.metric, qx, p.db_x + j * p.d_pad, p.dim);
             if (bi[k - 1] < 0 || s > bs[k - 1]) {
                 int pos = k - 1;
                 while (pos > 0 && (bi[pos - 1] < 0 || s > bs[pos - 1])) {
@@ -314,18 +310,17 @@ __global__ void __launch_bounds__(128) fallback_merge_kernel(const SelectParams 
 // Assignment of point qi = argmin_c sqL2_f32(p, c) with the reference's fp32
 // sequential sqL2 (src/Distance.h:33-37, used by src/CoarseQuantizer.mm:
 // 122-130) and strict '<' (lowest centroid wins a tie).  The screen gives the
-// top-KP centroids by 3xTF32 score; every centroid that could be the fp32
+// top-KP centroids by screen score; every centroid that could be the fp32
 // argmin lies within a window W of the best screen score (W covers the screen
 // error E on both sides and the rounding of the fp32 sequential sum,
 // gamma_s = (dim + 8) 2^-23 relative).  If the KP-th candidate is outside the
 // window the candidates inside it are re-scored with exactly the reference's
 // operations (__fsub_rn / __fmul_rn / __fadd_rn in index order) and the
 // minimum is taken; otherwise the point goes to the full fp32 scan.
-__device__ __forceinline__ float sql2_f32_seq(const float* ph, const float* pl, const float* xh,
-                                              const float* xl, int dim) {
+__device__ __forceinline__ float sql2_f32_seq(const float* p, const float* x, int dim) {
     float acc = 0.0f;
     for (int c = 0; c < dim; ++c) {
-        const float e = __fsub_rn(__fadd_rn(ph[c], pl[c]), __fadd_rn(xh[c], xl[c]));
+        const float e = __fsub_rn(p[c], x[c]);
         acc = __fadd_rn(acc, __fmul_rn(e, e));
     }
     return acc;
@@ -386,15 +381,14 @@ __global__ void __launch_bounds__(128) kmeans_select_kernel(const SelectParams p
         }
         return;
     }
-    const float* ph = p.q_hi + static_cast<int64_t>(qi) * p.d_pad;
-    const float* pl = p.q_lo + static_cast<int64_t>(qi) * p.d_pad;
+    const float* px = p.q_x + static_cast<int64_t>(qi) * p.d_pad;
     MinCand mc{0.0f, -1};
 #pragma unroll
     for (int i = 0; i < KP; ++i) {
         if (lane == i && sel_id[i] >= 0 &&
             static_cast<double>(sel_s[i]) >= static_cast<double>(sel_s[0]) - W) {
             const int64_t id = sel_id[i];
-            mc.v = sql2_f32_seq(ph, pl, p.db_hi + id * p.d_pad, p.db_lo + id * p.d_pad, p.dim);
+            mc.v = sql2_f32_seq(px, p.db_x + id * p.d_pad, p.dim);
             mc.id = sel_id[i];
         }
     }
@@ -410,11 +404,10 @@ __global__ void __launch_bounds__(128) kmeans_fallback_kernel(const SelectParams
     const int nflag = *p.flag_count;
     for (int f = wid; f < nflag; f += nwarps) {
         const int qi = p.flag_list[f];
-        const float* ph = p.q_hi + static_cast<int64_t>(qi) * p.d_pad;
-        const float* pl = p.q_lo + static_cast<int64_t>(qi) * p.d_pad;
+        const float* px = p.q_x + static_cast<int64_t>(qi) * p.d_pad;
         MinCand mc{0.0f, -1};
         for (int64_t c = lane; c < p.n; c += 32) {
-            const float v = sql2_f32_seq(ph, pl, p.db_hi + c * p.d_pad, p.db_lo + c * p.d_pad, p.dim);
+            const float v = sql2_f32_seq(px, p.db_x + c * p.d_pad, p.dim);
             if (mc.id < 0 || v < mc.v) { mc.v = v; mc.id = static_cast<int>(c); }
         }
         mc = warp_min(mc);

@@ -143,18 +143,16 @@ __device__ void bitonic_sort_int(int* a, int cnt) {
     }
 }
 
-__device__ __forceinline__ double exact_score_l(int metric, const float* qh, const float* ql,
-                                                const float* xh, const float* xl, int dim) {
+__device__ __forceinline__ double exact_score_l(int metric, const float* q, const float* x, int dim) {
     double acc = 0.0;
     if (metric == kL2) {
         for (int c = 0; c < dim; ++c) {
-            const double e = static_cast<double>(qh[c] + ql[c]) - static_cast<double>(xh[c] + xl[c]);
+            const double e = static_cast<double>(q[c]) - static_cast<double>(x[c]);
             acc += e * e;
         }
         return -acc;
     }
-    for (int c = 0; c < dim; ++c)
-        acc += static_cast<double>(qh[c] + ql[c]) * static_cast<double>(xh[c] + xl[c]);
+    for (int c = 0; c < dim; ++c) acc += static_cast<double>(q[c]) * static_cast<double>(x[c]);
     return acc;
 }
 
@@ -264,11 +262,10 @@ __global__ void __launch_bounds__(kSelThreads) select_large_kernel(const LargeSe
             return;
         }
         cnt = sh_pos;
-        const float* qh = p.q_hi + static_cast<int64_t>(qi) * p.d_pad;
-        const float* ql = p.q_lo + static_cast<int64_t>(qi) * p.d_pad;
+        const float* qx = p.q_x + static_cast<int64_t>(qi) * p.d_pad;
         for (int i = threadIdx.x; i < cnt; i += blockDim.x) {
             const int64_t id = ids[i];
-            key[i] = exact_score_l(p.metric, qh, ql, p.db_hi + id * p.d_pad, p.db_lo + id * p.d_pad, p.dim);
+            key[i] = exact_score_l(p.metric, qx, p.db_x + id * p.d_pad, p.dim);
         }
         __syncthreads();
         bitonic_sort(key, ids, cnt);
