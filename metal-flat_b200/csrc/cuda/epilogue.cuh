@@ -145,7 +145,9 @@ struct BufferRow {
     uint32_t cap;
 };
 
-__device__ __forceinline__ void append_passing(const float (&sc)[32], float floor_adj,
+// `scale` converts the compared values to scores (1, or 2 for the L2 screen
+// whose accumulator holds half the score); an exact power of two.
+__device__ __forceinline__ void append_passing(const float (&sc)[32], float floor_adj, float scale,
                                                const BufferRow& br, int id0) {
     const uint32_t mask = passing_mask(sc, floor_adj);
     uint32_t slot = atomicAdd(br.cnt, static_cast<uint32_t>(__popc(mask)));
@@ -157,7 +159,7 @@ __device__ __forceinline__ void append_passing(const float (&sc)[32], float floo
                 const int j = 4 * i + e;
                 if ((mask >> j) & 1u) {
                     if (slot < br.cap) {
-                        br.s[slot] = sc[j];
+                        br.s[slot] = scale * sc[j];
                         br.id[slot] = id0 + j;
                     }
                     ++slot;
@@ -199,14 +201,14 @@ struct AppendStage {
     }
 };
 
-__device__ __forceinline__ void stage_passing(const float (&sc)[32], float floor_adj,
+__device__ __forceinline__ void stage_passing(const float (&sc)[32], float floor_adj, float scale,
                                               const BufferRow& br, AppendStage& st, int id0) {
     const uint32_t mask = passing_mask(sc, floor_adj);
     const uint32_t np = __popc(mask);
     if (st.n + np > AppendStage::kStage) {
         st.flush(br);
         if (np > AppendStage::kStage) {
-            append_passing(sc, floor_adj, br, id0);
+            append_passing(sc, floor_adj, scale, br, id0);
             return;
         }
     }
@@ -216,7 +218,7 @@ __device__ __forceinline__ void stage_passing(const float (&sc)[32], float floor
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
                 const int j = 4 * i + e;
-                if ((mask >> j) & 1u) st.put(sc[j], id0 + j);
+                if ((mask >> j) & 1u) st.put(scale * sc[j], id0 + j);
             }
         }
     }
@@ -227,17 +229,19 @@ __device__ __forceinline__ void buffer_chunk(const uint32_t (&r)[32], const floa
                                              AppendStage& st, int id0) {
     float sc[32];
     chunk_scores(r, cb, alpha, sc);
-    if (max_tree32(sc) > floor_adj) stage_passing(sc, floor_adj, br, st, id0);
+    if (max_tree32(sc) > floor_adj) stage_passing(sc, floor_adj, 1.0f, br, st, id0);
 }
 
-// Inner-product variant for chunks wholly inside the database: the bias is 0,
-// so the accumulator is the score (no bias load, no FFMA).
-__device__ __forceinline__ void buffer_chunk_raw(const uint32_t (&r)[32], float floor_adj,
+// Accumulator compared as it is (no bias load, no FFMA): inner product on
+// chunks wholly inside the database (bias 0, scale 1), or the L2 screen with
+// the bias folded into the MMA (accumulator = score / 2: floor_adj halved,
+// scale 2).
+__device__ __forceinline__ void buffer_chunk_raw(const uint32_t (&r)[32], float floor_adj, float scale,
                                                  const BufferRow& br, AppendStage& st, int id0) {
     float sc[32];
 #pragma unroll
     for (int j = 0; j < 32; ++j) sc[j] = __uint_as_float(r[j]);
-    if (max_tree32(sc) > floor_adj) stage_passing(sc, floor_adj, br, st, id0);
+    if (max_tree32(sc) > floor_adj) stage_passing(sc, floor_adj, scale, br, st, id0);
 }
 
 template <int KP>

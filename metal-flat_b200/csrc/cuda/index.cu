@@ -110,7 +110,47 @@ bool make_map_u16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t r
     return r == CUDA_SUCCESS;
 }
 
+// Bias parts of the folded L2 screen: [rows][8] bf16 (hi, mid, lo, zeros),
+// 8-wide boxes of 256 rows, no swizzle (the MMA's K-major core-matrix layout).
+bool make_map_bias16(CUtensorMap* map, const void* base, uint64_t rows) {
+    if (!get_encoder()) return false;
+    cuuint64_t dims[2] = {8, rows};
+    cuuint64_t strides[1] = {16};
+    cuuint32_t box[2] = {8u, static_cast<cuuint32_t>(kBN)};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(base), dims,
+                          strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                          CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
 // ------------------------------------------------------------- kernels
+// b = colbias / 2 (exact) as hi + mid + lo: hi and mid truncated to bf16
+// (round toward zero), lo the remainder (8 bits, exact).  The three parts
+// share b's sign and cover disjoint bit ranges of its 24-bit significand, so
+// every partial sum is exact in fp32 and the tensor core's addition order
+// cannot change the result.  -inf (rows past n) becomes (-inf, 0, 0).
+__global__ void split_bias_kernel(const float* __restrict__ colbias, int64_t rows,
+                                  uint4* __restrict__ out) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= rows) return;
+    const float b = 0.5f * colbias[i];
+    uint16_t h, m = 0, l = 0;
+    if (isinf(b)) {
+        h = __bfloat16_as_ushort(__float2bfloat16_rn(b));
+    } else {
+        const __nv_bfloat16 hb = __float2bfloat16_rz(b);
+        const float r1 = b - __bfloat162float(hb);
+        const __nv_bfloat16 mb = __float2bfloat16_rz(r1);
+        const float r2 = r1 - __bfloat162float(mb);
+        h = __bfloat16_as_ushort(hb);
+        m = __bfloat16_as_ushort(mb);
+        l = __bfloat16_as_ushort(__float2bfloat16_rn(r2));
+    }
+    out[i] = make_uint4(static_cast<uint32_t>(h) | (static_cast<uint32_t>(m) << 16), l, 0u, 0u);
+}
+
 // fp32 -> 16-bit storage bits, round to nearest even.
 __device__ __forceinline__ uint16_t to_half_bits(float x, bool bf16) {
     if (bf16) return __bfloat16_as_ushort(__float2bfloat16_rn(x));
@@ -433,8 +473,12 @@ int check_device_error(mflat_cu_index* ix, cudaStream_t st) {
 
 // The fp32-storage screen over sp's query batch (bf16 planes in ix->q_h /
 // ix->q_l, rows in ix->db_h / ix->db_l), or the CUDA-core cross-check.
-cudaError_t launch_fp32_screen(mflat_cu_index* ix, const ScreenParams& sp, int kp, cudaStream_t st) {
-    if (ix->force_simt) return launch_screen_simt(kp, sp, st);
+cudaError_t launch_fp32_screen(mflat_cu_index* ix, const ScreenParams& sp_in, int kp, cudaStream_t st) {
+    if (ix->force_simt) return launch_screen_simt(kp, sp_in, st);
+    ScreenParams sp = sp_in;
+    sp.wait_ns = ix->wait_ns;
+    sp.test_stall = ix->test_stall;
+    ix->test_stall = 0;
     CUtensorMap ta_h, ta_l, tb_h, tb_l;
     if (!make_map_u16(&ta_h, ix->q_h.p, sp.d_pad, sp.m_pad, kBM) ||
         !make_map_u16(&ta_l, ix->q_l.p, sp.d_pad, sp.m_pad, kBM) ||
@@ -675,6 +719,8 @@ int search_large(mflat_cu_index* ix, const float* queries, int m, int k_out, int
         sp.tiles_per_chunk = tpc;
 
         LargeSelectParams ls{};
+        ls.n = ix->n;
+        ls.err = ix->err;
         ls.m = mb;
         ls.m_pad = mb_pad;
         ls.dim = ix->dim;
@@ -789,6 +835,22 @@ int search_half(mflat_cu_index* ix, const float* queries, int m, int k_out, int3
     CU_TRY(ix->part_i.ensure(parts * sizeof(int32_t)), "candidate lists");
     CUtensorMap tb;
     if (!make_map_u16(&tb, ix->db16, d_pad, ix->n, kBN)) return fail(ST_DEVICE, "tensor map encoding failed");
+    // L2: the bias goes into the MMA as three bf16 parts per row (derived from
+    // colbias once per database state), the epilogue compares accumulators
+    const bool fold = ix->metric == kL2;
+    CUtensorMap tbias;
+    if (fold) {
+        const int64_t rows_pad = static_cast<int64_t>(n_tiles) * kBN;
+        if (ix->bias16_n != ix->n) {
+            CU_TRY(ix->bias16.ensure(static_cast<size_t>(rows_pad) * 16), "bias parts");
+            split_bias_kernel<<<blocks_for(rows_pad, 256), 256, 0, st>>>(ix->colbias, rows_pad,
+                                                                          ix->bias16.as<uint4>());
+            CU_TRY(cudaGetLastError(), "bias parts");
+            ix->bias16_n = ix->n;
+        }
+        if (!make_map_bias16(&tbias, ix->bias16.p, rows_pad))
+            return fail(ST_DEVICE, "tensor map encoding failed");
+    }
     if (ix->timing) cudaEventRecord(ix->ev[0], st);
 
     for (int b0 = 0; b0 < m; b0 += P.batch) {
@@ -813,10 +875,11 @@ int search_half(mflat_cu_index* ix, const float* queries, int m, int k_out, int3
         sp.thr = ix->thr.as<uint32_t>();
         sp.part_score = ix->part_s.as<float>();
         sp.part_id = ix->part_i.as<int32_t>();
+        sp.wait_ns = ix->wait_ns;
         auto launch = [&](const ScreenParams& q, int kpp) {
             const int64_t units = static_cast<int64_t>(q.n_qtiles) * q.n_chunks;
             const int grid = static_cast<int>(std::min<int64_t>(units, ix->num_sms));
-            return launch_screen_f16(kpp, bf16, ta, tb, q, grid, st);
+            return launch_screen_f16(kpp, bf16, ta, tb, fold ? &tbias : nullptr, q, grid, st);
         };
         if (list_mode) {
             sp.use_floor = 1;
@@ -865,6 +928,8 @@ int search_half(mflat_cu_index* ix, const float* queries, int m, int k_out, int3
         sp.n_chunks = n_chunks;
         sp.tiles_per_chunk = tpc;
         LargeSelectParams ls{};
+        ls.n = ix->n;
+        ls.err = ix->err;
         ls.m = mb;
         ls.m_pad = mb_pad;
         ls.k_out = k_out;
@@ -961,6 +1026,7 @@ int index_add(mflat_cu_index_t* ix, const void* vectors, int64_t n, int on_devic
         if (!on_device) CU_TRY(cudaStreamSynchronize(ix->stream), "ingest");
     }
     ix->n += n;
+    ix->bias16_n = -1;
     if (on_device) order_after(caller, ix->stream);
     return ST_OK;
 }
@@ -1112,6 +1178,12 @@ int mflat_cu_index_create(int device, int dim, int metric, int storage, mflat_cu
     cudaDeviceGetAttribute(&ix->num_sms, cudaDevAttrMultiProcessorCount, device);
     const char* fs = std::getenv("MFLAT_SCREEN");
     ix->force_simt = fs && std::strcmp(fs, "simt") == 0;
+    if (const char* wl = std::getenv("MFLAT_WAIT_LIMIT_MS")) {
+        const double ms = std::atof(wl);
+        if (ms > 0.0) ix->wait_ns = static_cast<uint64_t>(ms * 1e6);
+    }
+    const char* stall = std::getenv("MFLAT_TEST_STALL_SCREEN");
+    ix->test_stall = (stall && std::strcmp(stall, "1") == 0) ? 1 : 0;
     cudaError_t e;
     if ((e = cudaStreamCreateWithFlags(&ix->stream, cudaStreamNonBlocking)) != cudaSuccess ||
         (e = cudaMalloc(&ix->xmax_bits, sizeof(unsigned))) != cudaSuccess ||
@@ -1151,7 +1223,7 @@ void mflat_cu_index_destroy(mflat_cu_index_t* ix) {
                       &ix->part_i, &ix->flag_list, &ix->out_ids, &ix->out_dist, &ix->gather_ids,
                       &ix->gather_dist, &ix->merge_tmp_ids, &ix->merge_tmp_dist, &ix->thr, &ix->thr_stat, &ix->fb_s,
                       &ix->fb_i, &ix->buf_cnt, &ix->buf_s, &ix->buf_i, &ix->lk_words,
-                      &ix->q16, &ix->qsq})
+                      &ix->q16, &ix->qsq, &ix->bias16})
         b->release();
     for (auto& slot : ix->ring)
         for (auto& ev : slot.ev)
@@ -1212,6 +1284,7 @@ int mflat_cu_index_reset(mflat_cu_index_t* ix) {
     cudaMemsetAsync(ix->xmax_bits, 0, sizeof(unsigned), ix->stream);
     CU_TRY(cudaStreamSynchronize(ix->stream), "reset");
     ix->n = 0;
+    ix->bias16_n = -1;
     return ST_OK;
 }
 

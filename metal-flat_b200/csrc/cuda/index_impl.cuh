@@ -89,6 +89,11 @@ struct mflat_cu_index {
     mflat_cu::DevBuf thr, thr_stat, fb_s, fb_i;
     mflat_cu::DevBuf buf_cnt, buf_s, buf_i, lk_words;   // large-k candidate buffers
     mflat_cu::DevBuf q16, qsq;                          // 16-bit queries, ||q||^2
+    // 16-bit L2: -||x||^2 / 2 as three bf16 parts per row ([rows][8] bf16,
+    // padding rows -inf), derived from colbias for rows_pad(n) rows; valid
+    // while bias16_n == n (add / reset set it to -1)
+    mflat_cu::DevBuf bias16;
+    int64_t bias16_n = -1;
     // Timing (mflat_cu_index_set_timing): each search records 4 events into
     // one slot of a ring and returns without waiting for them; a slot is read
     // (and its device times added to `sum`) only when it is reused, or by
@@ -108,6 +113,11 @@ struct mflat_cu_index {
     mutable int sum_n = 0;
     mflat_cu_timing_t last{};
     bool force_simt = false;
+    // Limit of the screens' bounded waits in ns (MFLAT_WAIT_LIMIT_MS; 0 = 2 s).
+    uint64_t wait_ns = 0;
+    // Test hook (MFLAT_TEST_STALL_SCREEN set at creation): the next fp32
+    // screen launch stalls on purpose until its bounded wait runs out; one shot.
+    int test_stall = 0;
     // row sharding (comm.cu)
     void* comm = nullptr;
     int rank = 0, world = 1;

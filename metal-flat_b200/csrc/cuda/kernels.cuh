@@ -81,6 +81,12 @@ struct ScreenParams {
     // SIMT path only: the fp32 queries and rows
     const float* q_x;
     const float* db_x;
+    // Limit of every bounded mbarrier wait in ns (0: kWaitTimeoutNs).
+    uint64_t wait_ns;
+    // Test hook (MFLAT_TEST_STALL_SCREEN): the MMA warp first waits on a
+    // barrier nothing arrives at, so the bounded wait runs out and the launch
+    // ends through its error path (error word kErrTimeout, TMEM freed).
+    int test_stall;
 };
 
 struct SelectParams {
@@ -112,6 +118,8 @@ struct LargeSelectParams {
     int32_t* out_ids; float* out_dist;
     int* flag_count; int* flag_list;      // proof failures (exact path)
     int* overflow;                        // buffers that overflowed / too many ties
+    int64_t n;                            // database rows (candidate ids are below)
+    const int* err;                       // device error word of the screens
 };
 
 // ---------------------------------------------------------------------------
@@ -159,9 +167,13 @@ cudaError_t launch_screen_bf16x3(int kp, const CUtensorMap& a_h, const CUtensorM
 cudaError_t launch_screen_simt(int kp, const ScreenParams& p, cudaStream_t stream);
 // fp16 / bf16 storage (q and db in 16-bit, d_pad a multiple of 64); kp 0 =
 // buffer mode; list mode writes two lists per (query, chunk).
+// fold_bias: tensor map of the L2 bias parts ([rows][8] bf16: -||x||^2 / 2 as
+// hi + mid + lo, then zeros; rows past n: -inf, 0, 0) -- the MMA adds them and
+// the accumulator is half the score; nullptr: bias in the epilogue.
 cudaError_t launch_screen_f16(int kp, bool bf16, const CUtensorMap& a, const CUtensorMap& b,
-                              const ScreenParams& p, int grid, cudaStream_t stream);
-int screen_f16_smem_bytes(int d_pad);
+                              const CUtensorMap* fold_bias, const ScreenParams& p, int grid,
+                              cudaStream_t stream);
+int screen_f16_smem_bytes(int d_pad, bool fold);
 cudaError_t launch_select_exact(int kp, const SelectParams& p, cudaStream_t stream);
 cudaError_t launch_fallback_exact(const SelectParams& p, int grid, cudaStream_t stream);
 int screen_bf16x3_smem_bytes(int d_pad);

@@ -161,6 +161,7 @@ extern "C" int mflat_cu_index_search_noalloc(mflat_cu_index_t* ix, const float* 
     sp.thr = thr;
     sp.tile_stride = 1;
     sp.use_floor = 1;
+    sp.wait_ns = ix->wait_ns;
     CUtensorMap ta_h, ta_l, tb_h, tb_l;
     if (!encode_map_bf16(&ta_h, q_h, d_pad, m_pad, kBM) ||
         !encode_map_bf16(&ta_l, q_l, d_pad, m_pad, kBM) ||

@@ -10,13 +10,15 @@ namespace mflat_cu {
 
 // A wait that has not completed after this many nanoseconds marks the CTA as
 // failed: the kernel records an error code, drains what it issued and exits.
-// Legitimate waits in these kernels last microseconds.
+// Legitimate waits in these kernels last microseconds.  The host can pass a
+// different limit per launch (ScreenParams::wait_ns, MFLAT_WAIT_LIMIT_MS).
 constexpr uint64_t kWaitTimeoutNs = 2000000000ull;
 
 enum ErrCode : int {
     kErrNone = 0,
     kErrTimeout = 1,        // a bounded mbarrier wait ran out
     kErrConfig = 2,         // kernel launched with an unsupported shape
+    kErrInternal = 3,       // a consistency check failed (e.g. a candidate id out of range)
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -52,17 +54,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t addr, uint32_t parity) {
 }
 
 // Bounded wait for the phase with the given parity.  Returns false when the
-// CTA-wide abort flag is (or becomes) set, or after kWaitTimeoutNs; in the
-// timeout case this thread sets the abort flag itself.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+// CTA-wide abort flag is (or becomes) set, or after limit_ns (0: the default
+// kWaitTimeoutNs); in the timeout case this thread sets the abort flag itself.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                          uint64_t limit_ns) {
     const uint32_t addr = smem_u32(bar);
     if (mbar_try_wait(addr, parity)) return true;
+    const uint64_t limit = limit_ns ? limit_ns : kWaitTimeoutNs;
     const uint64_t t0 = globaltimer_ns();
     for (uint32_t it = 1;; ++it) {
         if (mbar_try_wait(addr, parity)) return true;
         if ((it & 63u) == 0u) {
             if (*abort_flag) return false;
-            if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+            if (globaltimer_ns() - t0 > limit) {
                 *abort_flag = kErrTimeout;
                 return false;
             }
@@ -228,6 +232,24 @@ __device__ __forceinline__ uint64_t smem_desc_k_sw128(uint32_t smem_addr) {
     d |= static_cast<uint64_t>(1u) << 46;                           // version
     d |= static_cast<uint64_t>(2u) << 61;                           // SWIZZLE_128B
     return d;
+}
+
+// Shared-memory matrix descriptor, K-major, no swizzle: 8-row x 16-byte core
+// matrices, rows 16 bytes apart inside one; `lbo` = byte offset between core
+// matrices adjacent in K, `sbo` = between core matrices adjacent in M / N.
+__device__ __forceinline__ uint64_t smem_desc_k_none(uint32_t smem_addr, uint32_t lbo, uint32_t sbo) {
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((smem_addr & 0x3FFFFu) >> 4);      // start address
+    d |= static_cast<uint64_t>((lbo & 0x3FFFFu) >> 4) << 16;       // LBO
+    d |= static_cast<uint64_t>((sbo & 0x3FFFFu) >> 4) << 32;       // SBO
+    d |= static_cast<uint64_t>(1u) << 46;                           // version
+    return d;                                                       // layout 0: no swizzle
+}
+
+// Generic-proxy writes to shared memory made visible to the async proxy
+// (tcgen05.mma operands written by plain stores).
+__device__ __forceinline__ void fence_proxy_async_shared() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
 // Instruction descriptor: fp32 accumulator, A/B format code (tf32 = 2,

@@ -31,28 +31,41 @@ constexpr int kBKH = 64;                          // halves per 128-byte k-block
 constexpr int kATileBytesH = kBM * 128;           // 16 KB
 constexpr int kBTileBytesH = kBN * 128;           // 32 KB
 constexpr int kMaxStagesH = 6;
-constexpr int kSmemBudgetH = 7 * kBTileBytesH;    // 224 KB for A + ring
 constexpr int kMaxResidentKb = 6;                 // d_pad <= 384 keeps A resident
 constexpr int kBarBytesH = 256;                   // mbarriers, TMEM slot, abort flag
 constexpr int kBiasBytesH = kBN * 4;              // one tile's score bias (fp32)
+// Folded L2 bias (kFold): one more K = 16 MMA step per tile adds -||x||^2 / 2,
+// held as three bf16 parts per row, to the accumulator (A = a tile of ones),
+// so the accumulator is half the score and the epilogue compares it as it is.
+constexpr int kFoldSlots = 4;                     // bias tiles in flight (loaded one tile ahead)
+constexpr int kFoldSlotBytes = kBN * 16;          // 256 rows x 8 bf16: the 3 parts, then zeros
+constexpr int kOnesBytes = kBM * 16;              // 128 rows x 8 bf16: 1, 1, 1, 0, ...
+constexpr int kZeroBytes = kBN * 16;              // K columns 8..15 of both operands
+constexpr int kFoldBytes = kFoldSlots * kFoldSlotBytes + kOnesBytes + kZeroBytes;
+constexpr int kSmemMaxH = 232448;                 // opt-in shared memory per CTA
+constexpr uint32_t kOneBf16x2 = 0x3F803F80u;      // two bf16 1.0
 
 __host__ __device__ inline bool a_streamed(int kb) { return kb > kMaxResidentKb; }
 __host__ __device__ inline int stage_bytes_h(int kb) {
     return a_streamed(kb) ? kATileBytesH + kBTileBytesH : kBTileBytesH;
 }
-__host__ __device__ inline int n_stages_h(int kb) {
+__host__ __device__ inline int extra_bytes_h(bool fold) { return fold ? kFoldBytes : 2 * kBiasBytesH; }
+__host__ __device__ inline int n_stages_h(int kb, bool fold) {
     const int a = a_streamed(kb) ? 0 : kb * kATileBytesH;
-    const int s = (kSmemBudgetH - a) / stage_bytes_h(kb);
+    const int budget = kSmemMaxH - kBarBytesH - extra_bytes_h(fold);
+    const int s = (budget - a) / stage_bytes_h(kb);
     return s > kMaxStagesH ? kMaxStagesH : s;
 }
 
 struct SmemH {
     uint8_t* a;         // resident A [kb][16 KB] (resident mode)
     uint8_t* ring;      // [stages][stage bytes]: ([A 16 KB]) [B 32 KB]
-    uint64_t *full, *empty, *a_full, *a_empty, *acc_full, *acc_empty, *drain, *bias_full;
+    uint64_t *full, *empty, *a_full, *a_empty, *acc_full, *acc_empty, *drain;
+    uint64_t* bias_full;   // [2] (bias copy of accumulator buffer b) or [kFoldSlots]
     uint32_t* tmem_slot;
     int* abort_flag;
     float* bias;        // [2][kBN]: score bias of the tile in accumulator buffer b
+    uint8_t* fold;      // kFold: [kFoldSlots][4 KB] bias parts, ones [2 KB], zeros [4 KB]
 };
 
 __device__ inline SmemH carve_h(uint8_t* base, int kb, int stages) {
@@ -67,17 +80,18 @@ __device__ inline SmemH carve_h(uint8_t* base, int kb, int stages) {
     S.acc_full = S.a_full + 2;
     S.acc_empty = S.a_full + 4;
     S.drain = S.a_full + 6;
-    S.bias_full = S.a_full + 7;
-    S.tmem_slot = reinterpret_cast<uint32_t*>(S.a_full + 9);
+    S.bias_full = S.a_full + 7;                          // up to kFoldSlots barriers
+    S.tmem_slot = reinterpret_cast<uint32_t*>(S.bias_full + kFoldSlots);
     S.abort_flag = reinterpret_cast<int*>(S.tmem_slot + 1);
     S.bias = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + kBarBytesH);
+    S.fold = reinterpret_cast<uint8_t*>(bars) + kBarBytesH;
     return S;
 }
 
-template <int KP, bool kBuf, bool kBF16>
+template <int KP, bool kBuf, bool kBF16, bool kFold>
 __global__ void __launch_bounds__(threads_h(kBuf), 1)
 screen_f16_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
-                  const ScreenParams p) {
+                  const __grid_constant__ CUtensorMap tm_bias, const ScreenParams p) {
     // SWIZZLE_128B tiles need 1024-byte aligned shared memory.  The declared
     // alignment is checked, not assumed: a misaligned base ends the launch
     // with a configuration error before any copy is issued.
@@ -89,10 +103,11 @@ screen_f16_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
         return;
     }
     const bool stream_a = a_streamed(kb_count);
-    const int stages = n_stages_h(kb_count);
+    const int stages = n_stages_h(kb_count, kFold);
     const int sbytes = stage_bytes_h(kb_count);
     SmemH S = carve_h(base, kb_count, stages);
     constexpr uint32_t kIdesc = make_idesc(kBF16 ? 1u : 0u, kBM, kBN);
+    constexpr uint32_t kIdescBias = make_idesc(1u, kBM, kBN);   // the bias step is bf16
 
     constexpr int kEpiWG = epi_wg(kBuf);
     constexpr int kProducerWarpH = kEpiWG * 4;
@@ -112,10 +127,21 @@ screen_f16_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
             mbar_init(&S.acc_empty[b], kEpiWG * 4);   // one arrival per epilogue warp
         }
         mbar_init(S.drain, 1);
-        mbar_init(&S.bias_full[0], 1);
-        mbar_init(&S.bias_full[1], 1);
+        for (int s = 0; s < kFoldSlots; ++s) mbar_init(&S.bias_full[s], 1);
         *S.abort_flag = 0;
         fence_mbar_init();
+    }
+    if constexpr (kFold) {
+        // the constant operand rows of the bias step: A = (1, 1, 1, 0, ...),
+        // and zeros for K columns 8..15 of A and B; written once, then made
+        // visible to the tensor core's (async-proxy) reads
+        uint4* ones = reinterpret_cast<uint4*>(S.fold + kFoldSlots * kFoldSlotBytes);
+        uint4* zeros = ones + kOnesBytes / 16;
+        for (int i = threadIdx.x; i < kOnesBytes / 16 + kZeroBytes / 16; i += blockDim.x) {
+            if (i < kOnesBytes / 16) ones[i] = make_uint4(kOneBf16x2, kOneBf16x2 & 0xFFFFu, 0u, 0u);
+            else zeros[i - kOnesBytes / 16] = make_uint4(0u, 0u, 0u, 0u);
+        }
+        fence_proxy_async_shared();
     }
     if (warp == kMmaWarpH) {
         tmem_alloc(S.tmem_slot, 512);
@@ -124,6 +150,7 @@ screen_f16_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
     if (warp == kProducerWarpH && lane == 0) {
         tma_prefetch_desc(&tm_a);
         tma_prefetch_desc(&tm_b);
+        if constexpr (kFold) tma_prefetch_desc(&tm_bias);
     }
     tc_fence_before();
     __syncthreads();
@@ -146,7 +173,7 @@ screen_f16_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
                 const int t0 = ch * p.tiles_per_chunk;
                 const int t1 = min(t0 + p.tiles_per_chunk, p.n_tiles);
                 if (!stream_a) {
-                    if (!mbar_wait(S.a_empty, a_phase ^ 1u, abort_flag)) { ok = false; break; }
+                    if (!mbar_wait(S.a_empty, a_phase ^ 1u, abort_flag, p.wait_ns)) { ok = false; break; }
                     mbar_arrive_expect_tx(S.a_full, static_cast<uint32_t>(kb_count * kATileBytesH));
                     for (int kb = 0; kb < kb_count; ++kb)
                         tma_load_2d(&tm_a, S.a_full, S.a + kb * kATileBytesH, kb * kBKH, qt * kBM);
@@ -156,7 +183,7 @@ screen_f16_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
                 }
                 for (int t = t0; t < t1 && ok; ++t) {
                     for (int kb = 0; kb < kb_count; ++kb) {
-                        if (!mbar_wait(&S.empty[stage], sphase ^ 1u, abort_flag)) { ok = false; break; }
+                        if (!mbar_wait(&S.empty[stage], sphase ^ 1u, abort_flag, p.wait_ns)) { ok = false; break; }
                         uint8_t* st = S.ring + stage * sbytes;
                         mbar_arrive_expect_tx(&S.full[stage], static_cast<uint32_t>(sbytes));
                         if (stream_a) {
@@ -183,31 +210,60 @@ screen_f16_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
             uint32_t sphase = 0, a_phase = 0, tcount = 0;
             uint32_t bias_pending = 0, bias_phase = 0;   // bias copies issued (drain on abort)
             bool ok = true, issued_any = false;
+            // kFold: the bias parts of the CTA's tile number tc go to slot tc % 4,
+            // loaded one tile ahead.  Slot (tc + 1) % 4 last served tile tc - 3,
+            // whose bias step has completed once acc_empty of tile tc has been
+            // observed (the epilogue had received tile tc - 2, committed after it).
+            const uint32_t ones = smem_u32(S.fold + kFoldSlots * kFoldSlotBytes);
+            const uint32_t zeros = ones + kOnesBytes;
+            auto load_bias_parts = [&](uint32_t tc, int tile) {
+                const uint32_t sl = tc % kFoldSlots;
+                mbar_arrive_expect_tx(&S.bias_full[sl], kFoldSlotBytes);
+                tma_load_2d(&tm_bias, &S.bias_full[sl], S.fold + sl * kFoldSlotBytes, 0,
+                            tile * p.tile_stride * kBN);
+                bias_pending |= 1u << sl;
+                bias_phase = (bias_phase & ~(1u << sl)) | (((tc / kFoldSlots) & 1u) << sl);
+            };
+            if constexpr (kFold) {
+                if (static_cast<int>(blockIdx.x) < n_units)
+                    load_bias_parts(0, (blockIdx.x / p.n_qtiles) * p.tiles_per_chunk);
+            }
             for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
                 const int ch = u / p.n_qtiles;
                 const int t0 = ch * p.tiles_per_chunk;
                 const int t1 = min(t0 + p.tiles_per_chunk, p.n_tiles);
                 if (!stream_a) {
-                    if (!mbar_wait(S.a_full, a_phase, abort_flag)) { ok = false; break; }
+                    if (!mbar_wait(S.a_full, a_phase, abort_flag, p.wait_ns)) { ok = false; break; }
                     a_phase ^= 1u;
                     tc_fence_after();
                 }
                 for (int t = t0; t < t1 && ok; ++t, ++tcount) {
                     const uint32_t b = tcount & 1u;
                     const uint32_t ph = (tcount >> 1) & 1u;
-                    if (!mbar_wait(&S.acc_empty[b], ph ^ 1u, abort_flag)) { ok = false; break; }
+                    if (!mbar_wait(&S.acc_empty[b], ph ^ 1u, abort_flag, p.wait_ns)) { ok = false; break; }
                     tc_fence_after();
-                    // the epilogue is done with buffer b's tile (two tiles back),
-                    // so its bias slot takes this tile's bias; the copy lands
-                    // while the MMAs run
-                    mbar_arrive_expect_tx(&S.bias_full[b], kBiasBytesH);
-                    bulk_load_g2s(S.bias + b * kBN, p.colbias + static_cast<int64_t>(t) * p.tile_stride * kBN,
-                                  kBiasBytesH, &S.bias_full[b]);
-                    bias_pending |= 1u << b;
-                    bias_phase = (bias_phase & ~(1u << b)) | (ph << b);
+                    if constexpr (kFold) {
+                        // the CTA's next tile: the rest of this unit, else the
+                        // first tile of its next unit
+                        int nt = -1;
+                        if (t + 1 < t1) nt = t + 1;
+                        else if (u + static_cast<int>(gridDim.x) < n_units)
+                            nt = ((u + static_cast<int>(gridDim.x)) / p.n_qtiles) * p.tiles_per_chunk;
+                        if (nt >= 0) load_bias_parts(tcount + 1, nt);
+                    } else {
+                        // the epilogue is done with buffer b's tile (two tiles
+                        // back), so its bias slot takes this tile's bias; the copy
+                        // lands while the MMAs run
+                        mbar_arrive_expect_tx(&S.bias_full[b], kBiasBytesH);
+                        bulk_load_g2s(S.bias + b * kBN,
+                                      p.colbias + static_cast<int64_t>(t) * p.tile_stride * kBN,
+                                      kBiasBytesH, &S.bias_full[b]);
+                        bias_pending |= 1u << b;
+                        bias_phase = (bias_phase & ~(1u << b)) | (ph << b);
+                    }
                     const uint32_t d_tmem = tmem_base + b * kBN;
                     for (int kb = 0; kb < kb_count; ++kb) {
-                        if (!mbar_wait(&S.full[stage], sphase, abort_flag)) { ok = false; break; }
+                        if (!mbar_wait(&S.full[stage], sphase, abort_flag, p.wait_ns)) { ok = false; break; }
                         tc_fence_after();
                         const uint32_t st = smem_u32(S.ring + stage * sbytes);
                         const uint64_t ad = smem_desc_k_sw128(
@@ -222,6 +278,20 @@ screen_f16_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
                         tc_commit(&S.empty[stage]);
                         if (++stage == stages) { stage = 0; sphase ^= 1u; }
                     }
+                    if constexpr (kFold) {
+                        if (ok) {
+                            const uint32_t sl = tcount % kFoldSlots;
+                            if (!mbar_wait(&S.bias_full[sl], (tcount / kFoldSlots) & 1u, abort_flag, p.wait_ns)) {
+                                ok = false;
+                            } else {
+                                bias_pending &= ~(1u << sl);
+                                tc_fence_after();
+                                const uint32_t bslot = smem_u32(S.fold + sl * kFoldSlotBytes);
+                                tc_mma_f16(d_tmem, smem_desc_k_none(ones, zeros - ones, 128u),
+                                           smem_desc_k_none(bslot, zeros - bslot, 128u), kIdescBias, 1u);
+                            }
+                        }
+                    }
                     if (ok) tc_commit(&S.acc_full[b]);
                 }
                 if (ok && !stream_a) tc_commit(S.a_empty);
@@ -231,9 +301,9 @@ screen_f16_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
                 mbar_wait_drain(S.drain, 0u, 200000000ull);
             }
             if (*abort_flag) {
-                for (int b = 0; b < 2; ++b)
-                    if (bias_pending & (1u << b))
-                        mbar_wait_drain(&S.bias_full[b], (bias_phase >> b) & 1u, 200000000ull);
+                for (int sl = 0; sl < kFoldSlots; ++sl)
+                    if (bias_pending & (1u << sl))
+                        mbar_wait_drain(&S.bias_full[sl], (bias_phase >> sl) & 1u, 200000000ull);
             }
         }
     } else {
@@ -283,12 +353,15 @@ screen_f16_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
                 // one lane polls the barriers, the warp follows
                 bool ready = true;
                 if (lane == 0)
-                    ready = mbar_wait(&S.acc_full[b], ph, abort_flag) &&
-                            mbar_wait(&S.bias_full[b], ph, abort_flag);
+                    ready = mbar_wait(&S.acc_full[b], ph, abort_flag, p.wait_ns) &&
+                            (kFold || mbar_wait(&S.bias_full[b], ph, abort_flag, p.wait_ns));
                 if (!__shfl_sync(0xffffffffu, ready ? 1 : 0, 0)) { ok = false; break; }
+                // with the bias folded into the MMA the accumulator is half the
+                // score: it is compared against half the floor (exact)
                 const float floor_adj =
-                    !live ? __int_as_float(0x7f800000)
-                          : (p.use_floor ? floor_below(fkey) : -__int_as_float(0x7f800000));
+                    (!live ? __int_as_float(0x7f800000)
+                           : (p.use_floor ? floor_below(fkey) : -__int_as_float(0x7f800000))) *
+                    (kFold ? 0.5f : 1.0f);
                 const int id_tile = t * p.tile_stride * kBN + g * kCols;
                 const float* cb_tile = S.bias + b * kBN + g * kCols;   // shared memory
                 const uint32_t taddr = lane_addr + b * kBN + g * kCols;
@@ -306,10 +379,11 @@ screen_f16_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
                         float4 cb[8];
                         __syncwarp();
                         tmem_ld_32x32b_x32(taddr + c * 32, r);
-                        if (!raw) load_bias_shared(cb, cb_tile + c * 32);
+                        if (!kFold && !raw) load_bias_shared(cb, cb_tile + c * 32);
                         tmem_wait_ld_regs(r);
                         if (c == kCols / 32 - 1) release_acc(b);
-                        if (raw) buffer_chunk_raw(r, floor_adj, br, st, id_tile + c * 32);
+                        if (kFold) buffer_chunk_raw(r, floor_adj, 2.0f, br, st, id_tile + c * 32);
+                        else if (raw) buffer_chunk_raw(r, floor_adj, 1.0f, br, st, id_tile + c * 32);
                         else buffer_chunk(r, cb, p.alpha, floor_adj, br, st, id_tile + c * 32);
                     }
                 } else {
@@ -322,13 +396,13 @@ screen_f16_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
                     tmem_ld_32x32b_x32(taddr, ra);
 #pragma unroll 1
                     for (int c = 0; c < kCols / 32; c += 2) {
-                        if (!raw) load_bias_shared(cb, cb_tile + c * 32);
+                        if (!kFold && !raw) load_bias_shared(cb, cb_tile + c * 32);
                         tmem_wait_ld_regs(ra);
                         __syncwarp();
                         tmem_ld_32x32b_x32(taddr + (c + 1) * 32, rb);
-                        if (raw) scan_chunk_raw<KP>(ra, floor_adj, L, id_tile + c * 32);
+                        if (kFold || raw) scan_chunk_raw<KP>(ra, floor_adj, L, id_tile + c * 32);
                         else scan_chunk<KP>(ra, cb, p.alpha, floor_adj, L, id_tile + c * 32);
-                        if (!raw) load_bias_shared(cb, cb_tile + (c + 1) * 32);
+                        if (!kFold && !raw) load_bias_shared(cb, cb_tile + (c + 1) * 32);
                         tmem_wait_ld_regs(rb);
                         if (c + 2 < kCols / 32) {
                             __syncwarp();
@@ -336,7 +410,7 @@ screen_f16_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
                         } else {
                             release_acc(b);
                         }
-                        if (raw) scan_chunk_raw<KP>(rb, floor_adj, L, id_tile + (c + 1) * 32);
+                        if (kFold || raw) scan_chunk_raw<KP>(rb, floor_adj, L, id_tile + (c + 1) * 32);
                         else scan_chunk<KP>(rb, cb, p.alpha, floor_adj, L, id_tile + (c + 1) * 32);
                     }
                 }
@@ -347,12 +421,15 @@ screen_f16_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
                 const int64_t o = (static_cast<int64_t>(ch * kEpiWG + g) * p.m_pad + row) * KP;
                 float4* ps = reinterpret_cast<float4*>(p.part_score + o);
                 int4* pi = reinterpret_cast<int4*>(p.part_id + o);
+                const float sc = kFold ? 2.0f : 1.0f;   // list entries back to score units
 #pragma unroll
                 for (int i = 0; i < KP / 4; ++i) {
-                    ps[i] = make_float4(L.s[4 * i], L.s[4 * i + 1], L.s[4 * i + 2], L.s[4 * i + 3]);
+                    ps[i] = make_float4(sc * L.s[4 * i], sc * L.s[4 * i + 1], sc * L.s[4 * i + 2],
+                                        sc * L.s[4 * i + 3]);
                     pi[i] = make_int4(L.id[4 * i], L.id[4 * i + 1], L.id[4 * i + 2], L.id[4 * i + 3]);
                 }
-                if (p.use_floor && L.id[KP - 1] >= 0) atomicMax(p.thr + row, score_key(L.s[KP - 1]));
+                if (p.use_floor && L.id[KP - 1] >= 0)
+                    atomicMax(p.thr + row, score_key(sc * L.s[KP - 1]));
             }
         }
     }
@@ -364,42 +441,46 @@ screen_f16_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
     if (threadIdx.x == 0 && *abort_flag) atomicExch(p.err, *abort_flag);
 }
 
-template <int KP, bool kBuf, bool kBF16>
-cudaError_t launch_h(const CUtensorMap& a, const CUtensorMap& b, const ScreenParams& p, int grid,
-                     cudaStream_t stream) {
-    const int smem = screen_f16_smem_bytes(p.d_pad);
-    cudaError_t e = cudaFuncSetAttribute(screen_f16_kernel<KP, kBuf, kBF16>,
+template <int KP, bool kBuf, bool kBF16, bool kFold>
+cudaError_t launch_h(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& bias,
+                     const ScreenParams& p, int grid, cudaStream_t stream) {
+    const int smem = screen_f16_smem_bytes(p.d_pad, kFold);
+    cudaError_t e = cudaFuncSetAttribute(screen_f16_kernel<KP, kBuf, kBF16, kFold>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
-    screen_f16_kernel<KP, kBuf, kBF16><<<grid, threads_h(kBuf), smem, stream>>>(a, b, p);
+    screen_f16_kernel<KP, kBuf, kBF16, kFold><<<grid, threads_h(kBuf), smem, stream>>>(a, b, bias, p);
     return cudaGetLastError();
 }
 
-template <bool kBF16>
-cudaError_t launch_h_kp(int kp, const CUtensorMap& a, const CUtensorMap& b, const ScreenParams& p,
-                        int grid, cudaStream_t stream) {
+template <bool kBF16, bool kFold>
+cudaError_t launch_h_kp(int kp, const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& bias,
+                        const ScreenParams& p, int grid, cudaStream_t stream) {
     switch (kp) {
-        case 0: return launch_h<4, true, kBF16>(a, b, p, grid, stream);
-        case 4: return launch_h<4, false, kBF16>(a, b, p, grid, stream);
-        case 8: return launch_h<8, false, kBF16>(a, b, p, grid, stream);
-        case 16: return launch_h<16, false, kBF16>(a, b, p, grid, stream);
+        case 0: return launch_h<4, true, kBF16, kFold>(a, b, bias, p, grid, stream);
+        case 4: return launch_h<4, false, kBF16, kFold>(a, b, bias, p, grid, stream);
+        case 8: return launch_h<8, false, kBF16, kFold>(a, b, bias, p, grid, stream);
+        case 16: return launch_h<16, false, kBF16, kFold>(a, b, bias, p, grid, stream);
         default: return cudaErrorInvalidValue;
     }
 }
 
 }  // namespace
 
-int screen_f16_smem_bytes(int d_pad) {
+int screen_f16_smem_bytes(int d_pad, bool fold) {
     const int kb = d_pad / kBKH;
     const int a = a_streamed(kb) ? 0 : kb * kATileBytesH;
-    return a + n_stages_h(kb) * stage_bytes_h(kb) + kBarBytesH + 2 * kBiasBytesH;
+    return a + n_stages_h(kb, fold) * stage_bytes_h(kb) + kBarBytesH + extra_bytes_h(fold);
 }
 
 cudaError_t launch_screen_f16(int kp, bool bf16, const CUtensorMap& a, const CUtensorMap& b,
-                              const ScreenParams& p, int grid, cudaStream_t stream) {
+                              const CUtensorMap* fold_bias, const ScreenParams& p, int grid,
+                              cudaStream_t stream) {
     if (p.d_pad % kBKH != 0 || p.d_pad < kBKH) return cudaErrorInvalidValue;
-    return bf16 ? launch_h_kp<true>(kp, a, b, p, grid, stream)
-                : launch_h_kp<false>(kp, a, b, p, grid, stream);
+    if (fold_bias)
+        return bf16 ? launch_h_kp<true, true>(kp, a, b, *fold_bias, p, grid, stream)
+                    : launch_h_kp<false, true>(kp, a, b, *fold_bias, p, grid, stream);
+    return bf16 ? launch_h_kp<true, false>(kp, a, b, b, p, grid, stream)
+                : launch_h_kp<false, false>(kp, a, b, b, p, grid, stream);
 }
 
 }  // namespace mflat_cu

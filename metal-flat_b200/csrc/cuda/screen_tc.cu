@@ -162,7 +162,7 @@ screen_bf16x3_kernel(const __grid_constant__ CUtensorMap tm_a_h,
                 const int t0 = ch * p.tiles_per_chunk;
                 const int t1 = min(t0 + p.tiles_per_chunk, p.n_tiles);
                 if (!stream_a) {
-                    if (!mbar_wait(S.a_empty, a_phase ^ 1u, abort_flag)) { ok = false; break; }
+                    if (!mbar_wait(S.a_empty, a_phase ^ 1u, abort_flag, p.wait_ns)) { ok = false; break; }
                     mbar_arrive_expect_tx(S.a_full, static_cast<uint32_t>(kb_count * 2 * kATileBytes));
                     for (int kb = 0; kb < kb_count; ++kb) {
                         tma_load_2d(&tm_a_h, S.a_full, S.a + kb * kATileBytes, kb * kBK, qt * kBM);
@@ -176,7 +176,7 @@ screen_bf16x3_kernel(const __grid_constant__ CUtensorMap tm_a_h,
                 for (int t = t0; t < t1 && ok; ++t) {
                     for (int kb = 0; kb < kb_count && ok; ++kb) {
                         for (int plane = 0; plane < 2; ++plane) {
-                            if (!mbar_wait(&S.empty[stage], sphase ^ 1u, abort_flag)) { ok = false; break; }
+                            if (!mbar_wait(&S.empty[stage], sphase ^ 1u, abort_flag, p.wait_ns)) { ok = false; break; }
                             uint8_t* dst = S.b + stage * sbytes;
                             mbar_arrive_expect_tx(&S.full[stage], static_cast<uint32_t>(sbytes));
                             if (stream_a) {
@@ -208,12 +208,15 @@ screen_bf16x3_kernel(const __grid_constant__ CUtensorMap tm_a_h,
             uint32_t tcount = 0;
             bool ok = true;
             bool issued_any = false;
+            // test hook: the drain barrier completes no phase before an abort,
+            // so this bounded wait runs out and the CTA takes its error path
+            if (p.test_stall) ok = mbar_wait(S.drain, 0u, abort_flag, p.wait_ns) && false;
             for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
                 const int ch = u / p.n_qtiles;
                 const int t0 = ch * p.tiles_per_chunk;
                 const int t1 = min(t0 + p.tiles_per_chunk, p.n_tiles);
                 if (!stream_a) {
-                    if (!mbar_wait(S.a_full, a_phase, abort_flag)) { ok = false; break; }
+                    if (!mbar_wait(S.a_full, a_phase, abort_flag, p.wait_ns)) { ok = false; break; }
                     a_phase ^= 1u;
                     tc_fence_after();
                 }
@@ -221,7 +224,7 @@ screen_bf16x3_kernel(const __grid_constant__ CUtensorMap tm_a_h,
                 for (int t = t0; t < t1 && ok; ++t, ++tcount) {
                     const uint32_t b = tcount & 1u;
                     const uint32_t ph = (tcount >> 1) & 1u;
-                    if (!mbar_wait(&S.acc_empty[b], ph ^ 1u, abort_flag)) { ok = false; break; }
+                    if (!mbar_wait(&S.acc_empty[b], ph ^ 1u, abort_flag, p.wait_ns)) { ok = false; break; }
                     tc_fence_after();
                     const uint32_t d_tmem = tmem_base + b * kBN;
                     for (int kb = 0; kb < kb_count && ok && stream_a; ++kb) {
@@ -232,8 +235,8 @@ screen_bf16x3_kernel(const __grid_constant__ CUtensorMap tm_a_h,
                         const int s_l = stage;
                         const uint32_t ph_l = sphase;
                         if (++stage == stages) { stage = 0; sphase ^= 1u; }
-                        if (!mbar_wait(&S.full[s_h], ph_h, abort_flag) ||
-                            !mbar_wait(&S.full[s_l], ph_l, abort_flag)) { ok = false; break; }
+                        if (!mbar_wait(&S.full[s_h], ph_h, abort_flag, p.wait_ns) ||
+                            !mbar_wait(&S.full[s_l], ph_l, abort_flag, p.wait_ns)) { ok = false; break; }
                         tc_fence_after();
                         const uint32_t base_h = smem_u32(S.b + s_h * sbytes);
                         const uint32_t base_l = smem_u32(S.b + s_l * sbytes);
@@ -258,7 +261,7 @@ screen_bf16x3_kernel(const __grid_constant__ CUtensorMap tm_a_h,
                         const uint64_t a_l =
                             smem_desc_k_sw128(a_addr + (kb_count + kb) * kATileBytes);
                         // stage holding B_h of this k-block
-                        if (!mbar_wait(&S.full[stage], sphase, abort_flag)) { ok = false; break; }
+                        if (!mbar_wait(&S.full[stage], sphase, abort_flag, p.wait_ns)) { ok = false; break; }
                         tc_fence_after();
                         uint64_t bd = smem_desc_k_sw128(smem_u32(S.b + stage * kStageBytes));
 #pragma unroll
@@ -272,7 +275,7 @@ screen_bf16x3_kernel(const __grid_constant__ CUtensorMap tm_a_h,
                         tc_commit(&S.empty[stage]);
                         if (++stage == stages) { stage = 0; sphase ^= 1u; }
                         // stage holding B_l of this k-block
-                        if (!mbar_wait(&S.full[stage], sphase, abort_flag)) { ok = false; break; }
+                        if (!mbar_wait(&S.full[stage], sphase, abort_flag, p.wait_ns)) { ok = false; break; }
                         tc_fence_after();
                         bd = smem_desc_k_sw128(smem_u32(S.b + stage * kStageBytes));
 #pragma unroll
@@ -331,7 +334,7 @@ screen_bf16x3_kernel(const __grid_constant__ CUtensorMap tm_a_h,
                     prefetch_l1(p.colbias + static_cast<int64_t>(t + 1) * p.tile_stride * kBN + lane * 32);
                 // one lane polls the barrier, the warp follows
                 bool ready = true;
-                if (lane == 0) ready = mbar_wait(&S.acc_full[b], ph, abort_flag);
+                if (lane == 0) ready = mbar_wait(&S.acc_full[b], ph, abort_flag, p.wait_ns);
                 if (!__shfl_sync(0xffffffffu, ready ? 1 : 0, 0)) { ok = false; break; }
                 const float floor_adj =
                     !live ? __int_as_float(0x7f800000)

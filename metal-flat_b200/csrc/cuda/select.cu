@@ -182,10 +182,15 @@ __global__ void __launch_bounds__(128) select_exact_kernel(const SelectParams p)
     const int lane = threadIdx.x & 31;
     const int qi = blockIdx.x * 4 + (threadIdx.x >> 5);
     if (qi >= p.m) return;                      // uniform per warp
+    if (*p.err != 0) return;                    // the screen failed: its lists are not valid
     uint64_t top = warp_merge_lists<KP>(p.part_score, p.part_id, p.n_chunks, p.m_pad, qi, lane);
     if (lane >= KP) top = 0ull;                 // only the merged top-KP are proven candidates
     const float s_screen = key_score(top);
     const int id = key_id(top);
+    if (__any_sync(kFull, id >= p.n)) {         // never produced by a screen: report, read nothing
+        if (lane == 0) atomicExch(p.err, kErrInternal);
+        return;
+    }
     const int n_valid = __popc(__ballot_sync(kFull, id >= 0));
 
     // proof that the true top-k is inside the candidates
@@ -349,6 +354,7 @@ __global__ void __launch_bounds__(128) kmeans_select_kernel(const SelectParams p
     const int lane = threadIdx.x & 31;
     const int qi = blockIdx.x * 4 + (threadIdx.x >> 5);
     if (qi >= p.m) return;
+    if (*p.err != 0) return;                    // the screen failed: its lists are not valid
     float sel_s[KP];
     int sel_id[KP];
     int head = 0;
@@ -365,8 +371,16 @@ __global__ void __launch_bounds__(128) kmeans_select_kernel(const SelectParams p
         if (w.id >= 0 && w.owner == lane) ++head;
     }
     int n_valid = 0;
+    bool bad_id = false;
 #pragma unroll
-    for (int i = 0; i < KP; ++i) n_valid += sel_id[i] >= 0 ? 1 : 0;
+    for (int i = 0; i < KP; ++i) {
+        n_valid += sel_id[i] >= 0 ? 1 : 0;
+        bad_id |= sel_id[i] >= p.n;
+    }
+    if (bad_id) {                               // never produced by a screen: report, read nothing
+        if (lane == 0) atomicExch(p.err, kErrInternal);
+        return;
+    }
     const double qn = p.qnorm[qi];
     const double xmax = static_cast<double>(__uint_as_float(*p.xmax_bits));
     const double E = error_bound(kL2, qn, xmax, p.gamma);

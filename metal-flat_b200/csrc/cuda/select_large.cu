@@ -165,6 +165,7 @@ __device__ __forceinline__ double bound_e(int metric, double qn, double xmax, do
 __global__ void __launch_bounds__(kSelThreads) select_large_kernel(const LargeSelectParams p) {
     const int qi = blockIdx.x;
     if (qi >= p.m) return;
+    if (p.err && *p.err != 0) return;                     // a screen failed: buffers not valid
     __shared__ uint32_t hist[256];
     __shared__ uint32_t sh_prefix;
     __shared__ int sh_remaining, sh_pos, sh_tpos, sh_status;
@@ -265,6 +266,11 @@ __global__ void __launch_bounds__(kSelThreads) select_large_kernel(const LargeSe
         const float* qx = p.q_x + static_cast<int64_t>(qi) * p.d_pad;
         for (int i = threadIdx.x; i < cnt; i += blockDim.x) {
             const int64_t id = ids[i];
+            if (id < 0 || id >= p.n) {                  // never produced by a screen
+                atomicExch(const_cast<int*>(p.err), kErrInternal);
+                key[i] = -DBL_MAX;
+                continue;
+            }
             key[i] = exact_score_l(p.metric, qx, p.db_x + id * p.d_pad, p.dim);
         }
         __syncthreads();

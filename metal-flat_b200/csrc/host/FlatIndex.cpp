@@ -265,8 +265,25 @@ bool FlatIndex::load(const char* path) {
         std::fclose(f);
         return false;
     }
-    raise_status(mflat_cu_index_reset(dev), "load");
     const size_t row = static_cast<size_t>(h.dim) * elem_bytes(mImpl->storage);
+    // A short (truncated) file is rejected before anything is replaced, so a
+    // failed load leaves the index as it was.
+    const long here = std::ftell(f);
+    long end = -1;
+    if (here >= 0 && std::fseek(f, 0, SEEK_END) == 0) end = std::ftell(f);
+    if (end < 0 || std::fseek(f, here, SEEK_SET) != 0) {
+        MFLAT_LOG_ERROR("load %s: cannot determine the file size", path);
+        std::fclose(f);
+        return false;
+    }
+    const unsigned long long need = static_cast<unsigned long long>(h.n) * row;
+    if (static_cast<unsigned long long>(end - here) < need) {
+        MFLAT_LOG_ERROR("load %s: file holds %lld of the %llu bytes of rows its header announces",
+                        path, static_cast<long long>(end - here), need);
+        std::fclose(f);
+        return false;
+    }
+    raise_status(mflat_cu_index_reset(dev), "load");
     const int64_t chunk = std::max<int64_t>(1, static_cast<int64_t>(kIoChunkBytes / row));
     std::vector<uint8_t> buf;
     for (int64_t off = 0; off < h.n; off += chunk) {

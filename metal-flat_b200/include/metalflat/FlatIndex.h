@@ -95,7 +95,9 @@ public:
     // then int32 version 1, dim, metric, storage, n, 0, 0), then n x dim stored
     // elements (fp32, or the fp16 / bf16 bit patterns).  save() returns false on an I/O failure.
     // load() replaces this index's rows; it returns false (index unchanged)
-    // when the file is unreadable or its dim / metric / storage differ.
+    // when the file is unreadable, shorter than its header announces, or its
+    // dim / metric / storage differ.  A device failure while the rows are
+    // being appended throws DeviceError.
     bool save(const char* path) const;
     bool load(const char* path);
     // A new index on `device` (-1 = default) with the file's dim, metric and

@@ -2,12 +2,17 @@
 index holds the same rows and returns bit-identical results, for every
 storage precision and metric (Cosine rows are stored normalised and must not
 be normalised again on load)."""
+import os
+import shutil
+import subprocess
 import zlib
 
 import numpy as np
 import pytest
 
 import mflat_b200 as M
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 pytestmark = pytest.mark.gpu
 
@@ -53,3 +58,25 @@ def test_load_into_index_and_empty(tmp_path):
     assert back.size == 0
     ids, dist = back.search(np.zeros((2, 8), np.float32), 3)
     assert (ids == -1).all() and np.isinf(dist).all()
+
+
+def test_truncated_file_leaves_index_unchanged(tmp_path):
+    """FlatIndex::load (C++ API) on an index that holds rows: a file shorter
+    than its header announces is refused before anything is replaced."""
+    if shutil.which("g++") is None:
+        pytest.skip("g++ not available")
+    src = M.FlatIndex(37, "l2")
+    src.add(np.random.default_rng(2).standard_normal((900, 37)).astype(np.float32))
+    full = str(tmp_path / "full.mffl")
+    src.save(full)
+    cut = str(tmp_path / "cut.mffl")
+    with open(full, "rb") as f, open(cut, "wb") as g:
+        g.write(f.read()[: 32 + 600 * 37 * 4 + 5])
+    pkg = os.path.join(ROOT, "metal-flat_b200")
+    exe = str(tmp_path / "cxx_load_probe")
+    subprocess.run(["g++", "-std=c++17", "-O1", "-Wall", "-Werror", "-I", os.path.join(pkg, "include"),
+                    os.path.join(ROOT, "tests", "cxx_load_probe.cpp"), "-L", os.path.join(pkg, "lib"),
+                    "-lmetalflat_c", "-Wl,-rpath," + os.path.join(pkg, "lib"), "-o", exe], check=True)
+    out = subprocess.run([exe, full, cut], capture_output=True, text=True)
+    assert out.returncode == 0, out.stdout + out.stderr
+    assert out.stdout.split() == ["ok", "900"]

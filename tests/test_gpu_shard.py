@@ -29,3 +29,18 @@ def test_sharded_search_matches_oracle():
     r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=600)
     print(r.stdout[-3000:], r.stderr[-3000:])
     assert r.returncode == 0
+
+
+@pytest.mark.skipif(_gpus() < 2, reason="needs at least two GPUs")
+def test_dead_rank_reports_device_error():
+    """Rank 1 leaves between steps; rank 0's next sharded search ends with
+    MFLAT_ERR_DEVICE after the library's NCCL watchdog aborts the communicator
+    (MFLAT_NCCL_TIMEOUT_S), instead of hanging.  NVLS off, plain NCCL."""
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", MFLAT_NCCL_TIMEOUT_S="5")
+    cmd = ["timeout", "-k", "30", "240", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node=2", "--master-addr", "127.0.0.1", "--master-port", "29541",
+           os.path.join(ROOT, "tests", "dead_rank_worker.py")]
+    r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=300)
+    print(r.stdout[-3000:], r.stderr[-3000:])
+    assert "second step status 6" in r.stdout
+    assert "local search after abort ok True" in r.stdout
