@@ -586,7 +586,7 @@ def main():
     # (q_h x_h + q_l x_h + q_h x_l) at the bf16 tensor rate
     passes = 3.0 if fp32 else 1.0
     peak = bf16_peak
-    kernel = "screen_bf16x3_kernel" if fp32 else "screen_f16_kernel"
+    kernel = "screen_kernel"
     if kmeans:
         flops = passes * 2.0 * n_local * qh.shape[0] * wl.dim
         t_s = dev_s / args.steps

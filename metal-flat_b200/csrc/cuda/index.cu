@@ -110,7 +110,7 @@ bool make_map_u16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t r
     return r == CUDA_SUCCESS;
 }
 
-// Bias parts of the folded L2 screen: [rows][8] bf16 (hi, mid, lo, zeros),
+// Bias parts of the screens' bias MMA: [rows][8] bf16 (h, m, l, zeros),
 // 8-wide boxes of 256 rows, no swizzle (the MMA's K-major core-matrix layout).
 bool make_map_bias16(CUtensorMap* map, const void* base, uint64_t rows) {
     if (!get_encoder()) return false;
@@ -126,16 +126,17 @@ bool make_map_bias16(CUtensorMap* map, const void* base, uint64_t rows) {
 }
 
 // ------------------------------------------------------------- kernels
-// b = colbias / 2 (exact) as hi + mid + lo: hi and mid truncated to bf16
-// (round toward zero), lo the remainder (8 bits, exact).  The three parts
-// share b's sign and cover disjoint bit ranges of its 24-bit significand, so
-// every partial sum is exact in fp32 and the tensor core's addition order
-// cannot change the result.  -inf (rows past n) becomes (-inf, 0, 0).
-__global__ void split_bias_kernel(const float* __restrict__ colbias, int64_t rows,
-                                  uint4* __restrict__ out) {
-    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (i >= rows) return;
-    const float b = 0.5f * colbias[i];
+// b = colbias * scale (scale = 1 / alpha, an exact power of two) as
+// h + m + l: h and m truncated to bf16 (round toward zero), l the remainder
+// (8 bits, exact).  The three parts share b's sign and cover disjoint bit
+// ranges of its 24-bit significand, so every partial sum is exact in fp32 and
+// the tensor core's addition order cannot change the result.  -inf (rows past
+// n) becomes (-inf, 0, 0).  Rows [row0, row1).
+__global__ void split_bias_kernel(const float* __restrict__ colbias, int64_t row0, int64_t row1,
+                                  float scale, uint4* __restrict__ out) {
+    const int64_t i = row0 + static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= row1) return;
+    const float b = scale * colbias[i];
     uint16_t h, m = 0, l = 0;
     if (isinf(b)) {
         h = __bfloat16_as_ushort(__float2bfloat16_rn(b));
@@ -362,7 +363,7 @@ cudaError_t grow(mflat_cu_index* ix, int64_t need) {
     int64_t cap = std::max<int64_t>(need, ix->cap + ix->cap / 2);
     cap = (cap + kBN - 1) / kBN * kBN;
     // fp32 storage: x (4 B) + h, l (2 B each) per element; 16-bit: one plane
-    void *x = nullptr, *h = nullptr, *l = nullptr;
+    void *x = nullptr, *h = nullptr, *l = nullptr, *bp = nullptr;
     float *cb = nullptr, *dn = nullptr;
     const bool half = ix->storage != 0;
     const size_t row16 = static_cast<size_t>(ix->d_pad) * 2;
@@ -373,6 +374,9 @@ cudaError_t grow(mflat_cu_index* ix, int64_t need) {
     if (!half && (e = cudaMalloc(&x, cap * row32)) != cudaSuccess) goto bad;
     if ((e = cudaMalloc(&cb, cap * sizeof(float))) != cudaSuccess) goto bad;
     if ((e = cudaMalloc(&dn, cap * sizeof(float))) != cudaSuccess) goto bad;
+    if ((e = cudaMalloc(&bp, cap * sizeof(uint4))) != cudaSuccess) goto bad;
+    if (ix->bias16_rows > 0)
+        cudaMemcpyAsync(bp, ix->bias16, ix->bias16_rows * sizeof(uint4), cudaMemcpyDeviceToDevice, st);
     if (ix->n > 0) {
         cudaMemcpyAsync(h, half ? ix->db16 : static_cast<void*>(ix->db_h), ix->n * row16,
                         cudaMemcpyDeviceToDevice, st);
@@ -391,6 +395,8 @@ cudaError_t grow(mflat_cu_index* ix, int64_t need) {
     cudaFree(ix->db_x);
     cudaFree(ix->colbias);
     cudaFree(ix->dnorm);
+    cudaFree(ix->bias16);
+    ix->bias16 = static_cast<uint4*>(bp);
     if (half) {
         ix->db16 = h;
     } else {
@@ -403,6 +409,7 @@ cudaError_t grow(mflat_cu_index* ix, int64_t need) {
     ix->cap = cap;
     return cudaSuccess;
 bad:
+    cudaFree(bp);
     cudaFree(x);
     cudaFree(h);
     cudaFree(l);
@@ -471,6 +478,27 @@ int check_device_error(mflat_cu_index* ix, cudaStream_t st) {
     return ST_OK;
 }
 
+int prepare_bias_parts(mflat_cu_index* ix, cudaStream_t st, CUtensorMap* map) {
+    const int64_t rows_pad = (ix->n + kBN - 1) / kBN * kBN;
+    if (rows_pad == 0 || !ix->bias16 || rows_pad > ix->cap)
+        return fail(ST_INTERNAL, "screen bias parts: no rows");
+    if (ix->bias16_rows < rows_pad) {
+        const int64_t r0 = ix->bias16_rows;
+        const float scale = ix->metric == kL2 ? 0.5f : 1.0f;   // 1 / alpha
+        split_bias_kernel<<<blocks_for(rows_pad - r0, 256), 256, 0, st>>>(ix->colbias, r0, rows_pad,
+                                                                          scale, ix->bias16);
+        CU_TRY(cudaGetLastError(), "bias parts");
+        ix->bias16_rows = rows_pad;
+    }
+    if (!make_map_bias16(map, ix->bias16, static_cast<uint64_t>(rows_pad)))
+        return fail(ST_DEVICE, "tensor map encoding failed");
+    return ST_OK;
+}
+
+int fp32_lists_per_chunk(const mflat_cu_index* ix) {
+    return ix->force_simt ? 1 : kScreenListsPerChunk;
+}
+
 // The fp32-storage screen over sp's query batch (bf16 planes in ix->q_h /
 // ix->q_l, rows in ix->db_h / ix->db_l), or the CUDA-core cross-check.
 cudaError_t launch_fp32_screen(mflat_cu_index* ix, const ScreenParams& sp_in, int kp, cudaStream_t st) {
@@ -479,15 +507,16 @@ cudaError_t launch_fp32_screen(mflat_cu_index* ix, const ScreenParams& sp_in, in
     sp.wait_ns = ix->wait_ns;
     sp.test_stall = ix->test_stall;
     ix->test_stall = 0;
-    CUtensorMap ta_h, ta_l, tb_h, tb_l;
-    if (!make_map_u16(&ta_h, ix->q_h.p, sp.d_pad, sp.m_pad, kBM) ||
-        !make_map_u16(&ta_l, ix->q_l.p, sp.d_pad, sp.m_pad, kBM) ||
-        !make_map_u16(&tb_h, ix->db_h, sp.d_pad, ix->n, kBN) ||
-        !make_map_u16(&tb_l, ix->db_l, sp.d_pad, ix->n, kBN))
+    ScreenMaps maps;
+    if (!make_map_u16(&maps.a, ix->q_h.p, sp.d_pad, sp.m_pad, kBM) ||
+        !make_map_u16(&maps.a2, ix->q_l.p, sp.d_pad, sp.m_pad, kBM) ||
+        !make_map_u16(&maps.b, ix->db_h, sp.d_pad, ix->n, kBN) ||
+        !make_map_u16(&maps.b2, ix->db_l, sp.d_pad, ix->n, kBN))
         return cudaErrorInvalidValue;
+    if (prepare_bias_parts(ix, st, &maps.bias) != ST_OK) return cudaErrorInvalidValue;
     const int64_t units = static_cast<int64_t>(sp.n_qtiles) * sp.n_chunks;
     const int grid = static_cast<int>(std::min<int64_t>(units, ix->num_sms));
-    return launch_screen_bf16x3(kp, ta_h, ta_l, tb_h, tb_l, sp, grid, st);
+    return launch_screen(kp, ScreenKind::kBF16x3, maps, sp, grid, st);
 }
 
 int run_screen(mflat_cu_index* ix, const float* queries, int m, int kp, int on_device,
@@ -497,7 +526,8 @@ int run_screen(mflat_cu_index* ix, const float* queries, int m, int kp, int on_d
     const int n_tiles = static_cast<int>((ix->n + kBN - 1) / kBN);
     const int n_qtiles = m_pad / kBM;
     int n_chunks = 1, tpc = n_tiles;
-    plan_chunks(n_qtiles, n_tiles, ix->num_sms, max_chunks, n_chunks, tpc);
+    const int lpc = fp32_lists_per_chunk(ix);
+    plan_chunks(n_qtiles, n_tiles, ix->num_sms, max_chunks / lpc, n_chunks, tpc);
 
     const float* qsrc = queries;
     if (!on_device) {
@@ -511,7 +541,7 @@ int run_screen(mflat_cu_index* ix, const float* queries, int m, int kp, int on_d
     CU_TRY(ix->q_h.ensure(static_cast<size_t>(m_pad) * d_pad * 2), "query split");
     CU_TRY(ix->q_l.ensure(static_cast<size_t>(m_pad) * d_pad * 2), "query split");
     CU_TRY(ix->qnorm.ensure(static_cast<size_t>(m_pad) * sizeof(float)), "query norms");
-    const size_t parts = static_cast<size_t>(n_chunks) * m_pad * kp;
+    const size_t parts = static_cast<size_t>(n_chunks) * lpc * m_pad * kp;
     CU_TRY(ix->part_s.ensure(parts * sizeof(float)), "candidate lists");
     CU_TRY(ix->part_i.ensure(parts * sizeof(int32_t)), "candidate lists");
     CU_TRY(ix->thr.ensure(static_cast<size_t>(m_pad) * sizeof(uint32_t)), "score floors");
@@ -550,6 +580,7 @@ int run_screen(mflat_cu_index* ix, const float* queries, int m, int kp, int on_d
     out.m = m;
     out.m_pad = m_pad;
     out.n_chunks = n_chunks;
+    out.n_lists = n_chunks * lpc;
     out.q_x = sp.q_x;
     out.qnorm = ix->qnorm.as<float>();
     out.part_s = sp.part_score;
@@ -635,7 +666,8 @@ cudaError_t launch_pass(mflat_cu_index* ix, const ScreenParams& sp, int kp, cuda
 int search_large(mflat_cu_index* ix, const float* queries, int m, int k_out, int32_t* d_ids,
                  float* d_dist, int on_device, cudaStream_t st) {
     constexpr int kKP1 = 32;
-    const LargePlan P = plan_large(ix->n, k_out, m, kKP1, 2 * k_out, 1, ix->num_sms, buffer_budget());
+    const int lpc = fp32_lists_per_chunk(ix);   // stage-A lists per chunk
+    const LargePlan P = plan_large(ix->n, k_out, m, kKP1, 2 * k_out, lpc, ix->num_sms, buffer_budget());
     const int d_pad = ix->d_pad;
     const int n_tiles = static_cast<int>((ix->n + kBN - 1) / kBN);
     const float* qsrc = queries;
@@ -659,7 +691,7 @@ int search_large(mflat_cu_index* ix, const float* queries, int m, int k_out, int
     CU_TRY(ix->lk_words.ensure(4 * sizeof(int)), "status words");
     CU_TRY(ix->thr_stat.ensure(static_cast<size_t>(bm_pad) * sizeof(uint32_t)), "floors");
     if (P.prepass) {
-        const size_t parts = static_cast<size_t>(P.chunks_a) * bm_pad * kKP1;
+        const size_t parts = static_cast<size_t>(P.chunks_a) * lpc * bm_pad * kKP1;
         CU_TRY(ix->part_s.ensure(parts * sizeof(float)), "pre-pass lists");
         CU_TRY(ix->part_i.ensure(parts * sizeof(int32_t)), "pre-pass lists");
     } else {
@@ -704,7 +736,7 @@ int search_large(mflat_cu_index* ix, const float* queries, int m, int k_out, int
         sp.part_id = ix->part_i.as<int32_t>();
         if (P.prepass) {
             const int rc = estimate_floor(
-                ix, P, sp, 2 * k_out, kKP1, 1,
+                ix, P, sp, 2 * k_out, kKP1, lpc,
                 [&](const ScreenParams& q, int kp) { return launch_pass(ix, q, kp, st); },
                 [&](const ScreenParams& q) { return launch_pass(ix, q, 0, st); },
                 ix->thr_stat.as<uint32_t>(), words, st);
@@ -833,24 +865,14 @@ int search_half(mflat_cu_index* ix, const float* queries, int m, int k_out, int3
     const size_t parts = static_cast<size_t>(2 * std::max(max_lists, 1)) * bm_pad * lk;
     CU_TRY(ix->part_s.ensure(parts * sizeof(float)), "candidate lists");
     CU_TRY(ix->part_i.ensure(parts * sizeof(int32_t)), "candidate lists");
-    CUtensorMap tb;
-    if (!make_map_u16(&tb, ix->db16, d_pad, ix->n, kBN)) return fail(ST_DEVICE, "tensor map encoding failed");
-    // L2: the bias goes into the MMA as three bf16 parts per row (derived from
-    // colbias once per database state), the epilogue compares accumulators
-    const bool fold = ix->metric == kL2;
-    CUtensorMap tbias;
-    if (fold) {
-        const int64_t rows_pad = static_cast<int64_t>(n_tiles) * kBN;
-        if (ix->bias16_n != ix->n) {
-            CU_TRY(ix->bias16.ensure(static_cast<size_t>(rows_pad) * 16), "bias parts");
-            split_bias_kernel<<<blocks_for(rows_pad, 256), 256, 0, st>>>(ix->colbias, rows_pad,
-                                                                          ix->bias16.as<uint4>());
-            CU_TRY(cudaGetLastError(), "bias parts");
-            ix->bias16_n = ix->n;
-        }
-        if (!make_map_bias16(&tbias, ix->bias16.p, rows_pad))
-            return fail(ST_DEVICE, "tensor map encoding failed");
+    ScreenMaps maps;
+    if (!make_map_u16(&maps.b, ix->db16, d_pad, ix->n, kBN)) return fail(ST_DEVICE, "tensor map encoding failed");
+    maps.b2 = maps.b;
+    {
+        const int rc = prepare_bias_parts(ix, st, &maps.bias);
+        if (rc != ST_OK) return rc;
     }
+    const ScreenKind kind = bf16 ? ScreenKind::kBF16 : ScreenKind::kF16;
     if (ix->timing) cudaEventRecord(ix->ev[0], st);
 
     for (int b0 = 0; b0 < m; b0 += P.batch) {
@@ -861,8 +883,9 @@ int search_half(mflat_cu_index* ix, const float* queries, int m, int k_out, int3
             ix->q16.as<uint16_t>(), ix->qsq.as<float>());
         CU_TRY(cudaGetLastError(), "query prep launch");
         CU_TRY(cudaMemsetAsync(ix->thr.p, 0, static_cast<size_t>(mb_pad) * sizeof(uint32_t), st), "floors");
-        CUtensorMap ta;
-        if (!make_map_u16(&ta, ix->q16.p, d_pad, mb_pad, kBM)) return fail(ST_DEVICE, "tensor map encoding failed");
+        if (!make_map_u16(&maps.a, ix->q16.p, d_pad, mb_pad, kBM))
+            return fail(ST_DEVICE, "tensor map encoding failed");
+        maps.a2 = maps.a;
         ScreenParams sp{};
         sp.m = mb;
         sp.m_pad = mb_pad;
@@ -879,7 +902,7 @@ int search_half(mflat_cu_index* ix, const float* queries, int m, int k_out, int3
         auto launch = [&](const ScreenParams& q, int kpp) {
             const int64_t units = static_cast<int64_t>(q.n_qtiles) * q.n_chunks;
             const int grid = static_cast<int>(std::min<int64_t>(units, ix->num_sms));
-            return launch_screen_f16(kpp, bf16, ta, tb, fold ? &tbias : nullptr, q, grid, st);
+            return launch_screen(kpp, kind, maps, q, grid, st);
         };
         if (list_mode) {
             sp.use_floor = 1;
@@ -1025,8 +1048,9 @@ int index_add(mflat_cu_index_t* ix, const void* vectors, int64_t n, int on_devic
         CU_TRY(cudaGetLastError(), "ingest launch");
         if (!on_device) CU_TRY(cudaStreamSynchronize(ix->stream), "ingest");
     }
+    // rows [n_old, rows_pad(n_old)) were padding: their bias parts change
+    ix->bias16_rows = std::min(ix->bias16_rows, ix->n);
     ix->n += n;
-    ix->bias16_n = -1;
     if (on_device) order_after(caller, ix->stream);
     return ST_OK;
 }
@@ -1056,7 +1080,7 @@ int search_list_exact(mflat_cu_index* ix, const float* queries, int m, int k_out
     sel.dim = ix->dim;
     sel.d_pad = ix->d_pad;
     sel.k_out = k_out;
-    sel.n_chunks = run.n_chunks;
+    sel.n_chunks = run.n_lists;
     sel.metric = ix->metric == kL2 ? kL2 : kIP;
     sel.n = ix->n;
     sel.part_score = run.part_s;
@@ -1223,8 +1247,9 @@ void mflat_cu_index_destroy(mflat_cu_index_t* ix) {
                       &ix->part_i, &ix->flag_list, &ix->out_ids, &ix->out_dist, &ix->gather_ids,
                       &ix->gather_dist, &ix->merge_tmp_ids, &ix->merge_tmp_dist, &ix->thr, &ix->thr_stat, &ix->fb_s,
                       &ix->fb_i, &ix->buf_cnt, &ix->buf_s, &ix->buf_i, &ix->lk_words,
-                      &ix->q16, &ix->qsq, &ix->bias16})
+                      &ix->q16, &ix->qsq})
         b->release();
+    cudaFree(ix->bias16);
     for (auto& slot : ix->ring)
         for (auto& ev : slot.ev)
             if (ev) cudaEventDestroy(ev);
@@ -1284,7 +1309,7 @@ int mflat_cu_index_reset(mflat_cu_index_t* ix) {
     cudaMemsetAsync(ix->xmax_bits, 0, sizeof(unsigned), ix->stream);
     CU_TRY(cudaStreamSynchronize(ix->stream), "reset");
     ix->n = 0;
-    ix->bias16_n = -1;
+    ix->bias16_rows = 0;
     return ST_OK;
 }
 

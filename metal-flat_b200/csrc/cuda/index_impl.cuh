@@ -59,6 +59,7 @@ inline unsigned blocks_for(int64_t n, int t) { return static_cast<unsigned>((n +
 // Result of the screen stage of one search (per (query, chunk) top-KP lists).
 struct ScreenRun {
     int kp = 0, m = 0, m_pad = 0, n_chunks = 0;
+    int n_lists = 0;                  // lists per query (chunks x lists per chunk)
     const float* q_x = nullptr;       // fp32 queries [m_pad][d_pad] (exact re-rank)
     const float* qnorm = nullptr;
     const float* part_s = nullptr;
@@ -89,11 +90,12 @@ struct mflat_cu_index {
     mflat_cu::DevBuf thr, thr_stat, fb_s, fb_i;
     mflat_cu::DevBuf buf_cnt, buf_s, buf_i, lk_words;   // large-k candidate buffers
     mflat_cu::DevBuf q16, qsq;                          // 16-bit queries, ||q||^2
-    // 16-bit L2: -||x||^2 / 2 as three bf16 parts per row ([rows][8] bf16,
-    // padding rows -inf), derived from colbias for rows_pad(n) rows; valid
-    // while bias16_n == n (add / reset set it to -1)
-    mflat_cu::DevBuf bias16;
-    int64_t bias16_n = -1;
+    // Screen bias parts: colbias / alpha as three bf16 parts per row
+    // ([cap][8] bf16 = (h, m, l, 0 ...); rows past n: (-inf, 0, 0)), the
+    // operand of the screens' bias MMA.  Allocated with the rows (grow); rows
+    // [0, bias16_rows) are current, add / reset lower it.
+    uint4* bias16 = nullptr;
+    int64_t bias16_rows = 0;
     // Timing (mflat_cu_index_set_timing): each search records 4 events into
     // one slot of a ring and returns without waiting for them; a slot is read
     // (and its device times added to `sum`) only when it is reused, or by
@@ -155,6 +157,12 @@ cudaError_t launch_prep_queries(const float* src, int m, int m_pad, int dim, int
                                 cudaStream_t st);
 bool encode_map_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows,
                      uint32_t box_rows);
+// Bias parts of rows [0, rows_pad(n)) current (a kernel launch on `st` when
+// rows were added; no allocation), and their tensor map.
+int prepare_bias_parts(mflat_cu_index* ix, cudaStream_t st, CUtensorMap* map);
+// Screen lists per chunk of the fp32-storage screen in use (tensor core: 2,
+// MFLAT_SCREEN=simt cross-check: 1).
+int fp32_lists_per_chunk(const mflat_cu_index* ix);
 cudaError_t launch_fill_empty(int32_t* ids, float* dist, int64_t n, float v, cudaStream_t st);
 void plan_screen_chunks(int n_qtiles, int n_tiles, int num_sms, int max_chunks, int& n_chunks,
                         int& tiles_per_chunk);

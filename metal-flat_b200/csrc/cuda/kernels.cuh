@@ -160,23 +160,23 @@ __device__ __forceinline__ bool cand_better(float sa, int ia, float sb, int ib) 
 // ------------------------------------------------------------- launchers
 // All launchers enqueue on `stream` and return the launch status.
 // kp = 0 selects buffer mode (append every score above the floor).
-// fp32 storage: bf16 planes (a_h / a_l: queries, b_h / b_l: rows), 3 x bf16.
-cudaError_t launch_screen_bf16x3(int kp, const CUtensorMap& a_h, const CUtensorMap& a_l,
-                                 const CUtensorMap& b_h, const CUtensorMap& b_l,
-                                 const ScreenParams& p, int grid, cudaStream_t stream);
+// The tensor-core screen (screen.cu).  kF16 / kBF16: 16-bit storage, one
+// plane (maps a, b); kBF16x3: fp32 storage, bf16 split planes (a / a2: the
+// queries' h / l planes, b / b2: the rows').  `bias`: the rows' bias parts,
+// [rows][8] bf16 = (h, m, l, 0, ...) of colbias / alpha, 256-row boxes, no
+// swizzle (split_bias in index.cu).  kp 0 = buffer mode; list mode (kp 4 .. 32)
+// writes two lists per (query, chunk), list index = chunk * 2 + half.
+enum class ScreenKind : int { kF16 = 0, kBF16 = 1, kBF16x3 = 2 };
+struct ScreenMaps {
+    CUtensorMap a, a2, b, b2, bias;
+};
+constexpr int kScreenListsPerChunk = 2;
+cudaError_t launch_screen(int kp, ScreenKind kind, const ScreenMaps& maps, const ScreenParams& p,
+                          int grid, cudaStream_t stream);
+int screen_smem_bytes(int d_pad, bool x3);
 cudaError_t launch_screen_simt(int kp, const ScreenParams& p, cudaStream_t stream);
-// fp16 / bf16 storage (q and db in 16-bit, d_pad a multiple of 64); kp 0 =
-// buffer mode; list mode writes two lists per (query, chunk).
-// fold_bias: tensor map of the L2 bias parts ([rows][8] bf16: -||x||^2 / 2 as
-// hi + mid + lo, then zeros; rows past n: -inf, 0, 0) -- the MMA adds them and
-// the accumulator is half the score; nullptr: bias in the epilogue.
-cudaError_t launch_screen_f16(int kp, bool bf16, const CUtensorMap& a, const CUtensorMap& b,
-                              const CUtensorMap* fold_bias, const ScreenParams& p, int grid,
-                              cudaStream_t stream);
-int screen_f16_smem_bytes(int d_pad, bool fold);
 cudaError_t launch_select_exact(int kp, const SelectParams& p, cudaStream_t stream);
 cudaError_t launch_fallback_exact(const SelectParams& p, int grid, cudaStream_t stream);
-int screen_bf16x3_smem_bytes(int d_pad);
 cudaError_t launch_select_large(const LargeSelectParams& p, cudaStream_t stream);
 // Recall path, list mode: merge n_lists lists per query, write the top k_out
 // with screen distances (L2: max(0, ||q||^2 - s); IP / Cosine: s).

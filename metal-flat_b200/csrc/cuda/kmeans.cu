@@ -72,7 +72,7 @@ extern "C" int mflat_cu_kmeans_assign(const float* points, int64_t n, const floa
     sel.dim = dim;
     sel.d_pad = ix->d_pad;
     sel.k_out = 1;
-    sel.n_chunks = run.n_chunks;
+    sel.n_chunks = run.n_lists;
     sel.metric = kL2;
     sel.n = ix->n;
     sel.part_score = run.part_s;

@@ -41,7 +41,7 @@ constexpr int kNaMaxQueries = 128;                   // one query tile
 constexpr int kNaMaxDim = 128;
 constexpr int kNaMaxK = 21;
 constexpr int kNaKP = 32;
-constexpr int kNaMaxChunks = 32;
+constexpr int kNaMaxChunks = 16;                     // x 2 lists per chunk
 constexpr size_t kNaScratchBytes = size_t(4) << 20; // 4 MiB per device
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNaScratchBytes];
@@ -56,8 +56,8 @@ constexpr size_t kOffQH = kOffQX + align256(size_t(kNaMaxQueries) * kNaMaxDim * 
 constexpr size_t kOffQL = kOffQH + align256(size_t(kNaMaxQueries) * kNaMaxDim * 2);
 constexpr size_t kOffQNorm = kOffQL + align256(size_t(kNaMaxQueries) * kNaMaxDim * 2);
 constexpr size_t kOffPartS = kOffQNorm + align256(size_t(kNaMaxQueries) * 4);
-constexpr size_t kOffPartI = kOffPartS + align256(size_t(kNaMaxChunks) * kNaMaxQueries * kNaKP * 4);
-constexpr size_t kOffThr = kOffPartI + align256(size_t(kNaMaxChunks) * kNaMaxQueries * kNaKP * 4);
+constexpr size_t kOffPartI = kOffPartS + align256(size_t(kNaMaxChunks) * kScreenListsPerChunk * kNaMaxQueries * kNaKP * 4);
+constexpr size_t kOffThr = kOffPartI + align256(size_t(kNaMaxChunks) * kScreenListsPerChunk * kNaMaxQueries * kNaKP * 4);
 constexpr size_t kOffFlag = kOffThr + align256(size_t(kNaMaxQueries) * 4);
 constexpr size_t kOffFbS = kOffFlag + align256(size_t(kNaMaxQueries) * 4);
 constexpr size_t kOffFbI = kOffFbS + align256(size_t(kNaMaxQueries) * kFbChunks * kNaMaxK * 8);
@@ -162,14 +162,18 @@ extern "C" int mflat_cu_index_search_noalloc(mflat_cu_index_t* ix, const float* 
     sp.tile_stride = 1;
     sp.use_floor = 1;
     sp.wait_ns = ix->wait_ns;
-    CUtensorMap ta_h, ta_l, tb_h, tb_l;
-    if (!encode_map_bf16(&ta_h, q_h, d_pad, m_pad, kBM) ||
-        !encode_map_bf16(&ta_l, q_l, d_pad, m_pad, kBM) ||
-        !encode_map_bf16(&tb_h, ix->db_h, d_pad, ix->n, kBN) ||
-        !encode_map_bf16(&tb_l, ix->db_l, d_pad, ix->n, kBN))
+    ScreenMaps maps;
+    if (!encode_map_bf16(&maps.a, q_h, d_pad, m_pad, kBM) ||
+        !encode_map_bf16(&maps.a2, q_l, d_pad, m_pad, kBM) ||
+        !encode_map_bf16(&maps.b, ix->db_h, d_pad, ix->n, kBN) ||
+        !encode_map_bf16(&maps.b2, ix->db_l, d_pad, ix->n, kBN))
         return fail(ST_DEVICE, "tensor map encoding failed");
+    // the rows' bias parts live with the rows (allocated by add); this only
+    // brings rows added since the last search up to date, on `st`
+    rc = prepare_bias_parts(ix, st, &maps.bias);
+    if (rc != ST_OK) return rc;
     const int grid = n_chunks < ix->num_sms ? n_chunks : ix->num_sms;
-    CU_TRY(launch_screen_bf16x3(kNaKP, ta_h, ta_l, tb_h, tb_l, sp, grid, st), "screen launch");
+    CU_TRY(launch_screen(kNaKP, ScreenKind::kBF16x3, maps, sp, grid, st), "screen launch");
 
     SelectParams sel{};
     sel.m = m;
@@ -177,7 +181,7 @@ extern "C" int mflat_cu_index_search_noalloc(mflat_cu_index_t* ix, const float* 
     sel.dim = ix->dim;
     sel.d_pad = d_pad;
     sel.k_out = k_out;
-    sel.n_chunks = n_chunks;
+    sel.n_chunks = n_chunks * kScreenListsPerChunk;
     sel.metric = ix->metric == kL2 ? kL2 : kIP;
     sel.n = ix->n;
     sel.part_score = part_s;

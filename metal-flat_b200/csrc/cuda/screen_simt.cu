@@ -1,6 +1,6 @@
 // screen_simt.cu -- CUDA-core screen with exactly the inputs and outputs of
 // the tcgen05 kernel (per (query, chunk) top-KP lists).  It is the
-// independent GPU cross-check of screen_tc.cu, selected with
+// independent GPU cross-check of screen.cu (fp32 storage), selected with
 // MFLAT_SCREEN=simt; the fp32 dot product here is computed directly from the
 // stored fp32 rows, in index order.
 #include "kernels.cuh"

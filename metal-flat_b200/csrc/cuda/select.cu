@@ -1,6 +1,6 @@
 // select.cu -- candidate merge, exactness proof and exact re-rank.
 //
-// The screen (screen_tc.cu) leaves, per query and database chunk, the top-KP
+// The screen (screen.cu) leaves, per query and database chunk, the top-KP
 // rows by the fp32 screen score s' (3 x bf16 dot + norm term).  Every screen
 // score is within E of the exact score s (a-priori bound, see error_bound()).
 // If the KP-th best merged screen score is below (k-th best) - 2E, every row
@@ -67,10 +67,11 @@ __device__ Cand block_best(Cand c, Cand* red) {
 // Upper bound E on |screen score - exact score| for one query.
 //   dot:  |dot' - q.x| <= gamma * ||q|| * ||x||  (split + tensor-core
 //         accumulation error; sum |q_i x_i| <= ||q|| ||x|| by Cauchy-Schwarz)
-//   L2 adds the rounding of the fp32 ||x||^2 term and of the score FMA.
+//   L2 adds the rounding of the fp32 ||x||^2 term (u X^2) and of the bias
+//   step's accumulation into score / 2 (u (||q|| X + X^2 / 2), doubled).
 __device__ __forceinline__ double error_bound(int metric, double qn, double xmax, double gamma) {
     const double u = 1.0 / 8388608.0;    // 2^-23
-    if (metric == kL2) return 2.0 * gamma * qn * xmax + u * xmax * xmax + u * qn * xmax + 1e-30;
+    if (metric == kL2) return 2.0 * gamma * qn * xmax + u * xmax * xmax + 2.0 * u * qn * xmax + 1e-30;
     return gamma * qn * xmax + 1e-30;
 }
 

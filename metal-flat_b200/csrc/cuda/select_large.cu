@@ -158,7 +158,7 @@ __device__ __forceinline__ double exact_score_l(int metric, const float* q, cons
 
 __device__ __forceinline__ double bound_e(int metric, double qn, double xmax, double gamma) {
     const double u = 1.0 / 8388608.0;
-    if (metric == kL2) return 2.0 * gamma * qn * xmax + u * xmax * xmax + u * qn * xmax + 1e-30;
+    if (metric == kL2) return 2.0 * gamma * qn * xmax + u * xmax * xmax + 2.0 * u * qn * xmax + 1e-30;
     return gamma * qn * xmax + 1e-30;
 }
 

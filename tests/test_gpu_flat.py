@@ -224,7 +224,7 @@ def test_large_k_two_stage_floor_k1024():
 
 def test_large_k_two_stage_denser_stage_a():
     """5M rows at k = 1024: too few tiles for lists over 1/256 of them, so
-    stage A samples every 64th tile before the 1/16 buffer pass."""
+    stage A samples every 128th tile before the 1/16 buffer pass."""
     rng = np.random.default_rng(zlib.crc32(b"two-stage-stride-64"))
     db = rng.standard_normal((5_000_000, 8), dtype=np.float32)
     q = rng.standard_normal((5, 8), dtype=np.float32)

@@ -70,7 +70,7 @@ def test_large_plan_invariants(probe):
     for n in [1, 1000, 32768, 32769, 60_000, 150_000, 200_003, 1_000_000, 2_000_000,
               3_000_000, 5_000_000, 8_000_000, 17_000_000, 20_000_000, 100_000_000]:
         for k, m in [(22, 30), (100, 10_000), (300, 17), (1024, 16_384), (1024, 5)]:
-            cases.append((n, k, m, 32, 2 * k, 1, SMS, 16 * GB))      # fp32 exact path
+            cases.append((n, k, m, 32, 2 * k, 2, SMS, 16 * GB))      # fp32 exact path
             cases.append((n, k, m, 16, k, 2, SMS, 16 * GB))          # 16-bit buffer path
             cases.append((n, k, m, 16, k, 2, SMS, 1 * GB))
     for c, p in zip(cases, large(probe, cases)):
@@ -126,15 +126,18 @@ def test_large_plan_invariants(probe):
     # the 8M-row and 3M-row 16-bit cases: denser stage-A samples
     ((8_000_000, 1024, 16_384, 16, 1024, 2), ("two", 128)),
     ((3_000_000, 1024, 6, 16, 1024, 2), ("two", 64)),
-    # fp32 k = 1024: 17M rows (1/256), 10M rows (1/128), 5M rows (1/64)
-    ((17_000_000, 1024, 6, 32, 2048, 1), ("two", 256)),
-    ((10_000_000, 1024, 2048, 32, 2048, 1), ("two", 128)),
-    ((5_000_000, 1024, 5, 32, 2048, 1), ("two", 64)),
-    # the exact-path shapes whose tests expect a single-stage pre-pass or no
-    # pre-pass (k = 1024 on 586 tiles: the stride halves until 256 lists fit)
-    ((150_000, 1024, 33, 32, 2048, 1), ("one", 2)),
-    ((150_000, 64, 40, 32, 128, 1), ("one", 16)),
-    ((3000, 300, 17, 32, 600, 1), ("none", 0)),
+    # fp32 k = 1024 (two stage-A lists per chunk): 17M and 10M rows (1/256),
+    # 5M rows (1/128)
+    ((17_000_000, 1024, 6, 32, 2048, 2), ("two", 256)),
+    ((10_000_000, 1024, 2048, 32, 2048, 2), ("two", 256)),
+    ((5_000_000, 1024, 5, 32, 2048, 2), ("two", 128)),
+    # exact-path shapes with a single-stage pre-pass or none (k = 1024 on 586
+    # tiles: the stride halves until the 64 chunks of 2 lists fit), and a
+    # small k that gets both stages
+    ((150_000, 1024, 33, 32, 2048, 2), ("one", 4)),
+    ((150_000, 64, 40, 32, 128, 2), ("two", 64)),
+    ((2_000_000, 100, 2, 32, 200, 2), ("two", 256)),
+    ((3000, 300, 17, 32, 600, 2), ("none", 0)),
     # config 2 (fp16, 1M rows, k = 100): two-stage at 1/256
     ((1_000_000, 100, 10_000, 16, 100, 2), ("two", 256)),
 ])
