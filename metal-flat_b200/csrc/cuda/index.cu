@@ -597,11 +597,18 @@ int run_screen(mflat_cu_index* ix, const float* queries, int m, int kp, int on_d
 namespace {
 
 // Bytes the candidate buffers of one query batch may take: a quarter of the
-// device's free memory, at most 16 GB.
-size_t buffer_budget() {
+// device memory that is free or already held by this index's buffers, within
+// [1 GB, 16 GB].  Fixed at the index's first large-k search, so the plan (and
+// the buffers) of later searches do not follow the device's changing free
+// memory, and no later search queries it.
+size_t buffer_budget(mflat_cu_index* ix) {
+    if (ix->lk_budget) return ix->lk_budget;
     size_t free_b = 0, total_b = 0;
     if (cudaMemGetInfo(&free_b, &total_b) != cudaSuccess) return size_t(4) << 30;
-    return std::max<size_t>(size_t(1) << 30, std::min<size_t>(size_t(16) << 30, free_b / 4));
+    const size_t held = ix->buf_s.bytes + ix->buf_i.bytes;
+    ix->lk_budget = std::max<size_t>(size_t(1) << 30,
+                                     std::min<size_t>(size_t(16) << 30, (free_b + held) / 4));
+    return ix->lk_budget;
 }
 
 // Floor estimate for one query batch (see plan_large): stage A list-mode
@@ -667,7 +674,7 @@ int search_large(mflat_cu_index* ix, const float* queries, int m, int k_out, int
                  float* d_dist, int on_device, cudaStream_t st) {
     constexpr int kKP1 = 32;
     const int lpc = fp32_lists_per_chunk(ix);   // stage-A lists per chunk
-    const LargePlan P = plan_large(ix->n, k_out, m, kKP1, 2 * k_out, lpc, ix->num_sms, buffer_budget());
+    const LargePlan P = plan_large(ix->n, k_out, m, kKP1, 2 * k_out, lpc, ix->num_sms, buffer_budget(ix));
     const int d_pad = ix->d_pad;
     const int n_tiles = static_cast<int>((ix->n + kBN - 1) / kBN);
     const float* qsrc = queries;
@@ -843,7 +850,7 @@ int search_half(mflat_cu_index* ix, const float* queries, int m, int k_out, int3
     if (list_mode) {
         P.batch = m;
     } else {
-        P = plan_large(ix->n, k_out, m, kKP1, k_out, 2, ix->num_sms, buffer_budget());   // two lists (column halves) per chunk
+        P = plan_large(ix->n, k_out, m, kKP1, k_out, 2, ix->num_sms, buffer_budget(ix));   // two lists (column halves) per chunk
     }
     const int bm_pad = (P.batch + kBM - 1) / kBM * kBM;
     CU_TRY(ix->q16.ensure(static_cast<size_t>(bm_pad) * d_pad * 2), "query conversion");

@@ -89,6 +89,7 @@ struct mflat_cu_index {
     mflat_cu::DevBuf stage_in, q_in, q_x, q_h, q_l, qnorm, part_s, part_i, flag_list, out_ids, out_dist;
     mflat_cu::DevBuf thr, thr_stat, fb_s, fb_i;
     mflat_cu::DevBuf buf_cnt, buf_s, buf_i, lk_words;   // large-k candidate buffers
+    size_t lk_budget = 0;                               // their byte budget (first large search)
     mflat_cu::DevBuf q16, qsq;                          // 16-bit queries, ||q||^2
     // Screen bias parts: colbias / alpha as three bf16 parts per row
     // ([cap][8] bf16 = (h, m, l, 0 ...); rows past n: (-inf, 0, 0)), the
