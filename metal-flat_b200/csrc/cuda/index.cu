@@ -111,12 +111,13 @@ bool make_map_u16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t r
 }
 
 // Bias parts of the screens' bias MMA: [rows][8] bf16 (h, m, l, zeros),
-// 8-wide boxes of 256 rows, no swizzle (the MMA's K-major core-matrix layout).
-bool make_map_bias16(CUtensorMap* map, const void* base, uint64_t rows) {
+// 8-wide boxes of box_rows rows (a CTA's share of a tile), no swizzle (the
+// MMA's K-major core-matrix layout).
+bool make_map_bias16(CUtensorMap* map, const void* base, uint64_t rows, uint32_t box_rows) {
     if (!get_encoder()) return false;
     cuuint64_t dims[2] = {8, rows};
     cuuint64_t strides[1] = {16};
-    cuuint32_t box[2] = {8u, static_cast<cuuint32_t>(kBN)};
+    cuuint32_t box[2] = {8u, box_rows};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(base), dims,
                           strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -478,7 +479,17 @@ int check_device_error(mflat_cu_index* ix, cudaStream_t st) {
     return ST_OK;
 }
 
-int prepare_bias_parts(mflat_cu_index* ix, cudaStream_t st, CUtensorMap* map) {
+bool screen_pair_for(const mflat_cu_index* ix, int n_qtiles) {
+    return screen_pair_for(ix->screen_pair && !ix->force_simt, n_qtiles);
+}
+
+int screen_grid(const mflat_cu_index* ix, int n_qtiles, int n_chunks, bool pair) {
+    const int64_t units = static_cast<int64_t>(screen_qunits(n_qtiles, pair)) * n_chunks;
+    const int slots = static_cast<int>(std::min<int64_t>(units, screen_slots(ix->num_sms, pair)));
+    return pair ? 2 * slots : slots;
+}
+
+int prepare_bias_parts(mflat_cu_index* ix, cudaStream_t st, CUtensorMap* map, bool pair) {
     const int64_t rows_pad = (ix->n + kBN - 1) / kBN * kBN;
     if (rows_pad == 0 || !ix->bias16 || rows_pad > ix->cap)
         return fail(ST_INTERNAL, "screen bias parts: no rows");
@@ -490,7 +501,8 @@ int prepare_bias_parts(mflat_cu_index* ix, cudaStream_t st, CUtensorMap* map) {
         CU_TRY(cudaGetLastError(), "bias parts");
         ix->bias16_rows = rows_pad;
     }
-    if (!make_map_bias16(map, ix->bias16, static_cast<uint64_t>(rows_pad)))
+    if (!make_map_bias16(map, ix->bias16, static_cast<uint64_t>(rows_pad),
+                         static_cast<uint32_t>(screen_rows_per_cta(pair))))
         return fail(ST_DEVICE, "tensor map encoding failed");
     return ST_OK;
 }
@@ -507,16 +519,17 @@ cudaError_t launch_fp32_screen(mflat_cu_index* ix, const ScreenParams& sp_in, in
     sp.wait_ns = ix->wait_ns;
     sp.test_stall = ix->test_stall;
     ix->test_stall = 0;
+    const bool pair = screen_pair_for(ix, sp.n_qtiles);
+    const uint32_t rows_b = static_cast<uint32_t>(screen_rows_per_cta(pair));
     ScreenMaps maps;
     if (!make_map_u16(&maps.a, ix->q_h.p, sp.d_pad, sp.m_pad, kBM) ||
         !make_map_u16(&maps.a2, ix->q_l.p, sp.d_pad, sp.m_pad, kBM) ||
-        !make_map_u16(&maps.b, ix->db_h, sp.d_pad, ix->n, kBN) ||
-        !make_map_u16(&maps.b2, ix->db_l, sp.d_pad, ix->n, kBN))
+        !make_map_u16(&maps.b, ix->db_h, sp.d_pad, ix->n, rows_b) ||
+        !make_map_u16(&maps.b2, ix->db_l, sp.d_pad, ix->n, rows_b))
         return cudaErrorInvalidValue;
-    if (prepare_bias_parts(ix, st, &maps.bias) != ST_OK) return cudaErrorInvalidValue;
-    const int64_t units = static_cast<int64_t>(sp.n_qtiles) * sp.n_chunks;
-    const int grid = static_cast<int>(std::min<int64_t>(units, ix->num_sms));
-    return launch_screen(kp, ScreenKind::kBF16x3, maps, sp, grid, st);
+    if (prepare_bias_parts(ix, st, &maps.bias, pair) != ST_OK) return cudaErrorInvalidValue;
+    return launch_screen(kp, ScreenKind::kBF16x3, maps, sp, screen_grid(ix, sp.n_qtiles, sp.n_chunks, pair),
+                         pair, st);
 }
 
 int run_screen(mflat_cu_index* ix, const float* queries, int m, int kp, int on_device,
@@ -527,7 +540,9 @@ int run_screen(mflat_cu_index* ix, const float* queries, int m, int kp, int on_d
     const int n_qtiles = m_pad / kBM;
     int n_chunks = 1, tpc = n_tiles;
     const int lpc = fp32_lists_per_chunk(ix);
-    plan_chunks(n_qtiles, n_tiles, ix->num_sms, max_chunks / lpc, n_chunks, tpc);
+    const bool pair = screen_pair_for(ix, n_qtiles);
+    plan_chunks(screen_qunits(n_qtiles, pair), n_tiles, screen_slots(ix->num_sms, pair), max_chunks / lpc,
+                n_chunks, tpc);
 
     const float* qsrc = queries;
     if (!on_device) {
@@ -638,7 +653,9 @@ int estimate_floor(mflat_cu_index* ix, const LargePlan& P, const ScreenParams& b
     pb.tile_stride = P.stride_b;
     pb.n_tiles = P.sample_b;
     int n_chunks = 1, tpc = P.sample_b;
-    plan_buffer_chunks(pb.n_qtiles, P.sample_b, ix->num_sms, tile_bytes(ix), n_chunks, tpc);
+    const bool pair = screen_pair_for(ix, pb.n_qtiles);
+    plan_buffer_chunks(screen_qunits(pb.n_qtiles, pair), P.sample_b, screen_slots(ix->num_sms, pair),
+                       tile_bytes(ix), n_chunks, tpc);
     pb.n_chunks = n_chunks;
     pb.tiles_per_chunk = tpc;
     // Stage B runs above the stage-A guess (about want * stride_b / stride_a
@@ -674,7 +691,8 @@ int search_large(mflat_cu_index* ix, const float* queries, int m, int k_out, int
                  float* d_dist, int on_device, cudaStream_t st) {
     constexpr int kKP1 = 32;
     const int lpc = fp32_lists_per_chunk(ix);   // stage-A lists per chunk
-    const LargePlan P = plan_large(ix->n, k_out, m, kKP1, 2 * k_out, lpc, ix->num_sms, buffer_budget(ix));
+    const LargePlan P = plan_large(ix->n, k_out, m, kKP1, 2 * k_out, lpc, ix->num_sms, buffer_budget(ix),
+                                   ix->screen_pair && !ix->force_simt);
     const int d_pad = ix->d_pad;
     const int n_tiles = static_cast<int>((ix->n + kBN - 1) / kBN);
     const float* qsrc = queries;
@@ -753,7 +771,9 @@ int search_large(mflat_cu_index* ix, const float* queries, int m, int k_out, int
         sp.tile_stride = 1;
         sp.n_tiles = n_tiles;
         int n_chunks = 1, tpc = n_tiles;
-        plan_buffer_chunks(sp.n_qtiles, n_tiles, ix->num_sms, tile_bytes(ix), n_chunks, tpc);
+        const bool pair = screen_pair_for(ix, sp.n_qtiles);
+        plan_buffer_chunks(screen_qunits(sp.n_qtiles, pair), n_tiles, screen_slots(ix->num_sms, pair),
+                           tile_bytes(ix), n_chunks, tpc);
         sp.n_chunks = n_chunks;
         sp.tiles_per_chunk = tpc;
 
@@ -850,7 +870,8 @@ int search_half(mflat_cu_index* ix, const float* queries, int m, int k_out, int3
     if (list_mode) {
         P.batch = m;
     } else {
-        P = plan_large(ix->n, k_out, m, kKP1, k_out, 2, ix->num_sms, buffer_budget(ix));   // two lists (column halves) per chunk
+        // two lists (column halves) per chunk
+        P = plan_large(ix->n, k_out, m, kKP1, k_out, 2, ix->num_sms, buffer_budget(ix), ix->screen_pair);
     }
     const int bm_pad = (P.batch + kBM - 1) / kBM * kBM;
     CU_TRY(ix->q16.ensure(static_cast<size_t>(bm_pad) * d_pad * 2), "query conversion");
@@ -872,11 +893,14 @@ int search_half(mflat_cu_index* ix, const float* queries, int m, int k_out, int3
     const size_t parts = static_cast<size_t>(2 * std::max(max_lists, 1)) * bm_pad * lk;
     CU_TRY(ix->part_s.ensure(parts * sizeof(float)), "candidate lists");
     CU_TRY(ix->part_i.ensure(parts * sizeof(int32_t)), "candidate lists");
-    ScreenMaps maps;
-    if (!make_map_u16(&maps.b, ix->db16, d_pad, ix->n, kBN)) return fail(ST_DEVICE, "tensor map encoding failed");
-    maps.b2 = maps.b;
-    {
-        const int rc = prepare_bias_parts(ix, st, &maps.bias);
+    // tensor maps of the rows for single-CTA [0] and CTA-pair [1] screens
+    ScreenMaps maps[2];
+    for (int pr = 0; pr < 2; ++pr) {
+        if (!make_map_u16(&maps[pr].b, ix->db16, d_pad, ix->n,
+                          static_cast<uint32_t>(screen_rows_per_cta(pr != 0))))
+            return fail(ST_DEVICE, "tensor map encoding failed");
+        maps[pr].b2 = maps[pr].b;
+        const int rc = prepare_bias_parts(ix, st, &maps[pr].bias, pr != 0);
         if (rc != ST_OK) return rc;
     }
     const ScreenKind kind = bf16 ? ScreenKind::kBF16 : ScreenKind::kF16;
@@ -890,9 +914,12 @@ int search_half(mflat_cu_index* ix, const float* queries, int m, int k_out, int3
             ix->q16.as<uint16_t>(), ix->qsq.as<float>());
         CU_TRY(cudaGetLastError(), "query prep launch");
         CU_TRY(cudaMemsetAsync(ix->thr.p, 0, static_cast<size_t>(mb_pad) * sizeof(uint32_t), st), "floors");
-        if (!make_map_u16(&maps.a, ix->q16.p, d_pad, mb_pad, kBM))
-            return fail(ST_DEVICE, "tensor map encoding failed");
-        maps.a2 = maps.a;
+        for (int pr = 0; pr < 2; ++pr) {
+            if (!make_map_u16(&maps[pr].a, ix->q16.p, d_pad, mb_pad, kBM))
+                return fail(ST_DEVICE, "tensor map encoding failed");
+            maps[pr].a2 = maps[pr].a;
+        }
+        const bool pair = screen_pair_for(ix->screen_pair, mb_pad / kBM);   // no CUDA-core variant here
         ScreenParams sp{};
         sp.m = mb;
         sp.m_pad = mb_pad;
@@ -907,16 +934,16 @@ int search_half(mflat_cu_index* ix, const float* queries, int m, int k_out, int3
         sp.part_id = ix->part_i.as<int32_t>();
         sp.wait_ns = ix->wait_ns;
         auto launch = [&](const ScreenParams& q, int kpp) {
-            const int64_t units = static_cast<int64_t>(q.n_qtiles) * q.n_chunks;
-            const int grid = static_cast<int>(std::min<int64_t>(units, ix->num_sms));
-            return launch_screen(kpp, kind, maps, q, grid, st);
+            return launch_screen(kpp, kind, maps[pair ? 1 : 0], q, screen_grid(ix, q.n_qtiles, q.n_chunks, pair),
+                                 pair, st);
         };
         if (list_mode) {
             sp.use_floor = 1;
             sp.tile_stride = 1;
             sp.n_tiles = n_tiles;
             int n_chunks = 1, tpc = n_tiles;
-            plan_chunks(sp.n_qtiles, n_tiles, ix->num_sms, kMaxChunks / 2, n_chunks, tpc);
+            plan_chunks(screen_qunits(sp.n_qtiles, pair), n_tiles, screen_slots(ix->num_sms, pair), kMaxChunks / 2,
+                        n_chunks, tpc);
             sp.n_chunks = n_chunks;
             sp.tiles_per_chunk = tpc;
             if (ix->timing) cudaEventRecord(ix->ev[1], st);
@@ -954,7 +981,8 @@ int search_half(mflat_cu_index* ix, const float* queries, int m, int k_out, int3
         sp.tile_stride = 1;
         sp.n_tiles = n_tiles;
         int n_chunks = 1, tpc = n_tiles;
-        plan_buffer_chunks(sp.n_qtiles, n_tiles, ix->num_sms, tile_bytes(ix), n_chunks, tpc);
+        plan_buffer_chunks(screen_qunits(sp.n_qtiles, pair), n_tiles, screen_slots(ix->num_sms, pair),
+                           tile_bytes(ix), n_chunks, tpc);
         sp.n_chunks = n_chunks;
         sp.tiles_per_chunk = tpc;
         LargeSelectParams ls{};
@@ -1209,6 +1237,7 @@ int mflat_cu_index_create(int device, int dim, int metric, int storage, mflat_cu
     cudaDeviceGetAttribute(&ix->num_sms, cudaDevAttrMultiProcessorCount, device);
     const char* fs = std::getenv("MFLAT_SCREEN");
     ix->force_simt = fs && std::strcmp(fs, "simt") == 0;
+    if (const char* pr = std::getenv("MFLAT_SCREEN_PAIR")) ix->screen_pair = std::strcmp(pr, "0") != 0;
     if (const char* wl = std::getenv("MFLAT_WAIT_LIMIT_MS")) {
         const double ms = std::atof(wl);
         if (ms > 0.0) ix->wait_ns = static_cast<uint64_t>(ms * 1e6);

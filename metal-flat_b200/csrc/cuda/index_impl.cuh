@@ -116,6 +116,10 @@ struct mflat_cu_index {
     mutable int sum_n = 0;
     mflat_cu_timing_t last{};
     bool force_simt = false;
+    // Tensor-core screens of batches with two or more query tiles run as CTA
+    // pairs (cta_group::2); MFLAT_SCREEN_PAIR=0 at creation keeps every screen
+    // on single CTAs.
+    bool screen_pair = true;
     // Limit of the screens' bounded waits in ns (MFLAT_WAIT_LIMIT_MS; 0 = 2 s).
     uint64_t wait_ns = 0;
     // Test hook (MFLAT_TEST_STALL_SCREEN set at creation): the next fp32
@@ -159,8 +163,12 @@ cudaError_t launch_prep_queries(const float* src, int m, int m_pad, int dim, int
 bool encode_map_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows,
                      uint32_t box_rows);
 // Bias parts of rows [0, rows_pad(n)) current (a kernel launch on `st` when
-// rows were added; no allocation), and their tensor map.
-int prepare_bias_parts(mflat_cu_index* ix, cudaStream_t st, CUtensorMap* map);
+// rows were added; no allocation), and their tensor map (boxes for a single-CTA
+// or a CTA-pair screen).
+int prepare_bias_parts(mflat_cu_index* ix, cudaStream_t st, CUtensorMap* map, bool pair = false);
+// Whether a screen over n_qtiles query tiles runs as CTA pairs, and its grid.
+bool screen_pair_for(const mflat_cu_index* ix, int n_qtiles);
+int screen_grid(const mflat_cu_index* ix, int n_qtiles, int n_chunks, bool pair);
 // Screen lists per chunk of the fp32-storage screen in use (tensor core: 2,
 // MFLAT_SCREEN=simt cross-check: 1).
 int fp32_lists_per_chunk(const mflat_cu_index* ix);

@@ -163,17 +163,20 @@ __device__ __forceinline__ bool cand_better(float sa, int ia, float sb, int ib) 
 // The tensor-core screen (screen.cu).  kF16 / kBF16: 16-bit storage, one
 // plane (maps a, b); kBF16x3: fp32 storage, bf16 split planes (a / a2: the
 // queries' h / l planes, b / b2: the rows').  `bias`: the rows' bias parts,
-// [rows][8] bf16 = (h, m, l, 0, ...) of colbias / alpha, 256-row boxes, no
-// swizzle (split_bias in index.cu).  kp 0 = buffer mode; list mode (kp 4 .. 32)
-// writes two lists per (query, chunk), list index = chunk * 2 + half.
+// [rows][8] bf16 = (h, m, l, 0, ...) of colbias / alpha, no swizzle (split_bias
+// in index.cu).  The b, b2 and bias maps' boxes are screen_rows_per_cta(pair)
+// rows high.  kp 0 = buffer mode; list mode (kp 4 .. 32) writes two lists per
+// (query, chunk), list index = chunk * 2 + half.  pair: CTA pairs (grid even,
+// grid / 2 pairs; each pair works on two query tiles per unit).
 enum class ScreenKind : int { kF16 = 0, kBF16 = 1, kBF16x3 = 2 };
 struct ScreenMaps {
     CUtensorMap a, a2, b, b2, bias;
 };
 constexpr int kScreenListsPerChunk = 2;
 cudaError_t launch_screen(int kp, ScreenKind kind, const ScreenMaps& maps, const ScreenParams& p,
-                          int grid, cudaStream_t stream);
-int screen_smem_bytes(int d_pad, bool x3);
+                          int grid, bool pair, cudaStream_t stream);
+int screen_smem_bytes(int d_pad, bool x3, bool pair);
+int screen_rows_per_cta(bool pair);
 cudaError_t launch_screen_simt(int kp, const ScreenParams& p, cudaStream_t stream);
 cudaError_t launch_select_exact(int kp, const SelectParams& p, cudaStream_t stream);
 cudaError_t launch_fallback_exact(const SelectParams& p, int grid, cudaStream_t stream);

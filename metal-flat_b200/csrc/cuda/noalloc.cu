@@ -173,7 +173,7 @@ extern "C" int mflat_cu_index_search_noalloc(mflat_cu_index_t* ix, const float* 
     rc = prepare_bias_parts(ix, st, &maps.bias);
     if (rc != ST_OK) return rc;
     const int grid = n_chunks < ix->num_sms ? n_chunks : ix->num_sms;
-    CU_TRY(launch_screen(kNaKP, ScreenKind::kBF16x3, maps, sp, grid, st), "screen launch");
+    CU_TRY(launch_screen(kNaKP, ScreenKind::kBF16x3, maps, sp, grid, false, st), "screen launch");
 
     SelectParams sel{};
     sel.m = m;

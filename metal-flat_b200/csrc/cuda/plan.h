@@ -17,6 +17,13 @@ constexpr int kMaxChunks = 256;   // candidate lists per query (select kernel fa
 constexpr int kFloorMaxEntries = 4096;   // list entries per query the floor select takes
 constexpr int64_t kAllRowsBuffered = 32768;   // large k below this many rows: no pre-pass
 
+// Screens run as single CTAs or as CTA pairs (two SMs, two query tiles per
+// work unit).  Query units of a batch and the units that run at once.
+inline int screen_qunits(int n_qtiles, bool pair) { return pair ? (n_qtiles + 1) / 2 : n_qtiles; }
+inline int screen_slots(int num_sms, bool pair) { return pair ? std::max(1, num_sms / 2) : num_sms; }
+// CTA pairs when allowed and the batch has at least two query tiles.
+inline bool screen_pair_for(bool allowed, int n_qtiles) { return allowed && n_qtiles >= 2; }
+
 // Database chunks per query tile: whole work units on every SM.
 inline void plan_chunks(int n_qtiles, int n_tiles, int num_sms, int max_chunks, int& n_chunks,
                         int& tiles_per_chunk, int min_chunks = 1) {
@@ -68,9 +75,10 @@ struct LargePlan {
 // of m queries.  want: rank whose sampled score becomes the floor (2k exact
 // path, k recall); kp1: list length of the stage-A pass; lists_per_chunk: lists
 // one list-mode chunk produces (f16 kernel: 2); budget_bytes: what the
-// candidate buffers of one query batch may take.
+// candidate buffers of one query batch may take; pair: CTA-pair screens are
+// allowed (stage A's chunks are then planned in pair units).
 inline LargePlan plan_large(int64_t n, int k, int m, int kp1, int want, int lists_per_chunk,
-                            int num_sms, size_t budget_bytes) {
+                            int num_sms, size_t budget_bytes, bool pair = false) {
     LargePlan P;
     const int n_tiles = static_cast<int>((n + kBN - 1) / kBN);
     const int64_t n_round = (n + 255) / 256 * 256;
@@ -131,7 +139,9 @@ inline LargePlan plan_large(int64_t n, int k, int m, int kp1, int want, int list
         // tiles share the pass.
         const int n_qt = (P.batch + kBM - 1) / kBM;
         const int max_a = std::max(P.lists, kFloorMaxEntries / (kp1 * lists_per_chunk));
-        plan_chunks(n_qt, P.sample_a, num_sms, max_a, P.chunks_a, P.tpc_a);
+        const bool pr = screen_pair_for(pair, n_qt);
+        plan_chunks(screen_qunits(n_qt, pr), P.sample_a, screen_slots(num_sms, pr), max_a, P.chunks_a,
+                    P.tpc_a);
         if (P.chunks_a < P.lists) {
             // whole tiles per list, as few as keep >= `lists` chunks; coarser
             // only where that many lists would not fit the floor select

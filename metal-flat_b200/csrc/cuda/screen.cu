@@ -11,7 +11,7 @@
 //     A_h.B_h + A_l.B_h + A_h.B_l (3 x bf16).  Each product of bf16 values is
 //     exact in fp32; what the split drops is ~3 * 2^-16 of |q_i x_i|, inside
 //     the error bound the exact select works with (screen_gamma).
-// M = 128 queries x N = 256 rows per tile, K = 16 per MMA, fp32 accumulators
+// Per CTA a tile is 128 queries x 256 rows, K = 16 per MMA, fp32 accumulators
 // in TMEM (two 256-column buffers, so the epilogue of one tile overlaps the
 // MMAs of the next).  The screen score bias (-||x||^2 for L2, 0 for inner
 // product, -inf for rows past n) enters the accumulator through one more
@@ -19,20 +19,30 @@
 // (split_bias in index.cu; the parts are exact and sum exactly in any order),
 // so the accumulator holds score / alpha and the epilogue only compares.
 //
-// Work unit = (query tile, database chunk of whole tiles).  Persistent CTAs
-// (one per SM) walk units chunk-major so that the CTAs running at the same
-// time read the same database rows (L2 reuse).
+// CTA pairs (kPair): the two CTAs of a cluster issue their MMAs as one
+// tcgen05 cta_group::2 instruction (M = 256: CTA r holds query tile 2j + r
+// and rows [r * 128, r * 128 + 128) of each 256-row database tile; each CTA's
+// TMEM receives its 128 queries x all 256 columns).  Each SM then loads and
+// holds half of every database tile, which halves the per-SM L2 -> shared
+// memory traffic and doubles the tiles the ring holds in flight.  The
+// leader CTA (rank 0) owns the full / a_full / bias_full / acc_empty
+// barriers and the one MMA-issuing thread; both CTAs' TMA loads complete on
+// the leader's barriers (cta_group::2 loads, no multicast), MMA completion is
+// committed to the barriers of both CTAs, and the peer's epilogue warps
+// release accumulators on the leader's barrier.
 //
-// Warp roles: the epilogue warpgroups first (two in list mode, four in buffer
-// mode; warpgroup g owns columns [g * kCols, (g + 1) * kCols) of each tile and,
-// in list mode, its own top-KP per query row -- two lists per (query, chunk)),
-// then the TMA producer warp, then the MMA warp (TMEM allocator, one issuing
-// thread).  The query tile (all k-blocks, both planes for kX3) stays resident
-// in shared memory for a unit when it fits in 64 KB; above, each ring stage
-// carries the k-block's query plane with the database plane (kX3: a k-block's
-// h and l stages are consumed as a pair).  Every mbarrier wait is bounded; a
-// wait that runs out sets the CTA's abort flag, the warps drain what they
-// issued, TMEM is freed and the error word records kErrTimeout.
+// Work unit = (query tile (pair), database chunk of whole tiles).  Persistent
+// CTAs (pairs) walk units chunk-major so that the CTAs running at the same
+// time read the same database rows (L2 reuse).  Warp roles: the epilogue
+// warpgroups first (two in list mode, each owning 128 of a tile's 256 columns
+// and its own top-KP per query row -- two lists per (query, chunk); four in
+// buffer mode, 64 columns each), then the TMA producer warp, then the MMA warp
+// (TMEM allocator, one issuing thread).  The query tile stays resident in
+// shared memory for a unit when it fits in 64 KB; above, each ring stage
+// carries the k-block's query plane with the database plane (kX3: a
+// k-block's h and l stages are consumed as a pair).  Every mbarrier wait is
+// bounded; a wait that runs out sets the CTA's abort flag, the warps drain
+// what they issued, TMEM is freed and the error word records kErrTimeout.
 #include "epilogue.cuh"
 #include "kernels.cuh"
 #include "ptx.cuh"
@@ -43,70 +53,83 @@ namespace {
 __host__ __device__ constexpr int epi_wg(bool buf) { return buf ? 4 : 2; }
 __host__ __device__ constexpr int screen_threads(bool buf) { return epi_wg(buf) * 128 + 64; }
 constexpr int kATile = kBM * 128;                 // 16 KB: 128 rows x 128 B (one plane, one k-block)
-constexpr int kBTile = kBN * 128;                 // 32 KB: 256 rows x 128 B
-constexpr int kMaxStages = 6;
 constexpr int kAResidentMax = 64 * 1024;          // resident query tile budget
 constexpr int kSmemMax = 232448;                  // opt-in shared memory per CTA
-constexpr int kBarBytes = 256;                    // mbarriers, TMEM slot, abort flag
-// Folded bias: slot s holds the bias parts of one tile, [256 rows][8 bf16]
-// = (h, m, l, 0, ...); three slots, loaded one tile ahead (slot (t + 1) % 3
-// last served tile t - 2, whose MMAs have completed once the MMA warp has
-// seen tile t - 2's accumulator released).  The constant block holds 128
-// rows of (1, 1, 1, 0, ...) -- the A operand's K columns 0..7 -- then 128
-// zero rows -- its K columns 8..15.  B's K columns 8..15 read the whole
+constexpr int kBarBytes = 512;                    // mbarriers, TMEM slot, abort flag
+constexpr int kMaxStagesAll = 12;                 // barrier slots of the ring
+// Folded bias: slot s holds the bias parts of the CTA's rows of one tile,
+// [rows][8] bf16 = (h, m, l, 0, ...); a ring of three slots filled by the
+// producer (bias_full / bias_empty, like the operand ring).  The constant
+// block holds 128 rows of (1, 1, 1, 0, ...) -- the A operand's K columns 0..7
+// -- then 128 zero rows -- its K columns 8..15.  B's K columns 8..15 read the
 // constant block (finite values, multiplied by A's zeros).
 constexpr int kFoldSlots = 3;
-constexpr int kFoldSlotBytes = kBN * 16;          // 4 KB
 constexpr int kConstBytes = 2 * kBM * 16;         // 4 KB: ones rows, then zero rows
-constexpr int kFoldBytes = kFoldSlots * kFoldSlotBytes + kConstBytes;
 constexpr uint32_t kOneBf16x2 = 0x3F803F80u;      // two bf16 1.0
+
+// Per-CTA geometry of one mode.
+struct Geo {
+    int rows_b;          // database rows of a tile this CTA holds (256, or 128 in a pair)
+    int b_tile;          // bytes of one B plane k-block
+    int slot;            // bytes of one bias slot
+    int fold;            // slots + constant block
+    int max_stages;
+};
+__host__ __device__ constexpr Geo geo(bool pair) {
+    return pair ? Geo{kBN / 2, (kBN / 2) * 128, (kBN / 2) * 16, kFoldSlots * (kBN / 2) * 16 + kConstBytes, 12}
+                : Geo{kBN, kBN * 128, kBN * 16, kFoldSlots * kBN * 16 + kConstBytes, 6};
+}
 
 __host__ __device__ inline int a_bytes(int kb, int planes) { return kb * planes * kATile; }
 __host__ __device__ inline bool a_streamed(int kb, int planes) { return a_bytes(kb, planes) > kAResidentMax; }
-__host__ __device__ inline int stage_bytes(bool streamed) { return streamed ? kATile + kBTile : kBTile; }
-__host__ __device__ inline int n_stages(int kb, int planes) {
+__host__ __device__ inline int stage_bytes(bool streamed, bool pair) {
+    return (streamed ? kATile : 0) + geo(pair).b_tile;
+}
+__host__ __device__ inline int n_stages(int kb, int planes, bool pair) {
     const bool st = a_streamed(kb, planes);
     const int a = st ? 0 : a_bytes(kb, planes);
-    int s = (kSmemMax - kBarBytes - kFoldBytes - a) / stage_bytes(st);
-    if (s > kMaxStages) s = kMaxStages;
+    int s = (kSmemMax - kBarBytes - geo(pair).fold - a) / stage_bytes(st, pair);
+    if (s > geo(pair).max_stages) s = geo(pair).max_stages;
     if (st && planes == 2) s &= ~1;               // a k-block's h and l stages form a pair
     return s;
 }
-__host__ __device__ inline int smem_bytes(int kb, int planes) {
+__host__ __device__ inline int smem_bytes(int kb, int planes, bool pair) {
     const bool st = a_streamed(kb, planes);
-    return (st ? 0 : a_bytes(kb, planes)) + n_stages(kb, planes) * stage_bytes(st) + kBarBytes + kFoldBytes;
+    return (st ? 0 : a_bytes(kb, planes)) + n_stages(kb, planes, pair) * stage_bytes(st, pair) + kBarBytes +
+           geo(pair).fold;
 }
 
 struct Smem {
     uint8_t* a;          // resident A: [planes][kb][16 KB]
-    uint8_t* ring;       // [stages][stage bytes]: ([A plane 16 KB]) [B plane 32 KB]
-    uint64_t *full, *empty, *a_full, *a_empty, *acc_full, *acc_empty, *drain, *bias_full;
+    uint8_t* ring;       // [stages][stage bytes]: ([A plane 16 KB]) [B plane]
+    uint64_t *full, *empty, *a_full, *a_empty, *acc_full, *acc_empty, *drain, *bias_full, *bias_empty;
     uint32_t* tmem_slot;
     int* abort_flag;
-    uint8_t* fold;       // [kFoldSlots][4 KB] bias parts, then the 4 KB constant block
+    uint8_t* fold;       // [kFoldSlots][slot] bias parts, then the 4 KB constant block
 };
 
-__device__ inline Smem carve(uint8_t* base, int kb, int planes, int stages) {
+__device__ inline Smem carve(uint8_t* base, int kb, int planes, int stages, bool pair) {
     Smem S;
     const bool st = a_streamed(kb, planes);
     S.a = base;
     S.ring = base + (st ? 0 : a_bytes(kb, planes));
-    uint64_t* bars = reinterpret_cast<uint64_t*>(S.ring + stages * stage_bytes(st));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(S.ring + stages * stage_bytes(st, pair));
     S.full = bars;
-    S.empty = bars + kMaxStages;
-    S.a_full = bars + 2 * kMaxStages;
+    S.empty = bars + kMaxStagesAll;
+    S.a_full = bars + 2 * kMaxStagesAll;
     S.a_empty = S.a_full + 1;
     S.acc_full = S.a_full + 2;
     S.acc_empty = S.a_full + 4;
     S.drain = S.a_full + 6;
     S.bias_full = S.a_full + 7;
-    S.tmem_slot = reinterpret_cast<uint32_t*>(S.bias_full + kFoldSlots);
+    S.bias_empty = S.bias_full + kFoldSlots;
+    S.tmem_slot = reinterpret_cast<uint32_t*>(S.bias_empty + kFoldSlots);
     S.abort_flag = reinterpret_cast<int*>(S.tmem_slot + 1);
     S.fold = reinterpret_cast<uint8_t*>(bars) + kBarBytes;
     return S;
 }
 
-template <int KP, bool kBuf, bool kBF16, bool kX3>
+template <int KP, bool kBuf, bool kBF16, bool kX3, bool kPair>
 __global__ void __launch_bounds__(screen_threads(kBuf), 1)
 screen_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_a2,
               const __grid_constant__ CUtensorMap tm_b, const __grid_constant__ CUtensorMap tm_b2,
@@ -115,17 +138,23 @@ screen_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ 
     // alignment is checked, not assumed.
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     constexpr int kPlanes = kX3 ? 2 : 1;
+    constexpr Geo G = geo(kPair);
+    constexpr uint16_t kBoth = 0x3;              // CTA mask of a pair
     const int kb_count = p.d_pad / kBK;
+    // identical in both CTAs of a pair, so both leave together
     if (kb_count < 1 || kb_count * kBK != p.d_pad || (smem_u32(smem_raw) & 1023u) != 0u) {
         if (threadIdx.x == 0) atomicExch(p.err, kErrConfig);
         return;
     }
+    const uint32_t crank = kPair ? cluster_rank() : 0u;
+    const bool leader = crank == 0;
     const bool stream_a = a_streamed(kb_count, kPlanes);
-    const int sbytes = stage_bytes(stream_a);
-    const int stages = n_stages(kb_count, kPlanes);
-    Smem S = carve(smem_raw, kb_count, kPlanes, stages);
-    constexpr uint32_t kIdesc = make_idesc(kBF16 ? 1u : 0u, kBM, kBN);
-    constexpr uint32_t kIdescBias = make_idesc(1u, kBM, kBN);   // the bias step is bf16
+    const int sbytes = stage_bytes(stream_a, kPair);
+    const int stages = n_stages(kb_count, kPlanes, kPair);
+    Smem S = carve(smem_raw, kb_count, kPlanes, stages, kPair);
+    constexpr uint32_t kM = kPair ? 2 * kBM : kBM;
+    constexpr uint32_t kIdesc = make_idesc(kBF16 ? 1u : 0u, kM, kBN);
+    constexpr uint32_t kIdescBias = make_idesc(1u, kM, kBN);   // the bias step is bf16
 
     constexpr int kEpiWG = epi_wg(kBuf);
     constexpr int kProducerWarp = kEpiWG * 4;
@@ -134,7 +163,7 @@ screen_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kMaxStages; ++s) {
+        for (int s = 0; s < kMaxStagesAll; ++s) {
             mbar_init(&S.full[s], 1);
             mbar_init(&S.empty[s], 1);
         }
@@ -142,25 +171,34 @@ screen_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ 
         mbar_init(S.a_empty, 1);
         for (int b = 0; b < 2; ++b) {
             mbar_init(&S.acc_full[b], 1);
-            mbar_init(&S.acc_empty[b], kEpiWG * 4);   // one arrival per epilogue warp
+            // one arrival per epilogue warp (of both CTAs of a pair)
+            mbar_init(&S.acc_empty[b], kEpiWG * 4 * (kPair ? 2 : 1));
         }
         mbar_init(S.drain, 1);
-        for (int s = 0; s < kFoldSlots; ++s) mbar_init(&S.bias_full[s], 1);
+        for (int s = 0; s < kFoldSlots; ++s) {
+            mbar_init(&S.bias_full[s], 1);
+            mbar_init(&S.bias_empty[s], 1);
+        }
         *S.abort_flag = 0;
         fence_mbar_init();
     }
     {
         // constant operand rows of the bias step, written once and made
         // visible to the tensor core's (async-proxy) reads
-        uint4* cst = reinterpret_cast<uint4*>(S.fold + kFoldSlots * kFoldSlotBytes);
+        uint4* cst = reinterpret_cast<uint4*>(S.fold + kFoldSlots * G.slot);
         for (int i = threadIdx.x; i < kConstBytes / 16; i += blockDim.x)
             cst[i] = i < kBM ? make_uint4(kOneBf16x2, kOneBf16x2 & 0xFFFFu, 0u, 0u)
                              : make_uint4(0u, 0u, 0u, 0u);
         fence_proxy_async_shared();
     }
     if (warp == kMmaWarp) {
-        tmem_alloc(S.tmem_slot, 512);
-        tmem_relinquish();
+        if constexpr (kPair) {
+            tmem_alloc_pair(S.tmem_slot, 512);
+            tmem_relinquish_pair();
+        } else {
+            tmem_alloc(S.tmem_slot, 512);
+            tmem_relinquish();
+        }
     }
     if (warp == kProducerWarp && lane == 0) {
         tma_prefetch_desc(&tm_a);
@@ -172,88 +210,143 @@ screen_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ 
         tma_prefetch_desc(&tm_bias);
     }
     tc_fence_before();
-    __syncthreads();
+    if constexpr (kPair) cluster_sync();         // barriers of both CTAs initialised
+    else __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *S.tmem_slot;
     volatile int* abort_flag = S.abort_flag;
-    const int n_units = p.n_qtiles * p.n_chunks;
+    // query units: tiles, or pairs of tiles (the peer's tile may lie past m_pad:
+    // its TMA rows then read as zero and none of its rows is live)
+    const int n_qunits = kPair ? (p.n_qtiles + 1) / 2 : p.n_qtiles;
+    const int n_units = n_qunits * p.n_chunks;
+    const int unit0 = kPair ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+    const int unit_step = kPair ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
 
     if (warp == kProducerWarp) {
         if (lane == 0) {
             int stage = 0;
             uint32_t sphase = 0, a_phase = 0;
             uint32_t issued_mask = 0, issued_phase = 0;   // per stage, for the drain
-            bool a_issued = false;
+            uint32_t bias_mask = 0, bias_phase = 0;       // per bias slot, for the drain
+            bool a_issued = false, any_issued = false;
             uint32_t a_issue_phase = 0;
+            uint32_t tcount = 0;
             bool ok = true;
-            for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
-                const int qt = u % p.n_qtiles;
-                const int ch = u / p.n_qtiles;
+            // barrier the loads complete on: the leader's (pair) or this CTA's
+            auto bar_of = [&](uint64_t* bar) -> uint32_t {
+                if constexpr (kPair) return cluster_addr(bar, 0);
+                else return smem_u32(bar);
+            };
+            auto load = [&](const CUtensorMap* map, uint64_t* bar, void* dst, int x, int y) {
+                if constexpr (kPair) tma_load_2d_pair(map, bar_of(bar), dst, x, y);
+                else tma_load_2d(map, bar, dst, x, y);
+            };
+            constexpr uint32_t kShare = kPair ? 2u : 1u;   // the leader expects both CTAs' bytes
+            for (int u = unit0; u < n_units && ok; u += unit_step) {
+                const int qt = (u % n_qunits) * (kPair ? 2 : 1) + static_cast<int>(crank);
+                const int ch = u / n_qunits;
                 const int t0 = ch * p.tiles_per_chunk;
                 const int t1 = min(t0 + p.tiles_per_chunk, p.n_tiles);
                 if (!stream_a) {
                     if (!mbar_wait(S.a_empty, a_phase ^ 1u, abort_flag, p.wait_ns)) { ok = false; break; }
-                    mbar_arrive_expect_tx(S.a_full, static_cast<uint32_t>(a_bytes(kb_count, kPlanes)));
+                    if (leader)
+                        mbar_arrive_expect_tx(S.a_full, kShare * static_cast<uint32_t>(a_bytes(kb_count, kPlanes)));
                     for (int pl = 0; pl < kPlanes; ++pl)
                         for (int kb = 0; kb < kb_count; ++kb)
-                            tma_load_2d(pl ? &tm_a2 : &tm_a, S.a_full, S.a + (pl * kb_count + kb) * kATile,
-                                        kb * kBK, qt * kBM);
-                    a_issued = true;
+                            load(pl ? &tm_a2 : &tm_a, S.a_full, S.a + (pl * kb_count + kb) * kATile, kb * kBK,
+                                 qt * kBM);
+                    a_issued = any_issued = true;
                     a_issue_phase = a_phase;
                     a_phase ^= 1u;
                 }
-                for (int t = t0; t < t1 && ok; ++t) {
+                for (int t = t0; t < t1 && ok; ++t, ++tcount) {
+                    const int row0 = t * p.tile_stride * kBN + static_cast<int>(crank) * G.rows_b;
+                    {
+                        // bias parts of this tile into slot tcount % 3
+                        const uint32_t sl = tcount % kFoldSlots;
+                        const uint32_t use = tcount / kFoldSlots;
+                        if (!mbar_wait(&S.bias_empty[sl], (use & 1u) ^ 1u, abort_flag, p.wait_ns)) { ok = false; break; }
+                        if (leader) mbar_arrive_expect_tx(&S.bias_full[sl], kShare * static_cast<uint32_t>(G.slot));
+                        load(&tm_bias, &S.bias_full[sl], S.fold + sl * G.slot, 0, row0);
+                        bias_mask |= 1u << sl;
+                        bias_phase = (bias_phase & ~(1u << sl)) | ((use & 1u) << sl);
+                        any_issued = true;
+                    }
                     for (int kb = 0; kb < kb_count && ok; ++kb) {
                         for (int pl = 0; pl < kPlanes; ++pl) {
                             if (!mbar_wait(&S.empty[stage], sphase ^ 1u, abort_flag, p.wait_ns)) { ok = false; break; }
                             uint8_t* dst = S.ring + stage * sbytes;
-                            mbar_arrive_expect_tx(&S.full[stage], static_cast<uint32_t>(sbytes));
+                            if (leader) mbar_arrive_expect_tx(&S.full[stage], kShare * static_cast<uint32_t>(sbytes));
                             if (stream_a) {
-                                tma_load_2d(pl ? &tm_a2 : &tm_a, &S.full[stage], dst, kb * kBK, qt * kBM);
+                                load(pl ? &tm_a2 : &tm_a, &S.full[stage], dst, kb * kBK, qt * kBM);
                                 dst += kATile;
                             }
-                            tma_load_2d(pl ? &tm_b2 : &tm_b, &S.full[stage], dst, kb * kBK,
-                                        t * p.tile_stride * kBN);
+                            load(pl ? &tm_b2 : &tm_b, &S.full[stage], dst, kb * kBK, row0);
                             issued_mask |= 1u << stage;
                             issued_phase = (issued_phase & ~(1u << stage)) | (sphase << stage);
+                            any_issued = true;
                             if (++stage == stages) { stage = 0; sphase ^= 1u; }
                         }
                     }
                 }
             }
+            if (ok && !*abort_flag) {
+                // Tail: wait until the MMAs have released every stage, bias slot
+                // and query tile this warp filled, so that no commit (multicast
+                // in a pair) is still on its way to this CTA's barriers at exit.
+                for (int i = 0; i < stages && ok; ++i) {
+                    ok = mbar_wait(&S.empty[stage], sphase ^ 1u, abort_flag, p.wait_ns);
+                    if (++stage == stages) { stage = 0; sphase ^= 1u; }
+                }
+                for (int i = 0; i < kFoldSlots && ok; ++i, ++tcount)
+                    ok = mbar_wait(&S.bias_empty[tcount % kFoldSlots], ((tcount / kFoldSlots) & 1u) ^ 1u,
+                                   abort_flag, p.wait_ns);
+                if (ok && !stream_a) ok = mbar_wait(S.a_empty, a_phase ^ 1u, abort_flag, p.wait_ns);
+            }
             if (*abort_flag) {
-                // Drain: let every copy this thread issued land before exit.
-                for (int s = 0; s < stages; ++s)
-                    if (issued_mask & (1u << s))
-                        mbar_wait_drain(&S.full[s], (issued_phase >> s) & 1u, 200000000ull);
-                if (a_issued) mbar_wait_drain(S.a_full, a_issue_phase, 200000000ull);
+                if (leader) {
+                    // Drain: every copy issued into the full barriers (both CTAs'
+                    // bytes, in a pair) lands before exit.
+                    for (int s = 0; s < stages; ++s)
+                        if (issued_mask & (1u << s))
+                            mbar_wait_drain(&S.full[s], (issued_phase >> s) & 1u, 200000000ull);
+                    if (a_issued) mbar_wait_drain(S.a_full, a_issue_phase, 200000000ull);
+                    for (int sl = 0; sl < kFoldSlots; ++sl)
+                        if (bias_mask & (1u << sl))
+                            mbar_wait_drain(&S.bias_full[sl], (bias_phase >> sl) & 1u, 200000000ull);
+                } else if (any_issued) {
+                    // the peer's copies complete on the leader's barriers: give them
+                    // time to land in this CTA's shared memory before it exits
+                    const uint64_t t0 = globaltimer_ns();
+                    while (globaltimer_ns() - t0 < 200000ull) {
+                    }
+                }
             }
         }
     } else if (warp == kMmaWarp) {
-        if (lane == 0) {
+        if (lane == 0 && leader) {
             int stage = 0;
             uint32_t sphase = 0, a_phase = 0, tcount = 0;
-            uint32_t bias_pending = 0, bias_phase = 0;   // bias copies issued (drain on abort)
             bool ok = true, issued_any = false;
-            const uint32_t cst = smem_u32(S.fold + kFoldSlots * kFoldSlotBytes);
+            const uint32_t cst = smem_u32(S.fold + kFoldSlots * G.slot);
             // bias-step operand descriptors: K-major, no swizzle, 8-row x 16-byte
             // core matrices (SBO 128 B between row groups, LBO to the K columns 8..15)
             const uint64_t bias_a = smem_desc_k_none(cst, kConstBytes / 2, 128u);
-            auto load_bias_parts = [&](uint32_t tc, int tile) {
-                const uint32_t sl = tc % kFoldSlots;
-                mbar_arrive_expect_tx(&S.bias_full[sl], kFoldSlotBytes);
-                tma_load_2d(&tm_bias, &S.bias_full[sl], S.fold + sl * kFoldSlotBytes, 0,
-                            tile * p.tile_stride * kBN);
-                bias_pending |= 1u << sl;
-                bias_phase = (bias_phase & ~(1u << sl)) | (((tc / kFoldSlots) & 1u) << sl);
+            auto mma = [&](uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+                if constexpr (kPair) tc_mma_f16_pair(d, a, b, idesc, acc);
+                else tc_mma_f16(d, a, b, idesc, acc);
+            };
+            // every tcgen05 op of a kernel uses one cta_group: pair commits
+            // (multicast to both CTAs' barriers) in pair mode
+            auto commit = [&](uint64_t* bar) {
+                if constexpr (kPair) tc_commit_pair(bar, kBoth);
+                else tc_commit(bar);
             };
             // test hook: the drain barrier completes no phase before an abort,
             // so this bounded wait runs out and the CTA takes its error path
             if (p.test_stall) ok = mbar_wait(S.drain, 0u, abort_flag, p.wait_ns) && false;
-            if (ok && static_cast<int>(blockIdx.x) < n_units)
-                load_bias_parts(0, (blockIdx.x / p.n_qtiles) * p.tiles_per_chunk);
-            for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
-                const int ch = u / p.n_qtiles;
+            for (int u = unit0; u < n_units && ok; u += unit_step) {
+                const int ch = u / n_qunits;
                 const int t0 = ch * p.tiles_per_chunk;
                 const int t1 = min(t0 + p.tiles_per_chunk, p.n_tiles);
                 if (!stream_a) {
@@ -267,15 +360,6 @@ screen_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ 
                     const uint32_t ph = (tcount >> 1) & 1u;
                     if (!mbar_wait(&S.acc_empty[b], ph ^ 1u, abort_flag, p.wait_ns)) { ok = false; break; }
                     tc_fence_after();
-                    {
-                        // the bias parts of the CTA's next tile: the rest of this
-                        // unit, else the first tile of its next unit
-                        int nt = -1;
-                        if (t + 1 < t1) nt = t + 1;
-                        else if (u + static_cast<int>(gridDim.x) < n_units)
-                            nt = ((u + static_cast<int>(gridDim.x)) / p.n_qtiles) * p.tiles_per_chunk;
-                        if (nt >= 0) load_bias_parts(tcount + 1, nt);
-                    }
                     const uint32_t d_tmem = tmem_base + b * kBN;
                     if constexpr (!kX3) {
                         for (int kb = 0; kb < kb_count && ok; ++kb) {
@@ -287,10 +371,10 @@ screen_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ 
 #pragma unroll
                             for (int ks = 0; ks < kBK / 16; ++ks) {
                                 const uint64_t o = static_cast<uint64_t>(ks * 2);   // 32 B >> 4
-                                tc_mma_f16(d_tmem, ad + o, bd + o, kIdesc, (kb | ks) != 0 ? 1u : 0u);
+                                mma(d_tmem, ad + o, bd + o, kIdesc, (kb | ks) != 0 ? 1u : 0u);
                             }
                             issued_any = true;
-                            tc_commit(&S.empty[stage]);
+                            commit(&S.empty[stage]);
                             if (++stage == stages) { stage = 0; sphase ^= 1u; }
                         }
                     } else if (!stream_a) {
@@ -304,11 +388,11 @@ screen_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ 
 #pragma unroll
                             for (int ks = 0; ks < kBK / 16; ++ks) {
                                 const uint64_t o = static_cast<uint64_t>(ks * 2);
-                                tc_mma_f16(d_tmem, a_h + o, bd + o, kIdesc, (kb | ks) != 0 ? 1u : 0u);
-                                tc_mma_f16(d_tmem, a_l + o, bd + o, kIdesc, 1u);
+                                mma(d_tmem, a_h + o, bd + o, kIdesc, (kb | ks) != 0 ? 1u : 0u);
+                                mma(d_tmem, a_l + o, bd + o, kIdesc, 1u);
                             }
                             issued_any = true;
-                            tc_commit(&S.empty[stage]);
+                            commit(&S.empty[stage]);
                             if (++stage == stages) { stage = 0; sphase ^= 1u; }
                             // stage holding B_l of this k-block
                             if (!mbar_wait(&S.full[stage], sphase, abort_flag, p.wait_ns)) { ok = false; break; }
@@ -317,9 +401,9 @@ screen_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ 
 #pragma unroll
                             for (int ks = 0; ks < kBK / 16; ++ks) {
                                 const uint64_t o = static_cast<uint64_t>(ks * 2);
-                                tc_mma_f16(d_tmem, a_h + o, bd + o, kIdesc, 1u);
+                                mma(d_tmem, a_h + o, bd + o, kIdesc, 1u);
                             }
-                            tc_commit(&S.empty[stage]);
+                            commit(&S.empty[stage]);
                             if (++stage == stages) { stage = 0; sphase ^= 1u; }
                         }
                     } else {
@@ -343,13 +427,13 @@ screen_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ 
 #pragma unroll
                             for (int ks = 0; ks < kBK / 16; ++ks) {
                                 const uint64_t o = static_cast<uint64_t>(ks * 2);
-                                tc_mma_f16(d_tmem, a_h + o, b_h + o, kIdesc, (kb | ks) != 0 ? 1u : 0u);
-                                tc_mma_f16(d_tmem, a_l + o, b_h + o, kIdesc, 1u);
-                                tc_mma_f16(d_tmem, a_h + o, b_l + o, kIdesc, 1u);
+                                mma(d_tmem, a_h + o, b_h + o, kIdesc, (kb | ks) != 0 ? 1u : 0u);
+                                mma(d_tmem, a_l + o, b_h + o, kIdesc, 1u);
+                                mma(d_tmem, a_h + o, b_l + o, kIdesc, 1u);
                             }
                             issued_any = true;
-                            tc_commit(&S.empty[s_h]);
-                            tc_commit(&S.empty[s_l]);
+                            commit(&S.empty[s_h]);
+                            commit(&S.empty[s_l]);
                         }
                     }
                     if (ok) {
@@ -358,24 +442,19 @@ screen_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ 
                         if (!mbar_wait(&S.bias_full[sl], (tcount / kFoldSlots) & 1u, abort_flag, p.wait_ns)) {
                             ok = false;
                         } else {
-                            bias_pending &= ~(1u << sl);
                             tc_fence_after();
-                            const uint32_t bslot = smem_u32(S.fold + sl * kFoldSlotBytes);
-                            tc_mma_f16(d_tmem, bias_a, smem_desc_k_none(bslot, cst - bslot, 128u), kIdescBias, 1u);
-                            tc_commit(&S.acc_full[b]);
+                            const uint32_t bslot = smem_u32(S.fold + sl * G.slot);
+                            mma(d_tmem, bias_a, smem_desc_k_none(bslot, cst - bslot, 128u), kIdescBias, 1u);
+                            commit(&S.bias_empty[sl]);
+                            commit(&S.acc_full[b]);
                         }
                     }
                 }
-                if (ok && !stream_a) tc_commit(S.a_empty);
+                if (ok && !stream_a) commit(S.a_empty);
             }
             if (*abort_flag && issued_any) {
-                tc_commit(S.drain);
+                commit(S.drain);
                 mbar_wait_drain(S.drain, 0u, 200000000ull);
-            }
-            if (*abort_flag) {
-                for (int sl = 0; sl < kFoldSlots; ++sl)
-                    if (bias_pending & (1u << sl))
-                        mbar_wait_drain(&S.bias_full[sl], (bias_phase >> sl) & 1u, 200000000ull);
             }
         }
     } else {
@@ -388,18 +467,21 @@ screen_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ 
         // an exact power of two): compare against floor / alpha, store * alpha
         const float alpha = p.alpha;
         const float inv_alpha = 1.0f / alpha;
-        // Accumulator b goes back to the MMA warp as soon as the warp's last
+        // Accumulator b goes back to the MMA thread as soon as the warp's last
         // tcgen05.ld of the tile has completed, before that data is scored.
         auto release_acc = [&](uint32_t b) {
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&S.acc_empty[b]);
+            if (lane == 0) {
+                if constexpr (kPair) mbar_arrive_cluster(cluster_addr(&S.acc_empty[b], 0));
+                else mbar_arrive(&S.acc_empty[b]);
+            }
         };
         uint32_t tcount = 0;
         bool ok = true;
-        for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
-            const int qt = u % p.n_qtiles;
-            const int ch = u / p.n_qtiles;
+        for (int u = unit0; u < n_units && ok; u += unit_step) {
+            const int qt = (u % n_qunits) * (kPair ? 2 : 1) + static_cast<int>(crank);
+            const int ch = u / n_qunits;
             const int t0 = ch * p.tiles_per_chunk;
             const int t1 = min(t0 + p.tiles_per_chunk, p.n_tiles);
             const int row = qt * kBM + row_in_tile;
@@ -486,50 +568,84 @@ screen_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ 
         }
     }
 
+    __syncwarp();
     tc_fence_before();
-    __syncthreads();
+    if constexpr (kPair) cluster_sync();         // no CTA leaves while its peer may still use it
+    else __syncthreads();
     tc_fence_after();
-    if (warp == kMmaWarp) tmem_dealloc(tmem_base, 512);
+    if (warp == kMmaWarp) {
+        if constexpr (kPair) tmem_dealloc_pair(tmem_base, 512);
+        else tmem_dealloc(tmem_base, 512);
+    }
     if (threadIdx.x == 0 && *abort_flag) atomicExch(p.err, *abort_flag);
 }
 
-template <int KP, bool kBuf, bool kBF16, bool kX3>
+template <int KP, bool kBuf, bool kBF16, bool kX3, bool kPair>
 cudaError_t launch_one(const ScreenMaps& m, const ScreenParams& p, int grid, cudaStream_t stream) {
-    const int smem = smem_bytes(p.d_pad / kBK, kX3 ? 2 : 1);
-    cudaError_t e = cudaFuncSetAttribute(screen_kernel<KP, kBuf, kBF16, kX3>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    auto kernel = screen_kernel<KP, kBuf, kBF16, kX3, kPair>;
+    const int smem = smem_bytes(p.d_pad / kBK, kX3 ? 2 : 1, kPair);
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
-    screen_kernel<KP, kBuf, kBF16, kX3><<<grid, screen_threads(kBuf), smem, stream>>>(
-        m.a, kX3 ? m.a2 : m.a, m.b, kX3 ? m.b2 : m.b, m.bias, p);
-    return cudaGetLastError();
+    const CUtensorMap& a2 = kX3 ? m.a2 : m.a;
+    const CUtensorMap& b2 = kX3 ? m.b2 : m.b;
+    if constexpr (!kPair) {
+        kernel<<<grid, screen_threads(kBuf), smem, stream>>>(m.a, a2, m.b, b2, m.bias, p);
+        return cudaGetLastError();
+    } else {
+        cudaLaunchConfig_t cfg{};
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
+        cfg.blockDim = dim3(screen_threads(kBuf), 1, 1);
+        cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+        cfg.stream = stream;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        return cudaLaunchKernelEx(&cfg, kernel, m.a, a2, m.b, b2, m.bias, p);
+    }
 }
 
-template <bool kBF16, bool kX3>
+template <bool kBF16, bool kX3, bool kPair>
 cudaError_t launch_kind(int kp, const ScreenMaps& m, const ScreenParams& p, int grid, cudaStream_t stream) {
     switch (kp) {
-        case 0: return launch_one<4, true, kBF16, kX3>(m, p, grid, stream);
-        case 4: return launch_one<4, false, kBF16, kX3>(m, p, grid, stream);
-        case 8: return launch_one<8, false, kBF16, kX3>(m, p, grid, stream);
-        case 16: return launch_one<16, false, kBF16, kX3>(m, p, grid, stream);
-        case 32: return launch_one<32, false, kBF16, kX3>(m, p, grid, stream);
+        case 0: return launch_one<4, true, kBF16, kX3, kPair>(m, p, grid, stream);
+        case 4: return launch_one<4, false, kBF16, kX3, kPair>(m, p, grid, stream);
+        case 8: return launch_one<8, false, kBF16, kX3, kPair>(m, p, grid, stream);
+        case 16: return launch_one<16, false, kBF16, kX3, kPair>(m, p, grid, stream);
+        case 32: return launch_one<32, false, kBF16, kX3, kPair>(m, p, grid, stream);
         default: return cudaErrorInvalidValue;
     }
 }
 
-}  // namespace
-
-int screen_smem_bytes(int d_pad, bool x3) { return smem_bytes(d_pad / kBK, x3 ? 2 : 1); }
-
-cudaError_t launch_screen(int kp, ScreenKind kind, const ScreenMaps& maps, const ScreenParams& p,
-                          int grid, cudaStream_t stream) {
-    if (p.d_pad % kBK != 0 || p.d_pad < kBK || !(p.alpha == 1.0f || p.alpha == 2.0f))
-        return cudaErrorInvalidValue;
+template <bool kPair>
+cudaError_t launch_mode(int kp, ScreenKind kind, const ScreenMaps& maps, const ScreenParams& p,
+                        int grid, cudaStream_t stream) {
     switch (kind) {
-        case ScreenKind::kF16: return launch_kind<false, false>(kp, maps, p, grid, stream);
-        case ScreenKind::kBF16: return launch_kind<true, false>(kp, maps, p, grid, stream);
-        case ScreenKind::kBF16x3: return launch_kind<true, true>(kp, maps, p, grid, stream);
+        case ScreenKind::kF16: return launch_kind<false, false, kPair>(kp, maps, p, grid, stream);
+        case ScreenKind::kBF16: return launch_kind<true, false, kPair>(kp, maps, p, grid, stream);
+        case ScreenKind::kBF16x3: return launch_kind<true, true, kPair>(kp, maps, p, grid, stream);
     }
     return cudaErrorInvalidValue;
+}
+
+}  // namespace
+
+int screen_smem_bytes(int d_pad, bool x3, bool pair) { return smem_bytes(d_pad / kBK, x3 ? 2 : 1, pair); }
+
+int screen_rows_per_cta(bool pair) { return geo(pair).rows_b; }
+
+cudaError_t launch_screen(int kp, ScreenKind kind, const ScreenMaps& maps, const ScreenParams& p,
+                          int grid, bool pair, cudaStream_t stream) {
+    if (p.d_pad % kBK != 0 || p.d_pad < kBK || !(p.alpha == 1.0f || p.alpha == 2.0f))
+        return cudaErrorInvalidValue;
+    if (pair) {
+        if (grid < 2 || (grid & 1)) return cudaErrorInvalidValue;
+        return launch_mode<true>(kp, kind, maps, p, grid, stream);
+    }
+    return launch_mode<false>(kp, kind, maps, p, grid, stream);
 }
 
 }  // namespace mflat_cu

@@ -77,16 +77,43 @@ __device__ __forceinline__ double error_bound(int metric, double qn, double xmax
 
 // fp64 score of the stored fp32 query and row, index order (the fp64 oracle's
 // evaluation): -sum (q - x)^2 for L2, sum q x otherwise.
+// q and x are 16-byte aligned rows (d_pad floats apart).  The terms are summed
+// in ascending coordinate order; the rows are read four coordinates per load,
+// several loads in flight, so a lane's row costs a few memory latencies rather
+// than one per coordinate.
 __device__ __forceinline__ double exact_score(int metric, const float* q, const float* x, int dim) {
+    const float4* q4 = reinterpret_cast<const float4*>(q);
+    const float4* x4 = reinterpret_cast<const float4*>(x);
+    const int d4 = dim >> 2;
     double acc = 0.0;
     if (metric == kL2) {
-        for (int c = 0; c < dim; ++c) {
+#pragma unroll 4
+        for (int c = 0; c < d4; ++c) {
+            const float4 a = __ldg(q4 + c), b = __ldg(x4 + c);
+            double e = static_cast<double>(a.x) - static_cast<double>(b.x);
+            acc += e * e;
+            e = static_cast<double>(a.y) - static_cast<double>(b.y);
+            acc += e * e;
+            e = static_cast<double>(a.z) - static_cast<double>(b.z);
+            acc += e * e;
+            e = static_cast<double>(a.w) - static_cast<double>(b.w);
+            acc += e * e;
+        }
+        for (int c = 4 * d4; c < dim; ++c) {
             const double e = static_cast<double>(q[c]) - static_cast<double>(x[c]);
             acc += e * e;
         }
         return -acc;
     }
-    for (int c = 0; c < dim; ++c) acc += static_cast<double>(q[c]) * static_cast<double>(x[c]);
+#pragma unroll 4
+    for (int c = 0; c < d4; ++c) {
+        const float4 a = __ldg(q4 + c), b = __ldg(x4 + c);
+        acc += static_cast<double>(a.x) * static_cast<double>(b.x);
+        acc += static_cast<double>(a.y) * static_cast<double>(b.y);
+        acc += static_cast<double>(a.z) * static_cast<double>(b.z);
+        acc += static_cast<double>(a.w) * static_cast<double>(b.w);
+    }
+    for (int c = 4 * d4; c < dim; ++c) acc += static_cast<double>(q[c]) * static_cast<double>(x[c]);
     return acc;
 }
 
