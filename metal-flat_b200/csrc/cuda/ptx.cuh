@@ -145,10 +145,12 @@ __device__ __forceinline__ void cluster_sync() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 // Arrive once on an mbarrier given by its shared::cluster address (possibly
-// in the peer CTA).
+// in the peer CTA), with the default semantics (release, CTA scope): used to
+// hand an accumulator back after this thread's TMEM loads have completed
+// (tcgen05.wait::ld), which needs execution order only -- a cluster-scope
+// release would also wait for this thread's outstanding global stores.
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_bar) {
-    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar)
-                 : "memory");
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
 }
 // Tile load into this CTA's shared memory completing on an mbarrier of either
 // CTA of the pair (`cluster_bar`: shared::cluster address).  No multicast.

@@ -528,22 +528,19 @@ screen_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ 
                     buffer_chunk_raw(ra, floor_adj, alpha, br, st, id_tile);
                     buffer_chunk_raw(rb, floor_adj, alpha, br, st, id_tile + 32);
                 } else {
-                    // list mode, 2 warps per SMSP: the next chunk's TMEM load is
-                    // in flight while a chunk is scored
-                    tmem_ld_32x32b_x32(taddr, ra);
+                    // list mode, 2 warps per SMSP, 128 columns per warp: two
+                    // chunks' TMEM loads in flight together and one wait per
+                    // pair (a TMEM load's round trip is several hundred cycles,
+                    // more than scoring a chunk takes)
 #pragma unroll 1
                     for (int c = 0; c < kCols / 32; c += 2) {
-                        tmem_wait_ld_regs(ra);
-                        __syncwarp();
+                        if (c > 0) __syncwarp();
+                        tmem_ld_32x32b_x32(taddr + c * 32, ra);
                         tmem_ld_32x32b_x32(taddr + (c + 1) * 32, rb);
-                        scan_chunk_raw<KP>(ra, floor_adj, L, id_tile + c * 32);
+                        tmem_wait_ld_regs(ra);
                         tmem_wait_ld_regs(rb);
-                        if (c + 2 < kCols / 32) {
-                            __syncwarp();
-                            tmem_ld_32x32b_x32(taddr + (c + 2) * 32, ra);
-                        } else {
-                            release_acc(b);
-                        }
+                        if (c + 2 >= kCols / 32) release_acc(b);
+                        scan_chunk_raw<KP>(ra, floor_adj, L, id_tile + c * 32);
                         scan_chunk_raw<KP>(rb, floor_adj, L, id_tile + (c + 1) * 32);
                     }
                 }
