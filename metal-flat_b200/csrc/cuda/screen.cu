@@ -18,6 +18,7 @@
 // K = 16 MMA per tile against three bf16 parts of bias / alpha per row
 // (split_bias in index.cu; the parts are exact and sum exactly in any order),
 // so the accumulator holds score / alpha and the epilogue only compares.
+// The bias parts travel in the tile's last ring stage.
 //
 // CTA pairs (kPair): the two CTAs of a cluster issue their MMAs as one
 // tcgen05 cta_group::2 instruction (M = 256: CTA r holds query tile 2j + r
@@ -25,7 +26,7 @@
 // TMEM receives its 128 queries x all 256 columns).  Each SM then loads and
 // holds half of every database tile, which halves the per-SM L2 -> shared
 // memory traffic and doubles the tiles the ring holds in flight.  The
-// leader CTA (rank 0) owns the full / a_full / bias_full / acc_empty
+// leader CTA (rank 0) owns the full / a_full / acc_empty
 // barriers and the one MMA-issuing thread; both CTAs' TMA loads complete on
 // the leader's barriers (cta_group::2 loads, no multicast), MMA completion is
 // committed to the barriers of both CTAs, and the peer's epilogue warps
@@ -39,10 +40,15 @@
 // buffer mode, 64 columns each), then the TMA producer warp, then the MMA warp
 // (TMEM allocator, one issuing thread).  The query tile stays resident in
 // shared memory for a unit when it fits in 64 KB; above, each ring stage
-// carries the k-block's query plane with the database plane (kX3: a
-// k-block's h and l stages are consumed as a pair).  Every mbarrier wait is
+// carries the k-block's query planes with its database planes.  Every mbarrier wait is
 // bounded; a wait that runs out sets the CTA's abort flag, the warps drain
 // what they issued, TMEM is freed and the error word records kErrTimeout.
+//
+// Ring stages: a stage holds kps k-blocks (two where that still leaves three
+// stages, else one), each with all its planes ([query plane when streamed]
+// [database plane]), and room for the tile's bias parts, which the tile's last
+// stage carries.  A 16-bit d = 128 pair tile is then one stage: one full wait
+// and one release per tile besides the accumulator hand-off.
 #include "epilogue.cuh"
 #include "kernels.cuh"
 #include "ptx.cuh"
@@ -57,13 +63,11 @@ constexpr int kAResidentMax = 64 * 1024;          // resident query tile budget
 constexpr int kSmemMax = 232448;                  // opt-in shared memory per CTA
 constexpr int kBarBytes = 512;                    // mbarriers, TMEM slot, abort flag
 constexpr int kMaxStagesAll = 12;                 // barrier slots of the ring
-// Folded bias: slot s holds the bias parts of the CTA's rows of one tile,
-// [rows][8] bf16 = (h, m, l, 0, ...); a ring of three slots filled by the
-// producer (bias_full / bias_empty, like the operand ring).  The constant
-// block holds 128 rows of (1, 1, 1, 0, ...) -- the A operand's K columns 0..7
-// -- then 128 zero rows -- its K columns 8..15.  B's K columns 8..15 read the
-// constant block (finite values, multiplied by A's zeros).
-constexpr int kFoldSlots = 3;
+// Bias step operands: the bias parts of the CTA's rows of a tile, [rows][8]
+// bf16 = (h, m, l, 0, ...), sit at the end of the tile's last stage.  The
+// constant block holds 128 rows of (1, 1, 1, 0, ...) -- the A operand's K
+// columns 0..7 -- then 128 zero rows -- its K columns 8..15.  B's K columns
+// 8..15 read the constant block (finite values, multiplied by A's zeros).
 constexpr int kConstBytes = 2 * kBM * 16;         // 4 KB: ones rows, then zero rows
 constexpr uint32_t kOneBf16x2 = 0x3F803F80u;      // two bf16 1.0
 
@@ -71,49 +75,53 @@ constexpr uint32_t kOneBf16x2 = 0x3F803F80u;      // two bf16 1.0
 struct Geo {
     int rows_b;          // database rows of a tile this CTA holds (256, or 128 in a pair)
     int b_tile;          // bytes of one B plane k-block
-    int slot;            // bytes of one bias slot
-    int fold;            // slots + constant block
-    int max_stages;
+    int slot;            // bytes of the tile's bias parts
 };
 __host__ __device__ constexpr Geo geo(bool pair) {
-    return pair ? Geo{kBN / 2, (kBN / 2) * 128, (kBN / 2) * 16, kFoldSlots * (kBN / 2) * 16 + kConstBytes, 12}
-                : Geo{kBN, kBN * 128, kBN * 16, kFoldSlots * kBN * 16 + kConstBytes, 6};
+    return pair ? Geo{kBN / 2, (kBN / 2) * 128, (kBN / 2) * 16} : Geo{kBN, kBN * 128, kBN * 16};
 }
 
 __host__ __device__ inline int a_bytes(int kb, int planes) { return kb * planes * kATile; }
 __host__ __device__ inline bool a_streamed(int kb, int planes) { return a_bytes(kb, planes) > kAResidentMax; }
-__host__ __device__ inline int stage_bytes(bool streamed, bool pair) {
-    return (streamed ? kATile : 0) + geo(pair).b_tile;
+// one k-block, all planes: ([A plane]) [B plane] per plane
+__host__ __device__ inline int kblock_bytes(bool streamed, int planes, bool pair) {
+    return planes * ((streamed ? kATile : 0) + geo(pair).b_tile);
 }
-__host__ __device__ inline int n_stages(int kb, int planes, bool pair) {
+__host__ __device__ inline int stage_bytes(int kps, bool streamed, int planes, bool pair) {
+    return kps * kblock_bytes(streamed, planes, pair) + geo(pair).slot;
+}
+__host__ __device__ inline int stages_for(int kps, int kb, int planes, bool pair) {
     const bool st = a_streamed(kb, planes);
     const int a = st ? 0 : a_bytes(kb, planes);
-    int s = (kSmemMax - kBarBytes - geo(pair).fold - a) / stage_bytes(st, pair);
-    if (s > geo(pair).max_stages) s = geo(pair).max_stages;
-    if (st && planes == 2) s &= ~1;               // a k-block's h and l stages form a pair
-    return s;
+    const int s = (kSmemMax - kBarBytes - kConstBytes - a) / stage_bytes(kps, st, planes, pair);
+    return s < kMaxStagesAll ? s : kMaxStagesAll;
+}
+// k-blocks per stage: two where that still leaves three stages, else one
+__host__ __device__ inline int kblocks_per_stage(int kb, int planes, bool pair) {
+    return (kb % 2 == 0 && stages_for(2, kb, planes, pair) >= 3) ? 2 : 1;
 }
 __host__ __device__ inline int smem_bytes(int kb, int planes, bool pair) {
     const bool st = a_streamed(kb, planes);
-    return (st ? 0 : a_bytes(kb, planes)) + n_stages(kb, planes, pair) * stage_bytes(st, pair) + kBarBytes +
-           geo(pair).fold;
+    const int kps = kblocks_per_stage(kb, planes, pair);
+    return (st ? 0 : a_bytes(kb, planes)) + stages_for(kps, kb, planes, pair) * stage_bytes(kps, st, planes, pair) +
+           kBarBytes + kConstBytes;
 }
 
 struct Smem {
     uint8_t* a;          // resident A: [planes][kb][16 KB]
-    uint8_t* ring;       // [stages][stage bytes]: ([A plane 16 KB]) [B plane]
-    uint64_t *full, *empty, *a_full, *a_empty, *acc_full, *acc_empty, *drain, *bias_full, *bias_empty;
+    uint8_t* ring;       // [stages][stage bytes]
+    uint64_t *full, *empty, *a_full, *a_empty, *acc_full, *acc_empty, *drain;
     uint32_t* tmem_slot;
     int* abort_flag;
-    uint8_t* fold;       // [kFoldSlots][slot] bias parts, then the 4 KB constant block
+    uint8_t* cst;        // the 4 KB constant block of the bias step
 };
 
-__device__ inline Smem carve(uint8_t* base, int kb, int planes, int stages, bool pair) {
+__device__ inline Smem carve(uint8_t* base, int kb, int planes, int stages, int sbytes) {
     Smem S;
     const bool st = a_streamed(kb, planes);
     S.a = base;
     S.ring = base + (st ? 0 : a_bytes(kb, planes));
-    uint64_t* bars = reinterpret_cast<uint64_t*>(S.ring + stages * stage_bytes(st, pair));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(S.ring + stages * sbytes);
     S.full = bars;
     S.empty = bars + kMaxStagesAll;
     S.a_full = bars + 2 * kMaxStagesAll;
@@ -121,11 +129,9 @@ __device__ inline Smem carve(uint8_t* base, int kb, int planes, int stages, bool
     S.acc_full = S.a_full + 2;
     S.acc_empty = S.a_full + 4;
     S.drain = S.a_full + 6;
-    S.bias_full = S.a_full + 7;
-    S.bias_empty = S.bias_full + kFoldSlots;
-    S.tmem_slot = reinterpret_cast<uint32_t*>(S.bias_empty + kFoldSlots);
+    S.tmem_slot = reinterpret_cast<uint32_t*>(S.drain + 1);
     S.abort_flag = reinterpret_cast<int*>(S.tmem_slot + 1);
-    S.fold = reinterpret_cast<uint8_t*>(bars) + kBarBytes;
+    S.cst = reinterpret_cast<uint8_t*>(bars) + kBarBytes;
     return S;
 }
 
@@ -149,9 +155,11 @@ screen_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ 
     const uint32_t crank = kPair ? cluster_rank() : 0u;
     const bool leader = crank == 0;
     const bool stream_a = a_streamed(kb_count, kPlanes);
-    const int sbytes = stage_bytes(stream_a, kPair);
-    const int stages = n_stages(kb_count, kPlanes, kPair);
-    Smem S = carve(smem_raw, kb_count, kPlanes, stages, kPair);
+    const int kps = kblocks_per_stage(kb_count, kPlanes, kPair);
+    const int kbb = kblock_bytes(stream_a, kPlanes, kPair);
+    const int sbytes = stage_bytes(kps, stream_a, kPlanes, kPair);
+    const int stages = stages_for(kps, kb_count, kPlanes, kPair);
+    Smem S = carve(smem_raw, kb_count, kPlanes, stages, sbytes);
     constexpr uint32_t kM = kPair ? 2 * kBM : kBM;
     constexpr uint32_t kIdesc = make_idesc(kBF16 ? 1u : 0u, kM, kBN);
     constexpr uint32_t kIdescBias = make_idesc(1u, kM, kBN);   // the bias step is bf16
@@ -175,17 +183,13 @@ screen_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ 
             mbar_init(&S.acc_empty[b], kEpiWG * 4 * (kPair ? 2 : 1));
         }
         mbar_init(S.drain, 1);
-        for (int s = 0; s < kFoldSlots; ++s) {
-            mbar_init(&S.bias_full[s], 1);
-            mbar_init(&S.bias_empty[s], 1);
-        }
         *S.abort_flag = 0;
         fence_mbar_init();
     }
     {
         // constant operand rows of the bias step, written once and made
         // visible to the tensor core's (async-proxy) reads
-        uint4* cst = reinterpret_cast<uint4*>(S.fold + kFoldSlots * G.slot);
+        uint4* cst = reinterpret_cast<uint4*>(S.cst);
         for (int i = threadIdx.x; i < kConstBytes / 16; i += blockDim.x)
             cst[i] = i < kBM ? make_uint4(kOneBf16x2, kOneBf16x2 & 0xFFFFu, 0u, 0u)
                              : make_uint4(0u, 0u, 0u, 0u);
@@ -227,10 +231,8 @@ screen_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ 
             int stage = 0;
             uint32_t sphase = 0, a_phase = 0;
             uint32_t issued_mask = 0, issued_phase = 0;   // per stage, for the drain
-            uint32_t bias_mask = 0, bias_phase = 0;       // per bias slot, for the drain
             bool a_issued = false, any_issued = false;
             uint32_t a_issue_phase = 0;
-            uint32_t tcount = 0;
             bool ok = true;
             // barrier the loads complete on: the leader's (pair) or this CTA's
             auto bar_of = [&](uint64_t* bar) -> uint32_t {
@@ -259,48 +261,44 @@ screen_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ 
                     a_issue_phase = a_phase;
                     a_phase ^= 1u;
                 }
-                for (int t = t0; t < t1 && ok; ++t, ++tcount) {
+                for (int t = t0; t < t1 && ok; ++t) {
                     const int row0 = t * p.tile_stride * kBN + static_cast<int>(crank) * G.rows_b;
-                    {
-                        // bias parts of this tile into slot tcount % 3
-                        const uint32_t sl = tcount % kFoldSlots;
-                        const uint32_t use = tcount / kFoldSlots;
-                        if (!mbar_wait(&S.bias_empty[sl], (use & 1u) ^ 1u, abort_flag, p.wait_ns)) { ok = false; break; }
-                        if (leader) mbar_arrive_expect_tx(&S.bias_full[sl], kShare * static_cast<uint32_t>(G.slot));
-                        load(&tm_bias, &S.bias_full[sl], S.fold + sl * G.slot, 0, row0);
-                        bias_mask |= 1u << sl;
-                        bias_phase = (bias_phase & ~(1u << sl)) | ((use & 1u) << sl);
-                        any_issued = true;
-                    }
-                    for (int kb = 0; kb < kb_count && ok; ++kb) {
-                        for (int pl = 0; pl < kPlanes; ++pl) {
-                            if (!mbar_wait(&S.empty[stage], sphase ^ 1u, abort_flag, p.wait_ns)) { ok = false; break; }
-                            uint8_t* dst = S.ring + stage * sbytes;
-                            if (leader) mbar_arrive_expect_tx(&S.full[stage], kShare * static_cast<uint32_t>(sbytes));
-                            if (stream_a) {
-                                load(pl ? &tm_a2 : &tm_a, &S.full[stage], dst, kb * kBK, qt * kBM);
-                                dst += kATile;
+                    for (int kb0 = 0; kb0 < kb_count && ok; kb0 += kps) {
+                        if (!mbar_wait(&S.empty[stage], sphase ^ 1u, abort_flag, p.wait_ns)) { ok = false; break; }
+                        const bool last = kb0 + kps >= kb_count;
+                        uint8_t* base = S.ring + stage * sbytes;
+                        if (leader)
+                            mbar_arrive_expect_tx(&S.full[stage],
+                                                  kShare * static_cast<uint32_t>(kps * kbb + (last ? G.slot : 0)));
+                        uint8_t* dst = base;
+                        for (int j = 0; j < kps; ++j) {
+                            const int kb = kb0 + j;
+                            for (int pl = 0; pl < kPlanes; ++pl) {
+                                if (stream_a) {
+                                    load(pl ? &tm_a2 : &tm_a, &S.full[stage], dst, kb * kBK, qt * kBM);
+                                    dst += kATile;
+                                }
+                                load(pl ? &tm_b2 : &tm_b, &S.full[stage], dst, kb * kBK, row0);
+                                dst += G.b_tile;
                             }
-                            load(pl ? &tm_b2 : &tm_b, &S.full[stage], dst, kb * kBK, row0);
-                            issued_mask |= 1u << stage;
-                            issued_phase = (issued_phase & ~(1u << stage)) | (sphase << stage);
-                            any_issued = true;
-                            if (++stage == stages) { stage = 0; sphase ^= 1u; }
                         }
+                        // the tile's bias parts travel with its last stage
+                        if (last) load(&tm_bias, &S.full[stage], base + kps * kbb, 0, row0);
+                        issued_mask |= 1u << stage;
+                        issued_phase = (issued_phase & ~(1u << stage)) | (sphase << stage);
+                        any_issued = true;
+                        if (++stage == stages) { stage = 0; sphase ^= 1u; }
                     }
                 }
             }
             if (ok && !*abort_flag) {
-                // Tail: wait until the MMAs have released every stage, bias slot
-                // and query tile this warp filled, so that no commit (multicast
-                // in a pair) is still on its way to this CTA's barriers at exit.
+                // Tail: wait until the MMAs have released every stage and query
+                // tile this warp filled, so that no commit (multicast in a pair)
+                // is still on its way to this CTA's barriers at exit.
                 for (int i = 0; i < stages && ok; ++i) {
                     ok = mbar_wait(&S.empty[stage], sphase ^ 1u, abort_flag, p.wait_ns);
                     if (++stage == stages) { stage = 0; sphase ^= 1u; }
                 }
-                for (int i = 0; i < kFoldSlots && ok; ++i, ++tcount)
-                    ok = mbar_wait(&S.bias_empty[tcount % kFoldSlots], ((tcount / kFoldSlots) & 1u) ^ 1u,
-                                   abort_flag, p.wait_ns);
                 if (ok && !stream_a) ok = mbar_wait(S.a_empty, a_phase ^ 1u, abort_flag, p.wait_ns);
             }
             if (*abort_flag) {
@@ -311,9 +309,6 @@ screen_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ 
                         if (issued_mask & (1u << s))
                             mbar_wait_drain(&S.full[s], (issued_phase >> s) & 1u, 200000000ull);
                     if (a_issued) mbar_wait_drain(S.a_full, a_issue_phase, 200000000ull);
-                    for (int sl = 0; sl < kFoldSlots; ++sl)
-                        if (bias_mask & (1u << sl))
-                            mbar_wait_drain(&S.bias_full[sl], (bias_phase >> sl) & 1u, 200000000ull);
                 } else if (any_issued) {
                     // the peer's copies complete on the leader's barriers: give them
                     // time to land in this CTA's shared memory before it exits
@@ -328,7 +323,7 @@ screen_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ 
             int stage = 0;
             uint32_t sphase = 0, a_phase = 0, tcount = 0;
             bool ok = true, issued_any = false;
-            const uint32_t cst = smem_u32(S.fold + kFoldSlots * G.slot);
+            const uint32_t cst = smem_u32(S.cst);
             // bias-step operand descriptors: K-major, no swizzle, 8-row x 16-byte
             // core matrices (SBO 128 B between row groups, LBO to the K columns 8..15)
             const uint64_t bias_a = smem_desc_k_none(cst, kConstBytes / 2, 128u);
@@ -345,6 +340,7 @@ screen_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ 
             // test hook: the drain barrier completes no phase before an abort,
             // so this bounded wait runs out and the CTA takes its error path
             if (p.test_stall) ok = mbar_wait(S.drain, 0u, abort_flag, p.wait_ns) && false;
+            const uint32_t a_addr = smem_u32(S.a);
             for (int u = unit0; u < n_units && ok; u += unit_step) {
                 const int ch = u / n_qunits;
                 const int t0 = ch * p.tiles_per_chunk;
@@ -354,101 +350,60 @@ screen_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ 
                     a_phase ^= 1u;
                     tc_fence_after();
                 }
-                const uint32_t a_addr = smem_u32(S.a);
                 for (int t = t0; t < t1 && ok; ++t, ++tcount) {
                     const uint32_t b = tcount & 1u;
                     const uint32_t ph = (tcount >> 1) & 1u;
                     if (!mbar_wait(&S.acc_empty[b], ph ^ 1u, abort_flag, p.wait_ns)) { ok = false; break; }
                     tc_fence_after();
                     const uint32_t d_tmem = tmem_base + b * kBN;
-                    if constexpr (!kX3) {
-                        for (int kb = 0; kb < kb_count && ok; ++kb) {
-                            if (!mbar_wait(&S.full[stage], sphase, abort_flag, p.wait_ns)) { ok = false; break; }
-                            tc_fence_after();
-                            const uint32_t st = smem_u32(S.ring + stage * sbytes);
-                            const uint64_t ad = smem_desc_k_sw128(stream_a ? st : a_addr + kb * kATile);
-                            const uint64_t bd = smem_desc_k_sw128(stream_a ? st + kATile : st);
+                    for (int kb0 = 0; kb0 < kb_count && ok; kb0 += kps) {
+                        if (!mbar_wait(&S.full[stage], sphase, abort_flag, p.wait_ns)) { ok = false; break; }
+                        tc_fence_after();
+                        const uint32_t base = smem_u32(S.ring + stage * sbytes);
+                        for (int j = 0; j < kps; ++j) {
+                            const int kb = kb0 + j;
+                            const uint32_t blk = base + j * kbb;
+                            // this k-block's operands: A from the stage (streamed) or the
+                            // resident tile; B planes from the stage
+                            uint32_t ah, bh, al = 0, bl = 0;
+                            if (stream_a) {
+                                ah = blk;
+                                bh = blk + kATile;
+                                if constexpr (kX3) {
+                                    al = blk + kATile + G.b_tile;
+                                    bl = al + kATile;
+                                }
+                            } else {
+                                ah = a_addr + kb * kATile;
+                                bh = blk;
+                                if constexpr (kX3) {
+                                    al = a_addr + (kb_count + kb) * kATile;
+                                    bl = blk + G.b_tile;
+                                }
+                            }
+                            const uint64_t a_h = smem_desc_k_sw128(ah), b_h = smem_desc_k_sw128(bh);
+                            const uint64_t a_l = kX3 ? smem_desc_k_sw128(al) : 0ull;
+                            const uint64_t b_l = kX3 ? smem_desc_k_sw128(bl) : 0ull;
 #pragma unroll
                             for (int ks = 0; ks < kBK / 16; ++ks) {
                                 const uint64_t o = static_cast<uint64_t>(ks * 2);   // 32 B >> 4
-                                mma(d_tmem, ad + o, bd + o, kIdesc, (kb | ks) != 0 ? 1u : 0u);
-                            }
-                            issued_any = true;
-                            commit(&S.empty[stage]);
-                            if (++stage == stages) { stage = 0; sphase ^= 1u; }
-                        }
-                    } else if (!stream_a) {
-                        for (int kb = 0; kb < kb_count && ok; ++kb) {
-                            const uint64_t a_h = smem_desc_k_sw128(a_addr + kb * kATile);
-                            const uint64_t a_l = smem_desc_k_sw128(a_addr + (kb_count + kb) * kATile);
-                            // stage holding B_h of this k-block
-                            if (!mbar_wait(&S.full[stage], sphase, abort_flag, p.wait_ns)) { ok = false; break; }
-                            tc_fence_after();
-                            uint64_t bd = smem_desc_k_sw128(smem_u32(S.ring + stage * sbytes));
-#pragma unroll
-                            for (int ks = 0; ks < kBK / 16; ++ks) {
-                                const uint64_t o = static_cast<uint64_t>(ks * 2);
-                                mma(d_tmem, a_h + o, bd + o, kIdesc, (kb | ks) != 0 ? 1u : 0u);
-                                mma(d_tmem, a_l + o, bd + o, kIdesc, 1u);
-                            }
-                            issued_any = true;
-                            commit(&S.empty[stage]);
-                            if (++stage == stages) { stage = 0; sphase ^= 1u; }
-                            // stage holding B_l of this k-block
-                            if (!mbar_wait(&S.full[stage], sphase, abort_flag, p.wait_ns)) { ok = false; break; }
-                            tc_fence_after();
-                            bd = smem_desc_k_sw128(smem_u32(S.ring + stage * sbytes));
-#pragma unroll
-                            for (int ks = 0; ks < kBK / 16; ++ks) {
-                                const uint64_t o = static_cast<uint64_t>(ks * 2);
-                                mma(d_tmem, a_h + o, bd + o, kIdesc, 1u);
-                            }
-                            commit(&S.empty[stage]);
-                            if (++stage == stages) { stage = 0; sphase ^= 1u; }
-                        }
-                    } else {
-                        for (int kb = 0; kb < kb_count && ok; ++kb) {
-                            // the k-block's h stage [A_h | B_h] and l stage [A_l | B_l]
-                            const int s_h = stage;
-                            const uint32_t ph_h = sphase;
-                            if (++stage == stages) { stage = 0; sphase ^= 1u; }
-                            const int s_l = stage;
-                            const uint32_t ph_l = sphase;
-                            if (++stage == stages) { stage = 0; sphase ^= 1u; }
-                            if (!mbar_wait(&S.full[s_h], ph_h, abort_flag, p.wait_ns) ||
-                                !mbar_wait(&S.full[s_l], ph_l, abort_flag, p.wait_ns)) { ok = false; break; }
-                            tc_fence_after();
-                            const uint32_t base_h = smem_u32(S.ring + s_h * sbytes);
-                            const uint32_t base_l = smem_u32(S.ring + s_l * sbytes);
-                            const uint64_t a_h = smem_desc_k_sw128(base_h);
-                            const uint64_t b_h = smem_desc_k_sw128(base_h + kATile);
-                            const uint64_t a_l = smem_desc_k_sw128(base_l);
-                            const uint64_t b_l = smem_desc_k_sw128(base_l + kATile);
-#pragma unroll
-                            for (int ks = 0; ks < kBK / 16; ++ks) {
-                                const uint64_t o = static_cast<uint64_t>(ks * 2);
                                 mma(d_tmem, a_h + o, b_h + o, kIdesc, (kb | ks) != 0 ? 1u : 0u);
-                                mma(d_tmem, a_l + o, b_h + o, kIdesc, 1u);
-                                mma(d_tmem, a_h + o, b_l + o, kIdesc, 1u);
+                                if constexpr (kX3) {
+                                    mma(d_tmem, a_l + o, b_h + o, kIdesc, 1u);
+                                    mma(d_tmem, a_h + o, b_l + o, kIdesc, 1u);
+                                }
                             }
-                            issued_any = true;
-                            commit(&S.empty[s_h]);
-                            commit(&S.empty[s_l]);
                         }
-                    }
-                    if (ok) {
-                        // bias step: acc += (1, 1, 1, 0 ...) . (h, m, l, 0 ...) per row
-                        const uint32_t sl = tcount % kFoldSlots;
-                        if (!mbar_wait(&S.bias_full[sl], (tcount / kFoldSlots) & 1u, abort_flag, p.wait_ns)) {
-                            ok = false;
-                        } else {
-                            tc_fence_after();
-                            const uint32_t bslot = smem_u32(S.fold + sl * G.slot);
+                        issued_any = true;
+                        if (kb0 + kps >= kb_count) {
+                            // bias step: acc += (1, 1, 1, 0 ...) . (h, m, l, 0 ...) per row
+                            const uint32_t bslot = base + kps * kbb;
                             mma(d_tmem, bias_a, smem_desc_k_none(bslot, cst - bslot, 128u), kIdescBias, 1u);
-                            commit(&S.bias_empty[sl]);
-                            commit(&S.acc_full[b]);
                         }
+                        commit(&S.empty[stage]);
+                        if (++stage == stages) { stage = 0; sphase ^= 1u; }
                     }
+                    if (ok) commit(&S.acc_full[b]);
                 }
                 if (ok && !stream_a) commit(S.a_empty);
             }
