@@ -1,10 +1,13 @@
 """One rank of the dead-rank GPU test (tests/test_gpu_shard.py, 2 ranks under
 torchrun, NCCL_NVLS_ENABLE=0, short MFLAT_NCCL_TIMEOUT_S).  Both ranks run one
-sharded search; then rank 1 leaves between steps (nothing of it in flight:
-its index and communicator are closed after a host barrier) and rank 0 runs
-the next search, whose all-gather can no longer complete.  The library's
-watchdog must abort the communicator and return MFLAT_ERR_DEVICE within the
-timeout; rank 0 prints the outcome and exits without further collectives."""
+sharded search; then rank 1 stops taking part between steps: nothing of it is in
+flight (a host barrier follows the first step), and it neither searches again
+nor tears down its communicator -- its process and its NCCL buffers stay alive,
+so no peer ever touches freed memory.  Rank 0 runs the next search, whose
+all-gather can no longer complete; the library's watchdog must abort the
+communicator and return MFLAT_ERR_DEVICE within the timeout.  Rank 0 then
+checks that the index answers for its own rows, writes the flag file named by
+MFLAT_TEST_DONE_FLAG, and only then does rank 1 exit (bounded wait)."""
 import datetime
 import os
 import sys
@@ -37,11 +40,17 @@ def main():
     ids, _ = idx.search(q, 5)                  # a healthy collective step
     ok_first = bool((ids >= 0).all())
     dist.barrier()                             # everything of step 1 has completed
+    flag = os.environ["MFLAT_TEST_DONE_FLAG"]
     if rank == 1:
-        idx.close()                            # leaves between steps
-        print("rank 1 left", flush=True)
+        # stops taking part between steps; stays alive (communicator and its
+        # buffers intact) until rank 0 has finished, at most 180 s
+        print("rank 1 stopped taking part", flush=True)
+        t_end = time.time() + 180.0
+        while not os.path.exists(flag) and time.time() < t_end:
+            time.sleep(0.2)
         os._exit(0)
     time.sleep(2.0)
+    print("rank 0: second step starts", flush=True)
     t0 = time.time()
     try:
         idx.search(q, 5)
@@ -56,6 +65,8 @@ def main():
     local_ok = bool((ids2 >= lo).all() and (ids2 < hi).all())
     print(f"rank 0: local search after abort ok {local_ok}", flush=True)
     idx.close()
+    with open(flag, "w") as f:
+        f.write("done")
     os._exit(0 if (ok_first and status == 6 and took < 60 and local_ok) else 1)
 
 

@@ -3,6 +3,7 @@ against the fp64 oracle.  Skipped when fewer than two GPUs are visible."""
 import os
 import subprocess
 import sys
+import tempfile
 
 import pytest
 
@@ -33,10 +34,12 @@ def test_sharded_search_matches_oracle():
 
 @pytest.mark.skipif(_gpus() < 2, reason="needs at least two GPUs")
 def test_dead_rank_reports_device_error():
-    """Rank 1 leaves between steps; rank 0's next sharded search ends with
-    MFLAT_ERR_DEVICE after the library's NCCL watchdog aborts the communicator
-    (MFLAT_NCCL_TIMEOUT_S), instead of hanging.  NVLS off, plain NCCL."""
-    env = dict(os.environ, NCCL_NVLS_ENABLE="0", MFLAT_NCCL_TIMEOUT_S="5")
+    """Rank 1 stops taking part between steps (alive, its communicator intact);
+    rank 0's next sharded search ends with MFLAT_ERR_DEVICE after the library's
+    NCCL watchdog aborts the communicator (MFLAT_NCCL_TIMEOUT_S), instead of
+    hanging.  NVLS off, plain NCCL."""
+    flag = os.path.join(tempfile.mkdtemp(prefix="mflat_dead_rank_"), "rank0_done")
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", MFLAT_NCCL_TIMEOUT_S="5", MFLAT_TEST_DONE_FLAG=flag)
     cmd = ["timeout", "-k", "30", "240", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            "--nproc-per-node=2", "--master-addr", "127.0.0.1", "--master-port", "29541",
            os.path.join(ROOT, "tests", "dead_rank_worker.py")]
