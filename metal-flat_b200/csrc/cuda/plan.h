@@ -24,23 +24,30 @@ inline int screen_slots(int num_sms, bool pair) { return pair ? std::max(1, num_
 // CTA pairs when allowed and the batch has at least two query tiles.
 inline bool screen_pair_for(bool allowed, int n_qtiles) { return allowed && n_qtiles >= 2; }
 
-// Database chunks per query tile: whole work units on every SM.
+// Database chunks per query tile.  The critical path of a launch is the
+// tiles its busiest SM (or pair) streams: waves x tiles per chunk, where a wave
+// is one work unit on every slot.  The plan takes the fewest chunks whose
+// critical path is within 1 % of the shortest (fewer chunks: fewer candidate
+// lists to merge and fewer per-unit query-tile loads).
 inline void plan_chunks(int n_qtiles, int n_tiles, int num_sms, int max_chunks, int& n_chunks,
                         int& tiles_per_chunk, int min_chunks = 1) {
-    const int smax = std::min(max_chunks, n_tiles);
-    const int smin = std::max(1, std::min(min_chunks, smax));
-    int best_s = smin;
-    double best_eff = -1.0;
-    for (int s = smin; s <= smax; ++s) {
+    const int smin = std::max(1, std::min(min_chunks, std::min(max_chunks, n_tiles)));
+    // beyond a few chunks per slot more chunks only add lists and unit overheads
+    const int smax = std::min({max_chunks, n_tiles, smin + 4 * std::max(num_sms, 1)});
+    auto span = [&](int s) -> int64_t {
         const int tpc = (n_tiles + s - 1) / s;
         const int sc = (n_tiles + tpc - 1) / tpc;
         const int64_t units = static_cast<int64_t>(n_qtiles) * sc;
         const int64_t waves = (units + num_sms - 1) / num_sms;
-        const double eff = static_cast<double>(units) / static_cast<double>(waves * num_sms);
-        if (eff > best_eff + 0.02) { best_eff = eff; best_s = s; }
-        if (best_eff > 0.97 && units >= num_sms) break;
+        return waves * tpc;
+    };
+    int64_t best = span(smin);
+    for (int s = smin + 1; s <= smax; ++s) best = std::min(best, span(s));
+    int pick = smin;
+    for (int s = smin; s <= smax; ++s) {
+        if (span(s) * 100 <= best * 101) { pick = s; break; }
     }
-    tiles_per_chunk = (n_tiles + best_s - 1) / best_s;
+    tiles_per_chunk = (n_tiles + pick - 1) / pick;
     n_chunks = (n_tiles + tiles_per_chunk - 1) / tiles_per_chunk;
 }
 

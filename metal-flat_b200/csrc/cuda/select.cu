@@ -201,6 +201,71 @@ __device__ __forceinline__ void warp_sort_better_first(double& s, int& id, int l
     }
 }
 
+// Exact fp64 scores of the warp's candidates (lane j holds candidate j's row id,
+// -1 for none), the warp cooperating on each row: lane l reads coordinates
+// [4l, 4l + 4) of every 128-wide slab of the row, so a row is one coalesced
+// 512-byte read per slab, with kB rows in flight.  Each lane sums its
+// coordinates in ascending order; the 32 lane sums are added by the same
+// shuffle tree for every row, so identical rows score identically.  Lane j
+// returns candidate j's score (-DBL_MAX for none).  q and the rows are
+// zero-padded to d_pad (a multiple of 64), 16-byte aligned.
+template <int KP>
+__device__ __forceinline__ double warp_rescore(int metric, const float* __restrict__ q,
+                                               const float* __restrict__ db_x, int d_pad, int id, int lane) {
+    constexpr int kB = 8;
+    double mine = -DBL_MAX;
+#pragma unroll 1
+    for (int j0 = 0; j0 < KP; j0 += kB) {
+        int rid[kB];
+        double part[kB];
+#pragma unroll
+        for (int jj = 0; jj < kB; ++jj) {
+            rid[jj] = __shfl_sync(kFull, id, j0 + jj);
+            part[jj] = 0.0;
+        }
+#pragma unroll 1
+        for (int c0 = 0; c0 < d_pad; c0 += 128) {
+            const int c = c0 + 4 * lane;
+            const bool in = c < d_pad;
+            const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+            const float4 qv = in ? __ldg(reinterpret_cast<const float4*>(q + c)) : zero;
+            float4 xv[kB];
+#pragma unroll
+            for (int jj = 0; jj < kB; ++jj)
+                xv[jj] = (in && rid[jj] >= 0)
+                             ? __ldg(reinterpret_cast<const float4*>(db_x + static_cast<int64_t>(rid[jj]) * d_pad + c))
+                             : zero;
+#pragma unroll
+            for (int jj = 0; jj < kB; ++jj) {
+                if (metric == kL2) {
+                    double e = static_cast<double>(qv.x) - static_cast<double>(xv[jj].x);
+                    part[jj] += e * e;
+                    e = static_cast<double>(qv.y) - static_cast<double>(xv[jj].y);
+                    part[jj] += e * e;
+                    e = static_cast<double>(qv.z) - static_cast<double>(xv[jj].z);
+                    part[jj] += e * e;
+                    e = static_cast<double>(qv.w) - static_cast<double>(xv[jj].w);
+                    part[jj] += e * e;
+                } else {
+                    part[jj] += static_cast<double>(qv.x) * static_cast<double>(xv[jj].x);
+                    part[jj] += static_cast<double>(qv.y) * static_cast<double>(xv[jj].y);
+                    part[jj] += static_cast<double>(qv.z) * static_cast<double>(xv[jj].z);
+                    part[jj] += static_cast<double>(qv.w) * static_cast<double>(xv[jj].w);
+                }
+            }
+        }
+#pragma unroll
+        for (int jj = 0; jj < kB; ++jj) {
+            double v = part[jj];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) v += __shfl_down_sync(kFull, v, o);
+            v = __shfl_sync(kFull, v, 0);
+            if (lane == j0 + jj && rid[jj] >= 0) mine = metric == kL2 ? -v : v;
+        }
+    }
+    return mine;
+}
+
 // One warp per query: merge the chunk lists into the top KP candidates, prove
 // that the true top-k is among them, re-score them exactly in fp64 and write
 // the k nearest in (distance, id) order.  Queries whose proof fails are
@@ -239,11 +304,7 @@ __global__ void __launch_bounds__(128) select_exact_kernel(const SelectParams p)
     }
 
     // exact fp64 re-score (lane = candidate), then (distance, id) order
-    double ex = -DBL_MAX;
-    if (id >= 0) {
-        const int64_t r = id;
-        ex = exact_score(p.metric, p.q_x + static_cast<int64_t>(qi) * p.d_pad, p.db_x + r * p.d_pad, p.dim);
-    }
+    double ex = warp_rescore<KP>(p.metric, p.q_x + static_cast<int64_t>(qi) * p.d_pad, p.db_x, p.d_pad, id, lane);
     int rid = id;
     warp_sort_better_first(ex, rid, lane);
     if (lane < p.k_out) {
