@@ -204,7 +204,8 @@ __device__ __forceinline__ void warp_sort_better_first(double& s, int& id, int l
 // Exact fp64 scores of the warp's candidates (lane j holds candidate j's row id,
 // -1 for none), the warp cooperating on each row: lane l reads coordinates
 // [4l, 4l + 4) of every 128-wide slab of the row, so a row is one coalesced
-// 512-byte read per slab, with kB rows in flight.  Each lane sums its
+// 512-byte read per slab, with kB rows in flight (two: fewer registers, more
+// resident warps -- measured faster than four or eight).  Each lane sums its
 // coordinates in ascending order; the 32 lane sums are added by the same
 // shuffle tree for every row, so identical rows score identically.  Lane j
 // returns candidate j's score (-DBL_MAX for none).  q and the rows are
@@ -212,7 +213,7 @@ __device__ __forceinline__ void warp_sort_better_first(double& s, int& id, int l
 template <int KP>
 __device__ __forceinline__ double warp_rescore(int metric, const float* __restrict__ q,
                                                const float* __restrict__ db_x, int d_pad, int id, int lane) {
-    constexpr int kB = 8;
+    constexpr int kB = 2;
     double mine = -DBL_MAX;
 #pragma unroll 1
     for (int j0 = 0; j0 < KP; j0 += kB) {
