@@ -441,24 +441,42 @@ __device__ __forceinline__ MinCand warp_min(MinCand c) {
 template <int KP>
 __global__ void __launch_bounds__(128) kmeans_select_kernel(const SelectParams p,
                                                             int32_t* out_assign) {
-    const int lane = threadIdx.x & 31;
-    const int qi = blockIdx.x * 4 + (threadIdx.x >> 5);
+    // one thread per point: the sequential fp32 re-check below is one chain
+    // of dim operations per candidate, so a warp serves 32 points at once
+    const int qi = blockIdx.x * blockDim.x + threadIdx.x;
     if (qi >= p.m) return;
     if (*p.err != 0) return;                    // the screen failed: its lists are not valid
+    // the point's top KP over its lists, in (score desc, id asc) order, by a
+    // static compare-and-swap insertion (lists are read coalesced: thread qi's
+    // KP entries of a list are adjacent to thread qi + 1's)
     float sel_s[KP];
     int sel_id[KP];
-    int head = 0;
-    const int64_t base = (static_cast<int64_t>(lane) * p.m_pad + qi) * KP;
-    for (int r = 0; r < KP; ++r) {
-        Cand c{-DBL_MAX, -1, lane};
-        if (lane < p.n_chunks && head < KP) {
-            c.s = p.part_score[base + head];
-            c.id = p.part_id[base + head];
+#pragma unroll
+    for (int i = 0; i < KP; ++i) {
+        sel_s[i] = 0.0f;
+        sel_id[i] = -1;
+    }
+    for (int c = 0; c < p.n_chunks; ++c) {
+        const int64_t base = (static_cast<int64_t>(c) * p.m_pad + qi) * KP;
+#pragma unroll
+        for (int j = 0; j < KP; ++j) {
+            float s = p.part_score[base + j];
+            int id = p.part_id[base + j];
+            if (id < 0) continue;
+#pragma unroll
+            for (int i = 0; i < KP; ++i) {
+                const bool take = sel_id[i] < 0 || s > sel_s[i] || (s == sel_s[i] && id < sel_id[i]);
+                if (take) {
+                    const float ts = sel_s[i];
+                    const int ti = sel_id[i];
+                    sel_s[i] = s;
+                    sel_id[i] = id;
+                    s = ts;
+                    id = ti;
+                    if (id < 0) break;
+                }
+            }
         }
-        const Cand w = warp_best(c);
-        sel_s[r] = static_cast<float>(w.s);
-        sel_id[r] = w.id;
-        if (w.id >= 0 && w.owner == lane) ++head;
     }
     int n_valid = 0;
     bool bad_id = false;
@@ -468,7 +486,7 @@ __global__ void __launch_bounds__(128) kmeans_select_kernel(const SelectParams p
         bad_id |= sel_id[i] >= p.n;
     }
     if (bad_id) {                               // never produced by a screen: report, read nothing
-        if (lane == 0) atomicExch(p.err, kErrInternal);
+        atomicExch(p.err, kErrInternal);
         return;
     }
     const double qn = p.qnorm[qi];
@@ -479,25 +497,26 @@ __global__ void __launch_bounds__(128) kmeans_select_kernel(const SelectParams p
     const double W = 2.0 * E + 3.0 * gs * (db + E) + 1e-30;
     const bool ok = n_valid < KP || static_cast<double>(sel_s[KP - 1]) < static_cast<double>(sel_s[0]) - W;
     if (!ok) {
-        if (lane == 0) {
-            const int slot = atomicAdd(p.flag_count, 1);
-            p.flag_list[slot] = qi;
-        }
+        const int slot = atomicAdd(p.flag_count, 1);
+        p.flag_list[slot] = qi;
         return;
     }
+    // exact fp32 distance, in the reference's operation order, of every
+    // candidate within W of the best screen score; argmin, lowest id on ties
     const float* px = p.q_x + static_cast<int64_t>(qi) * p.d_pad;
     MinCand mc{0.0f, -1};
 #pragma unroll
     for (int i = 0; i < KP; ++i) {
-        if (lane == i && sel_id[i] >= 0 &&
-            static_cast<double>(sel_s[i]) >= static_cast<double>(sel_s[0]) - W) {
-            const int64_t id = sel_id[i];
-            mc.v = sql2_f32_seq(px, p.db_x + id * p.d_pad, p.dim);
-            mc.id = sel_id[i];
+        if (sel_id[i] >= 0 && static_cast<double>(sel_s[i]) >= static_cast<double>(sel_s[0]) - W) {
+            const int id = sel_id[i];
+            const float v = sql2_f32_seq(px, p.db_x + static_cast<int64_t>(id) * p.d_pad, p.dim);
+            if (mc.id < 0 || v < mc.v || (v == mc.v && id < mc.id)) {
+                mc.v = v;
+                mc.id = id;
+            }
         }
     }
-    mc = warp_min(mc);
-    if (lane == 0) out_assign[qi] = mc.id;
+    out_assign[qi] = mc.id;
 }
 
 __global__ void __launch_bounds__(128) kmeans_fallback_kernel(const SelectParams p,
@@ -568,7 +587,7 @@ cudaError_t launch_select_exact(int kp, const SelectParams& p, cudaStream_t stre
 cudaError_t launch_kmeans_select(const SelectParams& p, int32_t* out, int grid_fallback,
                                  cudaStream_t stream) {
     if (p.n_chunks > 32 || p.n_chunks < 1) return cudaErrorInvalidValue;
-    kmeans_select_kernel<4><<<(p.m + 3) / 4, 128, 0, stream>>>(p, out);
+    kmeans_select_kernel<4><<<(p.m + 127) / 128, 128, 0, stream>>>(p, out);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     kmeans_fallback_kernel<<<grid_fallback, 128, 0, stream>>>(p, out);
