@@ -56,6 +56,32 @@ def test_chunks_cover_the_tiles(probe):
             assert tpc <= -(-nt // minc)
 
 
+def _span(nq, nt, slots, s):
+    """Tiles the busiest slot streams when the tiles are cut into s chunks."""
+    tpc = -(-nt // s)
+    sc = -(-nt // tpc)
+    return -(-(nq * sc) // slots) * tpc
+
+
+def test_chunks_take_the_shortest_critical_path(probe):
+    """The plan's critical path (waves x tiles per chunk) is within 1 % of the
+    shortest over the chunk counts it may use, with the fewest such chunks; the
+    config-3 pair plan is 11 chunks of 3,552 tiles (440 pair units: the last of
+    six waves fills 70 of 74 slots) rather than 9 (360 units, 4.86 waves)."""
+    cases = list(itertools.product([1, 4, 40, 79, 256, 39063], [1, 7, 256, 391, 3907, 39063],
+                                   [SMS, SMS // 2], [16, 64, 128]))
+    res = probe(["chunks %d %d %d %d 1" % c for c in cases])
+    for (nq, nt, sms, maxc), (nc, tpc) in zip(cases, res):
+        smax = min(maxc, nt, 1 + 4 * sms)
+        best = min(_span(nq, nt, sms, s) for s in range(1, smax + 1))
+        got = -(-(nq * nc) // sms) * tpc
+        assert got * 100 <= best * 101, (nq, nt, sms, maxc, nc, tpc)
+        fewer = [s for s in range(1, smax + 1) if _span(nq, nt, sms, s) * 100 <= best * 101]
+        assert nc == -(-nt // (-(-nt // fewer[0]))), (nq, nt, sms, maxc, nc, fewer[0])
+    (p,) = probe(["chunks 40 39063 74 128 1"])
+    assert p == [11, 3552]
+
+
 def test_buffer_chunks_fit_in_l2_budget(probe):
     cases = list(itertools.product([1, 16, 64, 128], [1, 977, 7813, 31250, 390625],
                                    [BN * 128 * 2, BN * 128 * 8, BN * 768 * 2, BN * 960 * 8]))
