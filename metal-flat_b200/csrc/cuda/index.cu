@@ -231,34 +231,69 @@ __global__ void export_rows_bits_kernel(const uint16_t* __restrict__ db, int64_t
     out[e] = db[(row0 + r) * d_pad + c];
 }
 
-__global__ void prep_queries_half_kernel(const float* __restrict__ src, int m, int m_pad, int dim,
-                                         int d_pad, int metric, bool bf16, uint16_t* __restrict__ q,
-                                         float* __restrict__ qsq) {
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= m_pad) return;
-    uint16_t* o = q + static_cast<int64_t>(i) * d_pad;
-    if (i >= m) {
-        for (int c = 0; c < d_pad; ++c) o[c] = 0;
-        qsq[i] = 0.0f;
-        return;
-    }
-    const float* row = src + static_cast<int64_t>(i) * dim;
+// 16-bit query preparation (Cosine normalisation, rounding to the storage
+// type, sum of squares of the rounded values): 32 rows per 128-thread block
+// through shared memory in 64-column slabs, so global reads and writes are
+// coalesced; each row's arithmetic stays with one thread in ascending
+// coordinate order, the same operations as the per-row form.
+constexpr int kHalfPrepRows = 32;
+constexpr int kHalfPrepCols = 64;
+
+__global__ void __launch_bounds__(128) prep_queries_half_kernel(const float* __restrict__ src, int m, int m_pad,
+                                                                int dim, int d_pad, int metric, bool bf16,
+                                                                uint16_t* __restrict__ q, float* __restrict__ qsq) {
+    __shared__ float tin[kHalfPrepRows][kHalfPrepCols + 1];
+    __shared__ uint16_t tq[kHalfPrepRows][kHalfPrepCols + 2];
+    const int r0 = blockIdx.x * kHalfPrepRows;
+    const int t = threadIdx.x;
+    const int row = r0 + t;
+    const bool own = t < kHalfPrepRows && row < m_pad;   // this thread's row
+    const bool live = own && row < m;
+    auto load = [&](int c0) {
+        for (int i = t; i < kHalfPrepRows * kHalfPrepCols; i += blockDim.x) {
+            const int rr = i / kHalfPrepCols, cc = i % kHalfPrepCols;
+            const int r = r0 + rr, c = c0 + cc;
+            tin[rr][cc] = (r < m && c < dim) ? src[static_cast<int64_t>(r) * dim + c] : 0.0f;
+        }
+    };
     float inv = 1.0f;
     bool scale = false;
     if (metric == kCosine) {
         double s = 0.0;
-        for (int c = 0; c < dim; ++c) s += static_cast<double>(row[c]) * row[c];
-        if (s > 0.0) { inv = static_cast<float>(1.0 / sqrt(s)); scale = true; }
+        for (int c0 = 0; c0 < dim; c0 += kHalfPrepCols) {
+            load(c0);
+            __syncthreads();
+            if (live)
+                for (int cc = 0; cc < kHalfPrepCols && c0 + cc < dim; ++cc)
+                    s += static_cast<double>(tin[t][cc]) * tin[t][cc];
+            __syncthreads();
+        }
+        if (live && s > 0.0) { inv = static_cast<float>(1.0 / sqrt(s)); scale = true; }
     }
     double s2 = 0.0;
-    for (int c = 0; c < dim; ++c) {
-        const uint16_t h = to_half_bits(scale ? row[c] * inv : row[c], bf16);
-        const float x = from_half_bits(h, bf16);
-        s2 += static_cast<double>(x) * x;
-        o[c] = h;
+    for (int c0 = 0; c0 < d_pad; c0 += kHalfPrepCols) {
+        load(c0);
+        __syncthreads();
+        if (own) {
+            for (int cc = 0; cc < kHalfPrepCols; ++cc) {
+                uint16_t h = 0;
+                if (live && c0 + cc < dim) {
+                    h = to_half_bits(scale ? tin[t][cc] * inv : tin[t][cc], bf16);
+                    const float x = from_half_bits(h, bf16);
+                    s2 += static_cast<double>(x) * x;
+                }
+                tq[t][cc] = h;
+            }
+        }
+        __syncthreads();
+        for (int i = t; i < kHalfPrepRows * kHalfPrepCols; i += blockDim.x) {
+            const int rr = i / kHalfPrepCols, cc = i % kHalfPrepCols;
+            const int r = r0 + rr, c = c0 + cc;
+            if (r < m_pad && c < d_pad) q[static_cast<int64_t>(r) * d_pad + c] = tq[rr][cc];
+        }
+        __syncthreads();
     }
-    for (int c = dim; c < d_pad; ++c) o[c] = 0;
-    qsq[i] = static_cast<float>(s2);
+    if (own) qsq[row] = live ? static_cast<float>(s2) : 0.0f;
 }
 
 // x ~ h + l: h = bf16(x), l = bf16(x - h), both round to nearest (x - h is
@@ -949,7 +984,7 @@ int search_half(mflat_cu_index* ix, const float* queries, int m, int k_out, int3
     for (int b0 = 0; b0 < m; b0 += P.batch) {
         const int mb = std::min(P.batch, m - b0);
         const int mb_pad = (mb + kBM - 1) / kBM * kBM;
-        prep_queries_half_kernel<<<blocks_for(mb_pad, 128), 128, 0, st>>>(
+        prep_queries_half_kernel<<<blocks_for(mb_pad, kHalfPrepRows), 128, 0, st>>>(
             qsrc + static_cast<int64_t>(b0) * ix->dim, mb, mb_pad, ix->dim, d_pad, ix->metric, bf16,
             ix->q16.as<uint16_t>(), ix->qsq.as<float>());
         CU_TRY(cudaGetLastError(), "query prep launch");
